@@ -1,0 +1,431 @@
+#!/usr/bin/env python
+"""Benchmark of the g4w4 hot path on B200 (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ple|gemv|attn] [--impl g4|reference]
+
+Workloads (inputs are seeded synthetic data with the configs'
+shapes and value distributions -- the reference publishes no dataset):
+  ple   config 2: PLE W4 gather-dequant of 4096 token ids from the [262144, 8960]
+        table into bf16 [4096, 35, 256].  A step is one gather of a fresh id batch.
+  gemv  config 1: W4A16 decode GEMV, x [1,1536], W [6144,1536]; a step is one call,
+        rotating over 64 weight copies (340 MB > L2).
+  attn  decode attention, 8 q heads / 1 KV head, hd 256, one sequence at keylen 4096.
+Timing: W warm-up steps, then K steps captured in one CUDA graph and timed with
+CUDA events on the launching stream between barriers; max over ranks.
+--impl reference times the CPU restatement of the reference's TFJS path (the
+reference itself is JavaScript and cannot run here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu
+# captures (profiles/); None until a capture of that kernel exists.
+TRAFFIC = {"ple_gather_kernel": None, "gemv_w4a16_kernel": None, "attn_decode_kernel": None}
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {**PEAKS_FALLBACK, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ----------------------------------------------------------------- clocks ---
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait()
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": mx,
+                "samples": len(sms), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------ distributed ---
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, use_cuda: bool):
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            if use_cuda:
+                torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl" if use_cuda else "gloo", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local) if use_cuda else None)
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def time_graph(torch, ctx, launch, K, W, dist: Dist):
+    """Warm up W launches eagerly, capture K launches in a CUDA graph, replay it once
+    between barriers and return the device time (ms) of the K launches."""
+    for i in range(W):
+        launch(i)
+    ctx.sync()
+    stream = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    old = ctx.stream
+    with torch.cuda.stream(stream):
+        ctx.set_stream(stream)
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(K):
+                launch(W + i)
+    ctx.set_stream(old)
+    g.replay()  # untimed replay: uploads the graph
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dist.barrier()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        g.replay()
+        end.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = start.elapsed_time(end)
+    del g
+    return dist.max(ms)
+
+
+# ----------------------------------------------------------------- workloads
+def ple_setup(torch, rt, ctx, n_batches, T=4096, vocab=262144, width=8960, seed=0):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    q = torch.randint(-7, 8, (vocab, width // 2, 2), device="cuda", dtype=torch.int16, generator=gen)
+    nib = (q & 0xF).to(torch.uint8)
+    packed = (nib[..., 0] | (nib[..., 1] << 4)).contiguous()
+    del q, nib
+    sc = torch.randn((vocab, width // 32), device="cuda", generator=gen).abs_().mul_(0.05).to(torch.bfloat16)
+    tab = rt.PleW4Table(ctx, packed, sc)
+    del packed, sc
+    torch.cuda.empty_cache()
+    ids = torch.randint(0, vocab, (n_batches, T), device="cuda", dtype=torch.int32, generator=gen)
+    outs = [torch.empty((T, width), dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+    return tab, ids, outs
+
+
+PLE_BYTES = 4096 * (4480 + 560) + 4096 * 4 + 4096 * 8960 * 2   # 94,060,544 B per call
+
+
+def run_ple(args, torch, rt, ctx, dist, peaks):
+    lib = importlib.import_module("gemma4-js_b200._lib").load()
+    K, W = args.steps, args.warmup
+    tab, ids, outs = ple_setup(torch, rt, ctx, K + W)
+    T = 4096
+
+    def launch(i):
+        st = lib.g4_ple_gather(ctx.handle, tab.handle, C.c_void_p(ids[i].data_ptr()), T, 1,
+                               C.c_void_p(outs[i % 3].data_ptr()), 1)
+        if st:
+            raise RuntimeError(lib.g4_last_error_string())
+
+    n0 = rt.launch_count()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    ms = time_graph(torch, ctx, launch, K, W, dist)
+    clocks = clk.stop()
+    launches = rt.launch_count() - n0 - W
+    ctx.check_device()
+    per_launch_s = ms / 1e3 / K
+    gbs = PLE_BYTES / per_launch_s / 1e9
+    value = gbs * dist.world
+
+    # e2e through the public API: pinned host ids -> device, gather, bf16 rows -> pinned host
+    hid = [torch.randint(0, 262144, (T,), dtype=torch.int32).pin_memory() for _ in range(2)]
+    dev_ids = torch.empty(T, dtype=torch.int32, device="cuda")
+    hout = torch.empty((T, 8960), dtype=torch.bfloat16).pin_memory()
+    e2e_steps = max(3, min(K, 20))
+    for i in range(2):
+        dev_ids.copy_(hid[i], non_blocking=True)
+        tab.rows_to_gpu(dev_ids, out=outs[0])
+        hout.copy_(outs[0], non_blocking=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(e2e_steps):
+        dev_ids.copy_(hid[i % 2], non_blocking=True)
+        tab.rows_to_gpu(dev_ids, out=outs[0])
+        hout.copy_(outs[0], non_blocking=True)
+    e.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = dist.max(s.elapsed_time(e)) / e2e_steps
+    e2e = {"value": round(PLE_BYTES / (e2e_ms / 1e3) / 1e9 * dist.world, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": T * 4, "d2h_bytes_per_step": T * 8960 * 2}
+    peak = peaks["hbm_gbs"]
+    line = {
+        "metric": "PLE W4 gather-dequant throughput (algorithmic bytes)", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded int4 table, uniform ids)",
+        "config": {"workload": "config2_ple_gather", "tokens_per_step_per_gpu": T, "table": [262144, 8960],
+                   "out": "bf16 [4096,35,256]",
+                   "l2": "fresh random ids each step over a 1.32 GB table; 3 rotating 73 MB outputs (> 126 MB L2)"},
+        "roofline": {"bound": "hbm", "kernel": "ple_gather_kernel", "achieved": round(gbs, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
+                     "traffic": TRAFFIC["ple_gather_kernel"], "bytes_per_launch": PLE_BYTES},
+        "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+    }
+    if dist.rank == 0 and dist.world == 1:
+        line["cpu_baseline"] = cpu_ple(sample_s=args.cpu_seconds, threads=1)
+    return line
+
+
+def run_gemv(args, torch, rt, ctx, dist, peaks):
+    lib = importlib.import_module("gemma4-js_b200._lib").load()
+    K, W = args.steps, args.warmup
+    Kd, N, copies = 1536, 6144, 64
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    lins = []
+    for c in range(copies):
+        packed = torch.randint(-2**31, 2**31 - 1, (N, Kd // 8), device="cuda", dtype=torch.int32, generator=gen)
+        sc = torch.randn((N, Kd // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+        lins.append(rt.W4Linear(ctx, packed, sc))
+    x = torch.randn((1, Kd), device="cuda", generator=gen).to(torch.bfloat16)
+    ys = [torch.empty((1, N), dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+
+    def launch(i):
+        st = lib.g4_linear_w4a16_impl(ctx.handle, lins[i % copies].handle, C.c_void_p(x.data_ptr()), 1,
+                                      C.c_void_p(ys[i % 4].data_ptr()), 1, 1)
+        if st:
+            raise RuntimeError(lib.g4_last_error_string())
+
+    n0 = rt.launch_count()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    ms = time_graph(torch, ctx, launch, K, W, dist)
+    clocks = clk.stop()
+    launches = rt.launch_count() - n0 - W
+    byts = N * Kd // 2 + N * Kd // 32 * 2 + Kd * 2 + N * 2   # 5,323,776
+    per = ms / 1e3 / K
+    gbs = byts / per / 1e9
+    peak = peaks["hbm_gbs"]
+    return {
+        "metric": "W4A16 decode GEMV throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
+        "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded)", "config": {"workload": "config1_gemv", "M": 1, "K": Kd, "N": N,
+                                                  "l2": "64 rotating weight copies (340 MB > 126 MB L2)"},
+        "roofline": {"bound": "hbm", "kernel": "gemv_w4a16_kernel", "achieved": round(gbs, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
+                     "traffic": TRAFFIC["gemv_w4a16_kernel"], "bytes_per_launch": byts},
+        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3),
+    }
+
+
+def run_attn(args, torch, rt, ctx, dist, peaks):
+    K, W = args.steps, args.warmup
+    hd, keylen = 256, 4096
+    copies = 40  # 40 x 8 MB of K/V = 320 MB > L2
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    caches = []
+    for c in range(copies):
+        kv = rt.KVCache(ctx, hd, keylen)
+        kv.append(torch.randn((keylen, hd), device="cuda", generator=gen).to(torch.bfloat16),
+                  torch.randn((keylen, hd), device="cuda", generator=gen).to(torch.bfloat16), keylen, 0)
+        caches.append(kv)
+    q = (torch.randn((1, 8, hd), device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    out = torch.empty((1, 8, hd), dtype=torch.bfloat16, device="cuda")
+    ops = rt.GPUOps(ctx)
+
+    def launch(i):
+        ops.attention(q, caches[i % copies], 1, 8, hd, keylen, keylen - 1, False, 512, out=out)
+
+    n0 = rt.launch_count()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    ms = time_graph(torch, ctx, launch, K, W, dist)
+    clocks = clk.stop()
+    launches = rt.launch_count() - n0 - W
+    byts = keylen * hd * 2 * 2 + 2 * 8 * hd * 2
+    per = ms / 1e3 / K
+    gbs = byts / per / 1e9
+    peak = peaks["hbm_gbs"]
+    return {
+        "metric": "GQA decode attention throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
+        "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded)", "config": {"workload": "decode_attention_global", "keylen": keylen, "hd": hd,
+                                                  "heads": 8, "l2": "40 rotating KV caches (320 MB > L2)"},
+        "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": round(gbs, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
+                     "traffic": TRAFFIC["attn_decode_kernel"], "bytes_per_launch": byts},
+        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3),
+    }
+
+
+# ------------------------------------------------------------ CPU baseline --
+def native_oracle():
+    """The oracle's C restatement built for this host's CPU (-march=native)."""
+    oracle = importlib.import_module("oracle")
+    import platform
+    out = REPO / "_build" / f"oracle_native_{platform.node() or 'host'}.so"
+    return oracle, oracle.lib(oracle.build(out, march="native"))
+
+
+def cpu_ple(sample_s: float, threads: int, vocab_sample: int = 8192):
+    """Times the restated LocalPleW4ShardReader.readRows on 4096-id batches over a
+    host table of `vocab_sample` rows with the config's distributions."""
+    import numpy as np
+    oracle, L = native_oracle()
+    rng = np.random.default_rng(0)
+    q = rng.integers(-7, 8, size=(vocab_sample, 8960), dtype=np.int8)
+    nib = (q.astype(np.int16) & 0xF).astype(np.uint8)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+    scales = oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.05, (vocab_sample, 280))).astype(np.float32))
+    ids = rng.integers(0, vocab_sample, 4096).astype(np.int32)
+    oracle.ple_read_rows(packed, scales, ids[:64], bf16=True, nthreads=threads, L=L)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < sample_s:
+        oracle.ple_read_rows(packed, scales, ids, bf16=True, nthreads=threads, L=L)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(PLE_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} x 4096-id gathers (bf16 out) over a {vocab_sample}-row host table, {dt:.1f} s",
+            "calls_per_s": round(n / dt, 4)}
+
+
+def run_reference(args, dist):
+    """Reference arm: the CPU restatement of the TFJS path, all host threads, rank 0 only."""
+    threads = os.cpu_count() or 1
+    if args.workload != "ple":
+        return {"impl": "reference", "unavailable": f"reference arm implemented for workload ple only"}
+    K, W = args.steps, args.warmup
+    import numpy as np
+    oracle, L = native_oracle()
+    rng = np.random.default_rng(0)
+    vs = 8192
+    q = rng.integers(-7, 8, size=(vs, 8960), dtype=np.int8)
+    nib = (q.astype(np.int16) & 0xF).astype(np.uint8)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+    scales = oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.05, (vs, 280))).astype(np.float32))
+    batches = [rng.integers(0, vs, 4096).astype(np.int32) for _ in range(K + W)]
+    for i in range(W):
+        oracle.ple_read_rows(packed, scales, batches[i], bf16=True, nthreads=threads, L=L)
+    t0 = time.perf_counter()
+    for i in range(K):
+        oracle.ple_read_rows(packed, scales, batches[W + i], bf16=True, nthreads=threads, L=L)
+    dt = time.perf_counter() - t0
+    v = PLE_BYTES * K / dt / 1e9
+    return {"impl": "reference", "metric": "PLE W4 gather-dequant throughput (algorithmic bytes)",
+            "value": round(v, 3), "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W,
+            "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded int4 table, uniform ids)",
+            "config": {"workload": "config2_ple_gather", "tokens_per_step_per_gpu": 4096},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"{K} x 4096-id gathers over an {vs}-row host table (C restatement of "
+                                       f"ple-w4-shard-reader.js:65-104; the JS reference has no runtime here)"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="ple", choices=["ple", "gemv", "attn"])
+    ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    dist = Dist()
+    if args.impl == "reference":
+        if dist.rank == 0:
+            print(json.dumps(run_reference(args, dist)), flush=True)
+        return
+    import torch
+    dist.init(use_cuda=True)
+    torch.cuda.set_device(dist.local)
+    rt = importlib.import_module("gemma4-js_b200.runtime")
+    ctx = rt.Context(dist.local)
+    peaks = load_peaks()
+    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn}[args.workload]
+    line = fn(args, torch, rt, ctx, dist, peaks)
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.sync()
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

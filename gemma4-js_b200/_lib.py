@@ -1,0 +1,102 @@
+"""ctypes binding of libg4w4.so (the C ABI declared in include/g4w4.h).
+
+This is the Python twin of the N-API addon a Node host would load: plain pointers,
+sizes and status codes.  There is deliberately no fallback: if the CUDA library is
+missing, importing the runtime fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import re
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libg4w4.so"
+HEADER = PKG.parent / "include" / "g4w4.h"
+
+G4_OK = 0
+G4_F32 = 0
+G4_BF16 = 1
+
+STATUS_NAMES = {
+    0: "G4_OK", -1: "G4_ERR_INVALID", -2: "G4_ERR_OOM", -3: "G4_ERR_CUDA", -4: "G4_ERR_TIMEOUT",
+    -5: "G4_ERR_UNSUPPORTED", -6: "G4_ERR_RANGE", -7: "G4_ERR_DEVICE",
+}
+
+
+class G4Error(RuntimeError):
+    """A failing g4w4 call; `.status` is the g4_status code, str() the library message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+        self.status_name = STATUS_NAMES.get(status, str(status))
+
+
+_P = C.c_void_p
+_I = C.c_int
+_S = C.c_int32
+_PP = C.POINTER(C.c_void_p)
+
+# name -> (restype, argtypes); every g4_status function raises G4Error through check().
+SIGNATURES = {
+    "g4_ctx_create": (_S, [_I, _P, _PP]),
+    "g4_ctx_destroy": (_S, [_P]),
+    "g4_ctx_set_stream": (_S, [_P, _P]),
+    "g4_stream_sync": (_S, [_P]),
+    "g4_ctx_check_device": (_S, [_P, C.POINTER(C.c_uint32)]),
+    "g4_last_error_string": (C.c_char_p, []),
+    "g4_version": (C.c_char_p, []),
+    "g4_kernel_launch_count": (C.c_uint64, []),
+    "g4_linear_create": (_S, [_P, _P, _P, _I, _I, _I, _I, _PP]),
+    "g4_linear_destroy": (_S, [_P]),
+    "g4_linear_shape": (_S, [_P, C.POINTER(_I), C.POINTER(_I)]),
+    "g4_linear_w4a16": (_S, [_P, _P, _P, _I, _P, _I]),
+    "g4_linear_w4a16_impl": (_S, [_P, _P, _P, _I, _P, _I, _I]),
+    "g4_linear_dequant": (_S, [_P, _P, _I, _I, _P, _I]),
+    "g4_ple_table_create": (_S, [_P, _P, _P, _I, _I, _I, _I, _PP]),
+    "g4_ple_table_upload_rows": (_S, [_P, _P, _I, _I, _P, _P, _I]),
+    "g4_ple_table_destroy": (_S, [_P]),
+    "g4_ple_gather": (_S, [_P, _P, _P, _I, _I, _P, _I]),
+    "g4_kv_create": (_S, [_P, _I, _I, _PP]),
+    "g4_kv_destroy": (_S, [_P]),
+    "g4_kv_append": (_S, [_P, _P, _P, _P, _I, _I, _I]),
+    "g4_kv_info": (_S, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
+    "g4_kv_reset": (_S, [_P]),
+    "g4_kv_buffers": (_S, [_P, _PP, _PP]),
+    "g4_attention": (_S, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+}
+
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Every function name declared in include/g4w4.h."""
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:g4_status|const char\*|uint64_t)\s+(g4_\w+)\s*\(", text, re.M)))
+
+
+def load() -> C.CDLL:
+    """Loads libg4w4.so once (no GPU needed) and declares every signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(f"{LIB_PATH} is not built; run `python gemma4-js_b200/build.py`")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    if status != G4_OK:
+        msg = load().g4_last_error_string().decode(errors="replace")
+        raise G4Error(status, msg or STATUS_NAMES.get(status, str(status)))
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

@@ -1,0 +1,467 @@
+// g4_attention.cu -- bf16 KV cache and GQA decode attention (flash-decoding on B200).
+//
+// The reference runs attention as three WGSL dispatches with the logits and
+// probabilities materialised in global memory and a softmax of one thread per row
+// (custom-webgpu/gpu-runtime.js:1204-1248, :1357-1365).  Here one kernel streams the
+// bf16 K/V tiles through shared memory with TMA (128B-swizzled boxes, mbarrier
+// pipeline, one producer warp), computes S^T = K Q^T and O^T += V^T P^T on the tensor
+// cores with the 8 query heads as the n = 8 dimension (so no padding is computed),
+// and keeps an online softmax in registers.  Long key ranges are split over CTAs
+// (split-KV) and merged by a small combine kernel through a scratch buffer.
+#include <stdio.h>
+
+#include "g4_attention.cuh"
+#include "g4_common.cuh"
+
+namespace {
+
+using namespace g4dev;
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int HD>
+struct AttnCfg {
+    static constexpr int KT = 16384 / HD;       // keys per pipeline stage
+    static constexpr int WARPS = KT / 16;       // consumer warps, 16 keys each
+    static constexpr int BOXES = HD / 64;       // 128-byte wide TMA boxes per row
+    static constexpr int BOX_BYTES = KT * 128;  // one box: KT rows x 128 B
+    static constexpr int TILE_BYTES = KT * HD * 2;
+    static constexpr int STAGES = 3;
+    static constexpr int SMEM = STAGES * 2 * TILE_BYTES + 1024 + 256;
+    static constexpr int THREADS = (WARPS + 1) * 32;
+};
+
+// Smem address of (key, d) for ldmatrix in a 128B-swizzled [KT x HD] tile.
+template <int HD>
+__device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int d) {
+    const int box = d >> 6, chunk = (d & 63) >> 3;
+    return base + box * AttnCfg<HD>::BOX_BYTES + key * 128 + (((chunk ^ (key & 7))) << 4);
+}
+
+struct AttnParams {
+    const uint16_t* q;      // [rows, heads, hd]
+    uint16_t* out;          // [rows, heads, hd]
+    float* part_o;          // [rows, nsplit, 8, hd]   (nsplit > 1)
+    float2* part_ml;        // [rows, nsplit, 8]       (nsplit > 1)
+    uint32_t* err;
+    int heads, keylen, qpos0, sliding, window;
+    int nsplit, split_keys;  // keys per split (multiple of KT)
+    int kv_row0;             // first cache row of this sequence in the tensor map
+};
+
+template <int HD>
+__global__ void __launch_bounds__(AttnCfg<HD>::THREADS, 1)
+attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   AttnParams p) {
+    using C = AttnCfg<HD>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kst = smem;                                   // [STAGES][TILE]
+    uint8_t* vst = smem + C::STAGES * C::TILE_BYTES;       // [STAGES][TILE]
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * C::STAGES * C::TILE_BYTES);
+    uint64_t* empty = full + C::STAGES;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.y, split = blockIdx.x;
+    const int qp = p.qpos0 + r;
+    const int hi = min(qp, p.keylen - 1);
+    const int lo = p.sliding ? max(0, qp - p.window + 1) : 0;
+    const int s_lo = lo + split * p.split_keys;
+    const int s_hi = min(hi, s_lo + p.split_keys - 1);  // inclusive
+    const int nkeys = s_hi >= s_lo ? s_hi - s_lo + 1 : 0;
+    const int ntiles = (nkeys + C::KT - 1) / C::KT;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], C::WARPS);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == C::WARPS) {
+        // ------------------------------------------------ TMA producer warp --
+        if (lane == 0 && ntiles > 0) {
+            prefetch_tensor_map(&kmap);
+            prefetch_tensor_map(&vmap);
+            bool ok = true;
+            for (int t = 0; t < ntiles && ok; ++t) {
+                const int s = t % C::STAGES;
+                if (t >= C::STAGES) ok = mbar_wait(&empty[s], ((t / C::STAGES) - 1) & 1, p.err);
+                if (!ok) break;
+                mbar_arrive_expect_tx(&full[s], 2 * C::TILE_BYTES);
+                const int y = p.kv_row0 + s_lo + t * C::KT;
+#pragma unroll
+                for (int b = 0; b < C::BOXES; ++b) {
+                    tma_load_2d(kst + s * C::TILE_BYTES + b * C::BOX_BYTES, &kmap, &full[s], b * 64, y);
+                    tma_load_2d(vst + s * C::TILE_BYTES + b * C::BOX_BYTES, &vmap, &full[s], b * 64, y);
+                }
+            }
+            // Drain: do not leave while our copies may still be landing.
+            const int first = ntiles > C::STAGES ? ntiles - C::STAGES : 0;
+            for (int t = first; t < ntiles; ++t) mbar_wait(&full[t % C::STAGES], (t / C::STAGES) & 1, p.err);
+        }
+        // The producer warp still takes part in the final __syncthreads below.
+    }
+
+    const int g = lane >> 2, tq = lane & 3;
+    float o[HD / 16][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+    if (warp < C::WARPS) {
+        // Q^T as the B operand: b0b1 = Q[head g][16ks + 2tq ..], b2b3 = Q[g][16ks + 8 + 2tq ..]
+        uint32_t qf[HD / 16][2];
+        const uint32_t* qrow = reinterpret_cast<const uint32_t*>(p.q + ((size_t)r * p.heads + g) * HD);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+            qf[ks][0] = g < p.heads ? __ldg(qrow + ks * 8 + tq) : 0u;
+            qf[ks][1] = g < p.heads ? __ldg(qrow + ks * 8 + 4 + tq) : 0u;
+        }
+        const int j = lane >> 3, rr = lane & 7;
+        for (int t = 0; t < ntiles; ++t) {
+            const int s = t % C::STAGES;
+            if (!mbar_wait(&full[s], (t / C::STAGES) & 1, p.err)) break;
+            const uint32_t kb = smem_u32(kst + s * C::TILE_BYTES);
+            const uint32_t vb = smem_u32(vst + s * C::TILE_BYTES);
+            // ---- S^T[16 keys x 8 heads] = K Q^T ----
+            float sc[4] = {0.f, 0.f, 0.f, 0.f};
+            {
+                const int key = warp * 16 + ((j & 1) << 3) + rr;
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ++ks) {
+                    uint32_t a[4];
+                    ldmatrix_x4(a, tile_addr<HD>(kb, key, ks * 16 + ((j >> 1) << 3)));
+                    const uint32_t b[2] = {qf[ks][0], qf[ks][1]};
+                    mma_bf16_16816(sc, a, b, sc);
+                }
+            }
+            // ---- mask (QK_SHADER :1214-1217) and online softmax, base 2 ----
+            const int key0 = s_lo + t * C::KT + warp * 16 + g;
+            const bool v0 = key0 <= s_hi, v1 = key0 + 8 <= s_hi;
+            float x0 = v0 ? sc[0] * kLog2e : -INFINITY, x1 = v0 ? sc[1] * kLog2e : -INFINITY;
+            float x2 = v1 ? sc[2] * kLog2e : -INFINITY, x3 = v1 ? sc[3] * kLog2e : -INFINITY;
+            float mt0 = fmaxf(x0, x2), mt1 = fmaxf(x1, x3);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+                mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+            }
+            const float mn0 = fmaxf(m0, mt0), mn1 = fmaxf(m1, mt1);
+            const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
+            const float al0 = exp2f(m0 - mu0), al1 = exp2f(m1 - mu1);
+            const float p0 = exp2f(x0 - mu0), p1 = exp2f(x1 - mu1);
+            const float p2 = exp2f(x2 - mu0), p3 = exp2f(x3 - mu1);
+            l0 = l0 * al0 + p0 + p2;
+            l1 = l1 * al1 + p1 + p3;
+            m0 = mn0;
+            m1 = mn1;
+            if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+                for (int i = 0; i < HD / 16; ++i) {
+                    o[i][0] *= al0;
+                    o[i][1] *= al1;
+                    o[i][2] *= al0;
+                    o[i][3] *= al1;
+                }
+            }
+            // ---- P^T as the B operand: transpose the two 8x8 key blocks ----
+            const uint32_t pb[2] = {movmatrix_trans(pack_bf16x2_bits(p0, p1)),
+                                    movmatrix_trans(pack_bf16x2_bits(p2, p3))};
+            // ---- O^T[HD x 8] += V^T P^T ----
+            {
+                const int key = warp * 16 + ((j >> 1) << 3) + rr;
+#pragma unroll
+                for (int mi = 0; mi < HD / 16; ++mi) {
+                    uint32_t a[4];
+                    ldmatrix_x4_trans(a, tile_addr<HD>(vb, key, mi * 16 + ((j & 1) << 3)));
+                    mma_bf16_16816(o[mi], a, pb, o[mi]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // per-head l over the 8 lanes g of each tq
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+        }
+    }
+    __syncthreads();  // all TMA traffic has landed and been consumed: reuse the stages
+
+    // ---- merge the consumer warps in shared memory ----
+    float* osm = reinterpret_cast<float*>(smem);                  // [WARPS][8][HD]
+    float* msm = osm + C::WARPS * 8 * HD;                         // [WARPS][8]
+    float* lsm = msm + C::WARPS * 8;                              // [WARPS][8]
+    if (warp < C::WARPS) {
+        float* ow = osm + warp * 8 * HD;
+#pragma unroll
+        for (int i = 0; i < HD / 16; ++i) {
+            const int d = i * 16 + g;
+            ow[(2 * tq) * HD + d] = o[i][0];
+            ow[(2 * tq + 1) * HD + d] = o[i][1];
+            ow[(2 * tq) * HD + d + 8] = o[i][2];
+            ow[(2 * tq + 1) * HD + d + 8] = o[i][3];
+        }
+        if (g == 0) {
+            msm[warp * 8 + 2 * tq] = m0;
+            msm[warp * 8 + 2 * tq + 1] = m1;
+            lsm[warp * 8 + 2 * tq] = l0;
+            lsm[warp * 8 + 2 * tq + 1] = l1;
+        }
+    }
+    __syncthreads();
+    const int nh = p.heads;
+    for (int idx = threadIdx.x; idx < nh * HD; idx += blockDim.x) {
+        const int h = idx / HD, d = idx - h * HD;
+        float m = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < C::WARPS; ++w) m = fmaxf(m, msm[w * 8 + h]);
+        const float mu = m == -INFINITY ? 0.f : m;
+        float l = 0.f, acc = 0.f;
+#pragma unroll
+        for (int w = 0; w < C::WARPS; ++w) {
+            const float f = exp2f(msm[w * 8 + h] - mu);
+            l += f * lsm[w * 8 + h];
+            acc += f * osm[(w * 8 + h) * HD + d];
+        }
+        if (p.nsplit == 1) {
+            p.out[((size_t)r * nh + h) * HD + d] = (uint16_t)f32_to_bf16_bits(acc / l);
+        } else {
+            const size_t pi = ((size_t)r * p.nsplit + split) * 8 + h;
+            p.part_o[pi * HD + d] = acc;
+            if (d == 0) p.part_ml[pi] = make_float2(m, l);
+        }
+    }
+}
+
+// Merges the split-KV partials of one query row (log-sum-exp weights).
+template <int HD>
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
+                                    int nsplit, int heads, uint16_t* __restrict__ out) {
+    const int r = blockIdx.x;
+    for (int idx = threadIdx.x; idx < heads * HD; idx += blockDim.x) {
+        const int h = idx / HD, d = idx - h * HD;
+        float m = -INFINITY;
+        for (int s = 0; s < nsplit; ++s) m = fmaxf(m, part_ml[((size_t)r * nsplit + s) * 8 + h].x);
+        const float mu = m == -INFINITY ? 0.f : m;
+        float l = 0.f, acc = 0.f;
+        for (int s = 0; s < nsplit; ++s) {
+            const size_t pi = ((size_t)r * nsplit + s) * 8 + h;
+            const float2 ml = part_ml[pi];
+            const float f = exp2f(ml.x - mu);
+            l += f * ml.y;
+            acc += f * part_o[pi * HD + d];
+        }
+        out[((size_t)r * heads + h) * HD + d] = (uint16_t)f32_to_bf16_bits(acc / l);
+    }
+}
+
+// Appends rows to the bf16 cache, rounding f32 input to nearest even.
+__global__ void kv_append_f32_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                     uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, long long n) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    kc[i] = (uint16_t)f32_to_bf16_bits(k[i]);
+    vc[i] = (uint16_t)f32_to_bf16_bits(v[i]);
+}
+
+template <int HD>
+g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& vm, const uint16_t* q,
+                        int rows, int heads, int keylen, int qpos0, int sliding, int window, uint16_t* out,
+                        int kv_row0) {
+    using C = AttnCfg<HD>;
+    // Longest key range of any row decides the split.
+    const int qp_last = qpos0 + rows - 1;
+    int lmax = min(qp_last, keylen - 1) + 1;
+    if (sliding) lmax = min(lmax, window);
+    const int ntiles = (lmax + C::KT - 1) / C::KT;
+    int nsplit = (2 * ctx->num_sms + rows - 1) / rows;
+    nsplit = min(nsplit, max(1, (ntiles + 1) / 2));
+    nsplit = max(nsplit, 1);
+    const int tiles_per_split = (ntiles + nsplit - 1) / nsplit;
+    nsplit = (ntiles + tiles_per_split - 1) / tiles_per_split;
+    if (nsplit < 1) nsplit = 1;
+
+    AttnParams p{};
+    p.q = q;
+    p.out = out;
+    p.err = ctx->d_err;
+    p.heads = heads;
+    p.keylen = keylen;
+    p.qpos0 = qpos0;
+    p.sliding = sliding;
+    p.window = window;
+    p.nsplit = nsplit;
+    p.split_keys = tiles_per_split * C::KT;
+    p.kv_row0 = kv_row0;
+    if (nsplit > 1) {
+        const size_t ob = (size_t)rows * nsplit * 8 * HD * sizeof(float);
+        const size_t mb = (size_t)rows * nsplit * 8 * sizeof(float2);
+        g4_status st = g4::ensure_workspace(ctx, ob + mb + 256);
+        if (st) return st;
+        p.part_o = static_cast<float*>(ctx->ws);
+        p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(ctx->ws) + ((ob + 255) & ~size_t(255)));
+    }
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    attn_decode_kernel<HD><<<dim3(nsplit, rows), C::THREADS, C::SMEM, ctx->stream>>>(km, vm, p);
+    G4_CHECK_LAUNCH("attn_decode_kernel");
+    if (nsplit > 1) {
+        attn_combine_kernel<HD><<<rows, 256, 0, ctx->stream>>>(p.part_o, p.part_ml, nsplit, heads, out);
+        G4_CHECK_LAUNCH("attn_combine_kernel");
+    }
+    return G4_OK;
+}
+
+}  // namespace
+
+namespace g4 {
+
+g4_status make_kv_maps(g4_kv* kv) {
+    const uint32_t kt = 16384u / (uint32_t)kv->hd;
+    g4_status st = encode_tensor_map_2d(&kv->kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kv->k, kv->hd,
+                                        kv->rows_total, (uint64_t)kv->hd * 2, 64, kt,
+                                        CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    return encode_tensor_map_2d(&kv->vmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kv->v, kv->hd, kv->rows_total,
+                                (uint64_t)kv->hd * 2, 64, kt, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+g4_status launch_attention(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows, int heads,
+                           int keylen, int qpos0, int sliding, int window, uint16_t* out) {
+    switch (kv->hd) {
+        case 64: return launch_attn_t<64>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
+        case 128: return launch_attn_t<128>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
+        case 256: return launch_attn_t<256>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
+        case 512: return launch_attn_t<512>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
+        default: return set_error(G4_ERR_UNSUPPORTED, "attention: head dim %d (64/128/256/512 supported)", kv->hd);
+    }
+}
+
+}  // namespace g4
+
+extern "C" {
+
+g4_status g4_kv_create(g4_ctx* ctx, int hd, int capacity, g4_kv** out) {
+    if (!out) return g4::set_error(G4_ERR_INVALID, "g4_kv_create: null out");
+    *out = nullptr;
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (hd != 64 && hd != 128 && hd != 256 && hd != 512)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_kv_create: head dim %d (64/128/256/512 supported)", hd);
+    if (capacity <= 0) return g4::set_error(G4_ERR_INVALID, "g4_kv_create: capacity %d", capacity);
+    g4_kv* kv = new g4_kv();
+    kv->ctx = ctx;
+    kv->hd = hd;
+    kv->capacity = capacity;
+    kv->rows_total = capacity;
+    const size_t bytes = (size_t)capacity * hd * 2;
+    cudaError_t e = cudaMalloc(&kv->k, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&kv->v, bytes);
+    // Zero-fill: masked keys must hold finite values (p = 0 times V must stay 0).
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->k, 0, bytes, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->v, 0, bytes, ctx->stream);
+    if (e != cudaSuccess) {
+        g4_kv_destroy(kv);
+        return g4::cuda_error(e, "g4_kv_create");
+    }
+    st = g4::make_kv_maps(kv);
+    if (st) {
+        g4_kv_destroy(kv);
+        return st;
+    }
+    *out = kv;
+    return G4_OK;
+}
+
+g4_status g4_kv_destroy(g4_kv* kv) {
+    if (!kv) return G4_OK;
+    if (kv->ctx) {
+        cudaSetDevice(kv->ctx->device);
+        cudaStreamSynchronize(kv->ctx->stream);
+    }
+    cudaFree(kv->k);
+    cudaFree(kv->v);
+    delete kv;
+    return G4_OK;
+}
+
+g4_status g4_kv_append(g4_ctx* ctx, g4_kv* kv, const void* k, const void* v, int rows, int start_pos,
+                       g4_dtype src_dtype) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!kv || !k || !v) return g4::set_error(G4_ERR_INVALID, "g4_kv_append: null argument");
+    // gemma4-webgpu.js:129-130
+    if (start_pos != kv->length)
+        return g4::set_error(G4_ERR_INVALID, "KV append position %d != cache length %d", start_pos, kv->length);
+    if (rows < 0 || start_pos + rows > kv->capacity)
+        return g4::set_error(G4_ERR_RANGE, "KV cache capacity %d exceeded", kv->capacity);
+    if (rows == 0) return G4_OK;
+    const size_t n = (size_t)rows * kv->hd;
+    uint16_t* kd = kv->k + (size_t)start_pos * kv->hd;
+    uint16_t* vd = kv->v + (size_t)start_pos * kv->hd;
+    if (src_dtype == G4_BF16) {
+        G4_CHECK_CUDA(cudaMemcpyAsync(kd, k, n * 2, cudaMemcpyDeviceToDevice, ctx->stream));
+        G4_CHECK_CUDA(cudaMemcpyAsync(vd, v, n * 2, cudaMemcpyDeviceToDevice, ctx->stream));
+    } else if (src_dtype == G4_F32) {
+        kv_append_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
+            static_cast<const float*>(k), static_cast<const float*>(v), kd, vd, (long long)n);
+        G4_CHECK_LAUNCH("kv_append_f32_kernel");
+    } else {
+        return g4::set_error(G4_ERR_INVALID, "g4_kv_append: dtype %d", (int)src_dtype);
+    }
+    kv->length += rows;
+    return G4_OK;
+}
+
+g4_status g4_kv_info(const g4_kv* kv, int* length, int* hd, int* capacity) {
+    if (!kv) return g4::set_error(G4_ERR_INVALID, "null kv");
+    if (length) *length = kv->length;
+    if (hd) *hd = kv->hd;
+    if (capacity) *capacity = kv->capacity;
+    return G4_OK;
+}
+
+g4_status g4_kv_reset(g4_kv* kv) {
+    if (!kv) return g4::set_error(G4_ERR_INVALID, "null kv");
+    kv->length = 0;
+    return G4_OK;
+}
+
+g4_status g4_kv_buffers(const g4_kv* kv, void** k, void** v) {
+    if (!kv) return g4::set_error(G4_ERR_INVALID, "null kv");
+    if (k) *k = kv->k;
+    if (v) *v = kv->v;
+    return G4_OK;
+}
+
+g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads, int hd,
+                       int keylen, int qpos0, int sliding, int window, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!kv || !q_bf16 || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_attention: null argument");
+    if (rows < 0) return g4::set_error(G4_ERR_INVALID, "g4_attention: rows %d", rows);
+    if (rows == 0) return G4_OK;
+    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "g4_attention: hd %d != cache hd %d", hd, kv->hd);
+    if (heads < 1 || heads > 8)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_attention: %d heads per KV head (1..8 supported)", heads);
+    if (keylen < 1 || keylen > kv->length)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention: keylen %d outside cache length %d", keylen, kv->length);
+    if (qpos0 < 0 || qpos0 + rows > keylen)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention: query positions [%d,%d) not below keylen %d", qpos0,
+                             qpos0 + rows, keylen);
+    if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "g4_attention: window %d", window);
+    if (reinterpret_cast<uintptr_t>(q_bf16) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention: q must be 16-byte aligned");
+    return g4::launch_attention(ctx, kv, 0, static_cast<const uint16_t*>(q_bf16), rows, heads, keylen, qpos0,
+                                sliding ? 1 : 0, window, static_cast<uint16_t*>(out_bf16));
+}
+
+}  // extern "C"

@@ -1,0 +1,412 @@
+// g4_linear.cu -- W4A16 linear: device re-layout, bit-exact dequant, split-K decode GEMV.
+//
+// The reference uploads `weight_packed` I32 [N, K/8] and `weight_scale` BF16 [N, K/32]
+// unchanged (custom-webgpu/gpu-runtime.js:1385-1392) and runs one WGSL thread per
+// output element over all of K (W4_SHADER :1068-1102).  Here g4_linear_create
+// re-lays the same bits out once, into the order the kernels consume:
+//
+//   wfrag: uint4 [N/16][K/64][32 lanes]  (one 512-byte block per 16 rows x 64 columns)
+//     lane l = 4g + t holds, for rows r0 = 16*nt + g and r1 = r0 + 8 and the two
+//     32-column groups G = 2c, 2c+1, word t of that row-group (columns 32G+8t..+7):
+//       {word(r0, 2c, t), word(r1, 2c, t), word(r0, 2c+1, t), word(r1, 2c+1, t)}
+//     with the 8 nibbles of each word reordered n0 n2 n4 n6 n1 n3 n5 n7 (low to high),
+//     so (w >> 4p) & 0x000F000F yields columns (2p, 2p+1) as a bf16x2 pair.
+//   sfrag: uint2 [N/16][K/64][8]: {s(r0,2c), s(r1,2c), s(r0,2c+1), s(r1,2c+1)} for g.
+//
+// That is exactly the register fragment of mma.m16n8k16 (A = 16 weight rows, B = 8
+// activation rows) once the k index inside each group is permuted consistently for
+// weights and activations, so every lane loads its operand with one 16-byte load and
+// activations with two 16-byte loads.  The same blocks feed the tcgen05 GEMM producer.
+#include <cooperative_groups.h>
+#include <stdio.h>
+
+#include "g4_common.cuh"
+#include "g4_linear.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace {
+
+using namespace g4dev;
+
+__host__ __device__ __forceinline__ uint32_t permute_nibbles(uint32_t w) {
+    // nibble i of the input goes to position kPos[i] = {0,4,1,5,2,6,3,7}[i]
+    uint32_t o = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int pos = (i >> 1) + ((i & 1) << 2);
+        o |= ((w >> (4 * i)) & 0xFu) << (4 * pos);
+    }
+    return o;
+}
+
+__host__ __device__ __forceinline__ uint32_t unpermute_nibble(uint32_t w, int i) {
+    const int pos = (i >> 1) + ((i & 1) << 2);
+    return (w >> (4 * pos)) & 0xFu;
+}
+
+// One thread per (n-tile, 64-column chunk, lane).
+__global__ void repack_kernel(const uint32_t* __restrict__ raw, const uint16_t* __restrict__ raw_s,
+                              int K, int N, int Kc, int NT, uint4* __restrict__ wfrag,
+                              uint2* __restrict__ sfrag) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)NT * Kc * 32) return;
+    const int lane = (int)(i & 31);
+    const long long blk = i >> 5;
+    const int c = (int)(blk % Kc);
+    const int nt = (int)(blk / Kc);
+    const int g = lane >> 2, t = lane & 3;
+    const int groups = K / 32, words = K / 8;
+    uint32_t out[4];
+    uint16_t sc[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int row = nt * 16 + g + ((q & 1) ? 8 : 0);
+        const int G = 2 * c + (q >> 1);
+        const bool ok = row < N && G < groups;
+        const uint32_t wv = ok ? raw[(size_t)row * words + G * 4 + t] : 0x88888888u;
+        out[q] = permute_nibbles(wv);
+        sc[q] = ok ? raw_s[(size_t)row * groups + G] : (uint16_t)0;
+    }
+    wfrag[i] = make_uint4(out[0], out[1], out[2], out[3]);
+    if (t == 0)
+        sfrag[blk * 8 + g] = make_uint2((uint32_t)sc[0] | ((uint32_t)sc[1] << 16),
+                                        (uint32_t)sc[2] | ((uint32_t)sc[3] << 16));
+}
+
+// Reads one original word back out of the fragment layout.
+__device__ __forceinline__ void locate(const g4_linear_dev& L, int row, int word, uint32_t& w,
+                                       uint32_t& sbits) {
+    const int nt = row >> 4, r16 = row & 15, g = r16 & 7, hi = r16 >> 3;
+    const int k = word * 8, Gabs = k >> 5, c = Gabs >> 1, G = Gabs & 1, t = (k & 31) >> 3;
+    const size_t blk = (size_t)nt * L.Kc + c;
+    const uint4 v = L.wfrag[blk * 32 + g * 4 + t];
+    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+    w = vw[G * 2 + hi];
+    const uint2 s = L.sfrag[blk * 8 + g];
+    const uint32_t sw = G ? s.y : s.x;
+    sbits = hi ? (sw >> 16) : (sw & 0xFFFFu);
+}
+
+// dequantizeOfficialW4A16Rows (official-w4a16.js:84-96) over the device layout.
+template <bool kF32Out>
+__global__ void dequant_kernel(g4_linear_dev L, int row_start, int row_count, void* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int words = L.K / 8;
+    if (i >= (long long)row_count * words) return;
+    const int lr = (int)(i / words), word = (int)(i - (long long)lr * words);
+    uint32_t w, sbits;
+    locate(L, row_start + lr, word, w, sbits);
+    const float s = bf16_bits_to_f32(sbits);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = (float)((int)unpermute_nibble(w, e) - 8) * s;
+    if constexpr (kF32Out) {
+        float4* o = reinterpret_cast<float4*>(out) + i * 2;
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        uint4* o = reinterpret_cast<uint4*>(out) + i;
+        *o = make_uint4(pack_bf16x2_bits(v[0], v[1]), pack_bf16x2_bits(v[2], v[3]),
+                        pack_bf16x2_bits(v[4], v[5]), pack_bf16x2_bits(v[6], v[7]));
+    }
+}
+
+__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+constexpr int kGemvWarps = 4;
+constexpr int kGemvUnroll = 4;
+
+// Split-K decode GEMV.  CTA (nt, s) owns rows 16*nt..+15 and the s-th slice of the
+// K chunks; its 4 warps interleave over the slice's 512-byte blocks.  Partial tiles
+// are summed across warps in shared memory and across the S CTAs of the cluster
+// through distributed shared memory, so no global scratch and no atomics are used.
+// kNB = number of 8-row activation tiles (1: M <= 8, 2: M <= 16).
+template <int kNB>
+__global__ void __launch_bounds__(kGemvWarps * 32, 4)
+gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ldx,
+                  void* __restrict__ y, int ldy, int y_f32, int chunks_per_split) {
+    __shared__ float red[kGemvWarps][kNB * 4][32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int nt = blockIdx.x;
+    const int split = blockIdx.y;
+    const int c_begin = split * chunks_per_split;
+    const int c_end = min(L.Kc, c_begin + chunks_per_split);
+
+    float acc[kNB][4];
+#pragma unroll
+    for (int j = 0; j < kNB; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+
+    const uint4* wbase = L.wfrag + (size_t)nt * L.Kc * 32 + lane;
+    const uint2* sbase = L.sfrag + (size_t)nt * L.Kc * 8 + g;
+
+    for (int c0 = c_begin + warp; c0 < c_end; c0 += kGemvWarps * kGemvUnroll) {
+        uint4 wv[kGemvUnroll];
+        uint2 sv[kGemvUnroll];
+        uint4 xv[kGemvUnroll][kNB][2];
+        // ---- issue every load of up to kGemvUnroll chunks before any math ----
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            const int c = c0 + u * kGemvWarps;
+            const bool cv = c < c_end;
+            wv[u] = cv ? ld_stream_u4(wbase + (size_t)c * 32) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+            sv[u] = cv ? __ldg(sbase + (size_t)c * 8) : make_uint2(0, 0);
+#pragma unroll
+            for (int j = 0; j < kNB; ++j) {
+                const int b = j * 8 + g;
+#pragma unroll
+                for (int G = 0; G < 2; ++G) {
+                    const int k = c * 64 + G * 32 + t * 8;
+                    xv[u][j][G] = (cv && b < M && k < L.K)
+                                      ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)b * ldx + k))
+                                      : make_uint4(0, 0, 0, 0);
+                }
+            }
+        }
+        // ---- dequant + tensor-core dot per 32-column group ----
+#pragma unroll
+        for (int u = 0; u < kGemvUnroll; ++u) {
+            const uint32_t wq[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+            for (int G = 0; G < 2; ++G) {
+                const uint32_t w0 = wq[2 * G], w1 = wq[2 * G + 1];
+                const uint32_t a0[4] = {int4pair_to_bf16x2(w0), int4pair_to_bf16x2(w1),
+                                        int4pair_to_bf16x2(w0 >> 4), int4pair_to_bf16x2(w1 >> 4)};
+                const uint32_t a1[4] = {int4pair_to_bf16x2(w0 >> 8), int4pair_to_bf16x2(w1 >> 8),
+                                        int4pair_to_bf16x2(w0 >> 12), int4pair_to_bf16x2(w1 >> 12)};
+                const uint32_t sw = G ? sv[u].y : sv[u].x;
+                const float s_lo = bf16_bits_to_f32(sw & 0xFFFFu), s_hi = bf16_bits_to_f32(sw >> 16);
+#pragma unroll
+                for (int j = 0; j < kNB; ++j) {
+                    const uint4 xg = xv[u][j][G];
+                    const uint32_t b0[2] = {xg.x, xg.y}, b1[2] = {xg.z, xg.w};
+                    float d[4];
+                    const float z[4] = {0.f, 0.f, 0.f, 0.f};
+                    mma_bf16_16816(d, a0, b0, z);
+                    mma_bf16_16816(d, a1, b1, d);
+                    acc[j][0] = fmaf(s_lo, d[0], acc[j][0]);
+                    acc[j][1] = fmaf(s_lo, d[1], acc[j][1]);
+                    acc[j][2] = fmaf(s_hi, d[2], acc[j][2]);
+                    acc[j][3] = fmaf(s_hi, d[3], acc[j][3]);
+                }
+            }
+        }
+    }
+
+    // ---- reduce the 4 warps of the CTA ----
+#pragma unroll
+    for (int j = 0; j < kNB; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) red[warp][j * 4 + e][lane] = acc[j][e];
+    __syncthreads();
+    if (warp == 0) {
+#pragma unroll
+        for (int q = 0; q < kNB * 4; ++q) {
+            float s = red[0][q][lane];
+#pragma unroll
+            for (int w2 = 1; w2 < kGemvWarps; ++w2) s += red[w2][q][lane];
+            red[0][q][lane] = s;
+        }
+    }
+    // ---- reduce the S CTAs of the cluster through distributed shared memory ----
+    const int S = gridDim.y;
+    if (S > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (split == 0 && warp == 0) {
+#pragma unroll
+            for (int q = 0; q < kNB * 4; ++q) {
+                float s = red[0][q][lane];
+                for (int r = 1; r < S; ++r) s += cluster.map_shared_rank(&red[0][q][lane], r)[0];
+                red[0][q][lane] = s;
+            }
+        }
+        cluster.sync();
+        if (split != 0) return;
+    } else {
+        __syncthreads();
+    }
+    if (warp != 0) return;
+#pragma unroll
+    for (int j = 0; j < kNB; ++j) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int row = nt * 16 + g + ((e & 2) ? 8 : 0);
+            const int b = j * 8 + 2 * t + (e & 1);
+            if (row < L.N && b < M) {
+                const float v = red[0][j * 4 + e][lane];
+                if (y_f32)
+                    reinterpret_cast<float*>(y)[(size_t)b * ldy + row] = v;
+                else
+                    reinterpret_cast<uint16_t*>(y)[(size_t)b * ldy + row] = (uint16_t)f32_to_bf16_bits(v);
+            }
+        }
+    }
+}
+
+}  // namespace
+
+namespace g4 {
+
+g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y,
+                      int y_f32) {
+    const g4_linear_dev& L = lin->dev;
+    for (int m0 = 0; m0 < M; m0 += 16) {
+        const int mm = (M - m0) < 16 ? (M - m0) : 16;
+        int S = 1;
+        const int target = ctx->num_sms * 4;
+        while (L.NT * S < target && S < 8 && L.Kc >= 2 * S * kGemvWarps) S *= 2;
+        const int cps = (L.Kc + S - 1) / S;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(L.NT, S, 1);
+        cfg.blockDim = dim3(kGemvWarps * 32, 1, 1);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = ctx->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = S;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const uint16_t* xs = x + (size_t)m0 * L.K;
+        void* ys = y_f32 ? (void*)(reinterpret_cast<float*>(y) + (size_t)m0 * L.N)
+                         : (void*)(reinterpret_cast<uint16_t*>(y) + (size_t)m0 * L.N);
+        cudaError_t e;
+        if (mm <= 8)
+            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<1>, L, xs, mm, L.K, ys, L.N, y_f32, cps);
+        else
+            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<2>, L, xs, mm, L.K, ys, L.N, y_f32, cps);
+        if (e != cudaSuccess) return cuda_error(e, "gemv_w4a16_kernel");
+        count_launch();
+    }
+    return G4_OK;
+}
+
+}  // namespace g4
+
+extern "C" {
+
+g4_status g4_linear_create(g4_ctx* ctx, const void* packed_i32, const void* scales_bf16, int K,
+                           int N, int group, int src_on_device, g4_linear** out) {
+    if (!out) return g4::set_error(G4_ERR_INVALID, "g4_linear_create: null out");
+    *out = nullptr;
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!packed_i32 || !scales_bf16) return g4::set_error(G4_ERR_INVALID, "g4_linear_create: null weights");
+    if (K <= 0 || N <= 0) return g4::set_error(G4_ERR_INVALID, "g4_linear_create: K=%d N=%d", K, N);
+    // official-w4a16.js:59-64
+    if (K % 8 != 0) return g4::set_error(G4_ERR_INVALID, "inDim must be divisible by 8.");
+    if (group <= 0 || K % group != 0) return g4::set_error(G4_ERR_INVALID, "inDim must be divisible by groupSize.");
+    if (group != 32)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_linear_create: group size %d (only 32 is implemented)", group);
+    g4_linear* lin = new g4_linear();
+    lin->ctx = ctx;
+    g4_linear_dev& L = lin->dev;
+    L.K = K;
+    L.N = N;
+    L.Kc = (K + 63) / 64;
+    L.NT = (N + 15) / 16;
+    const size_t raw_w = (size_t)N * (K / 8) * 4, raw_s = (size_t)N * (K / 32) * 2;
+    const size_t nblk = (size_t)L.NT * L.Kc;
+    void *dw = nullptr, *ds = nullptr;
+    cudaError_t e = cudaMalloc(&L.wfrag, nblk * 32 * sizeof(uint4));
+    if (e == cudaSuccess) e = cudaMalloc(&L.sfrag, nblk * 8 * sizeof(uint2));
+    if (e == cudaSuccess && !src_on_device) {
+        e = cudaMalloc(&dw, raw_w);
+        if (e == cudaSuccess) e = cudaMalloc(&ds, raw_s);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(dw, packed_i32, raw_w, cudaMemcpyHostToDevice, ctx->stream);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(ds, scales_bf16, raw_s, cudaMemcpyHostToDevice, ctx->stream);
+    }
+    if (e == cudaSuccess) {
+        const uint32_t* rw = static_cast<const uint32_t*>(src_on_device ? packed_i32 : dw);
+        const uint16_t* rs = static_cast<const uint16_t*>(src_on_device ? scales_bf16 : ds);
+        const long long threads = (long long)nblk * 32;
+        repack_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, ctx->stream>>>(rw, rs, K, N, L.Kc, L.NT,
+                                                                                  L.wfrag, L.sfrag);
+        e = cudaGetLastError();
+        g4::count_launch();
+    }
+    if (e == cudaSuccess && !src_on_device) e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(dw);
+    cudaFree(ds);
+    if (e != cudaSuccess) {
+        g4_linear_destroy(lin);
+        return g4::cuda_error(e, "g4_linear_create");
+    }
+    *out = lin;
+    return G4_OK;
+}
+
+g4_status g4_linear_destroy(g4_linear* lin) {
+    if (!lin) return G4_OK;
+    if (lin->ctx) cudaSetDevice(lin->ctx->device);
+    cudaFree(lin->dev.wfrag);
+    cudaFree(lin->dev.sfrag);
+    delete lin;
+    return G4_OK;
+}
+
+g4_status g4_linear_shape(const g4_linear* lin, int* K, int* N) {
+    if (!lin) return g4::set_error(G4_ERR_INVALID, "null linear");
+    if (K) *K = lin->dev.K;
+    if (N) *N = lin->dev.N;
+    return G4_OK;
+}
+
+g4_status g4_linear_dequant(g4_ctx* ctx, const g4_linear* lin, int row_start, int row_count,
+                            void* out, g4_dtype out_dtype) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!lin || !out) return g4::set_error(G4_ERR_INVALID, "g4_linear_dequant: null argument");
+    if (row_start < 0 || row_count < 0 || row_start + row_count > lin->dev.N)
+        return g4::set_error(G4_ERR_RANGE, "g4_linear_dequant: rows [%d,%d) outside %d", row_start,
+                             row_start + row_count, lin->dev.N);
+    if (row_count == 0) return G4_OK;
+    const long long threads = (long long)row_count * (lin->dev.K / 8);
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    if (out_dtype == G4_F32)
+        dequant_kernel<true><<<blocks, 256, 0, ctx->stream>>>(lin->dev, row_start, row_count, out);
+    else if (out_dtype == G4_BF16)
+        dequant_kernel<false><<<blocks, 256, 0, ctx->stream>>>(lin->dev, row_start, row_count, out);
+    else
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_dequant: dtype %d", (int)out_dtype);
+    G4_CHECK_LAUNCH("dequant_kernel");
+    return G4_OK;
+}
+
+g4_status g4_linear_w4a16_impl(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
+                               void* y, g4_dtype y_dtype, int impl) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!lin) return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16: null linear");
+    if (M < 0) return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16: M = %d", M);
+    if (M == 0) return G4_OK;
+    if (!x_bf16 || !y) return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16: null x/y");
+    if (y_dtype != G4_F32 && y_dtype != G4_BF16)
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16: y dtype %d", (int)y_dtype);
+    if (reinterpret_cast<uintptr_t>(x_bf16) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16: x must be 16-byte aligned");
+    const int y_f32 = y_dtype == G4_F32;
+    if (impl == 0) impl = (M <= 16) ? 1 : 2;
+    if (impl == 2 && !g4::gemm_supported(lin, M)) impl = 1;
+    if (impl == 1) return g4::launch_gemv(ctx, lin, static_cast<const uint16_t*>(x_bf16), M, y, y_f32);
+    if (impl == 2) return g4::launch_gemm(ctx, lin, static_cast<const uint16_t*>(x_bf16), M, y, y_f32);
+    return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_impl: impl %d", impl);
+}
+
+g4_status g4_linear_w4a16(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, void* y,
+                          g4_dtype y_dtype) {
+    return g4_linear_w4a16_impl(ctx, lin, x_bf16, M, y, y_dtype, 0);
+}
+
+}  // extern "C"

@@ -1,0 +1,228 @@
+// g4_ple.cu -- PLE W4 table on the device and the gather-dequant kernel.
+//
+// Replaces the reference's per-token shard byte gather on the CPU plus the WGSL
+// dequant (custom-webgpu/gpu-runtime.js:218-256, :265-335, :487-527): here the whole
+// [vocab, 8960] W4 table (1.32 GB) stays resident in HBM and one kernel gathers and
+// dequantises the rows of a token batch straight into [T, 35, 256].
+#include <stdio.h>
+
+#include "g4_common.cuh"
+
+struct g4_ple_table {
+    g4_ctx* ctx = nullptr;
+    int vocab = 0, width = 0, group = 0;
+    uint8_t* packed = nullptr;   // [vocab, width/2]
+    uint16_t* scales = nullptr;  // [vocab, width/group] bf16 bits
+};
+
+namespace {
+
+using namespace g4dev;
+
+// One thread per (token, group of 32 columns): 16 B of packed nibbles and one bf16
+// scale in, 64 B (bf16) or 128 B (f32) out.  Consecutive threads walk consecutive
+// groups of a row, so loads and stores are fully coalesced.
+//
+// Decode (ple-w4-shard-reader.js:89-95): column c is nibble (c & 1) of byte c >> 1,
+// i.e. bits 4c..4c+3 of the little-endian 32-bit word c >> 3; value = two's
+// complement nibble * f32(scale), exact in f32.
+template <bool kF32Out>
+__global__ void __launch_bounds__(256) ple_gather_kernel(const uint4* __restrict__ packed,
+                                                         const uint16_t* __restrict__ scales,
+                                                         const int32_t* __restrict__ ids, int T,
+                                                         int vocab, int groups_per_row,
+                                                         void* __restrict__ out, uint32_t* err) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = (long long)T * groups_per_row;
+    if (i >= total) return;
+    const int t = (int)(i / groups_per_row);
+    const int j = (int)(i - (long long)t * groups_per_row);
+    const int id = __ldg(ids + t);
+    const bool ok = (unsigned)id < (unsigned)vocab;
+    if (!ok && j == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
+    const size_t src = (size_t)(ok ? id : 0) * groups_per_row + j;
+    uint4 p = make_uint4(0, 0, 0, 0);
+    uint32_t sbits = 0;
+    if (ok) {
+        p = __ldg(packed + src);
+        sbits = __ldg(scales + src);
+    }
+    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
+    if constexpr (!kF32Out) {
+        // bf16 out = RNE(q * s).  q * s is exact in f32, so rounding it once to bf16
+        // equals one correctly rounded bf16 multiply of the exact operands q and s.
+        const uint32_t s2 = sbits | (sbits << 16);
+        uint4* o = reinterpret_cast<uint4*>(out) + i * 4;
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            uint32_t r[4];
+#pragma unroll
+            for (int pp = 0; pp < 4; ++pp) {
+                // nibbles pp and pp+4 of the word -> bf16x2 (136 + q) -> exact q
+                uint32_t v;
+                asm("lop3.b32 %0, %1, %2, %3, 0x6A;"
+                    : "=r"(v)
+                    : "r"(w[wi] >> (4 * pp)), "r"(0x000F000Fu), "r"(0x43084308u));
+                uint32_t q;
+                asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(0x43084308u));
+                asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[pp]) : "r"(q), "r"(s2));
+            }
+            // r[pp] holds columns (pp, pp+4) of this word; emit (0,1) (2,3) (4,5) (6,7)
+            uint4 ov;
+            ov.x = __byte_perm(r[0], r[1], 0x5410);
+            ov.y = __byte_perm(r[2], r[3], 0x5410);
+            ov.z = __byte_perm(r[0], r[1], 0x7632);
+            ov.w = __byte_perm(r[2], r[3], 0x7632);
+            o[wi] = ov;
+        }
+    } else {
+        const float s = bf16_bits_to_f32(sbits);
+        float4* o = reinterpret_cast<float4*>(out) + i * 8;
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                // ((n ^ 8) | 0x4B000000) as f32 = 2^23 + q + 8
+                const uint32_t m = ((w[wi] >> (4 * e)) & 0xFu) ^ 0x4B000008u;
+                v[e] = (__uint_as_float(m) - 8388616.0f) * s;
+            }
+            o[wi * 2 + 0] = make_float4(v[0], v[1], v[2], v[3]);
+            o[wi * 2 + 1] = make_float4(v[4], v[5], v[6], v[7]);
+        }
+    }
+}
+
+g4_status copy_in(void* dst, const void* src, size_t bytes, int src_on_device, cudaStream_t s) {
+    G4_CHECK_CUDA(cudaMemcpyAsync(dst, src, bytes,
+                                  src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s));
+    return G4_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+g4_status g4_ple_table_create(g4_ctx* ctx, const void* packed_u8, const void* scales_bf16,
+                              int vocab, int width, int group, int src_on_device,
+                              g4_ple_table** out) {
+    if (!out) return g4::set_error(G4_ERR_INVALID, "g4_ple_table_create: null out");
+    *out = nullptr;
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (vocab <= 0 || width <= 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_ple_table_create: bad geometry %d x %d", vocab, width);
+    if (group != 32 || width % 32 != 0)
+        return g4::set_error(G4_ERR_UNSUPPORTED,
+                             "g4_ple_table_create: group %d / width %d (group 32 and width %% 32 == 0 required)",
+                             group, width);
+    if ((packed_u8 == nullptr) != (scales_bf16 == nullptr))
+        return g4::set_error(G4_ERR_INVALID, "g4_ple_table_create: packed and scales must both be given or both NULL");
+    g4_ple_table* t = new g4_ple_table();
+    t->ctx = ctx;
+    t->vocab = vocab;
+    t->width = width;
+    t->group = group;
+    const size_t pbytes = (size_t)vocab * (width / 2), sbytes = (size_t)vocab * (width / group) * 2;
+    cudaError_t e = cudaMalloc(&t->packed, pbytes);
+    if (e == cudaSuccess) e = cudaMalloc(&t->scales, sbytes);
+    if (e != cudaSuccess) {
+        cudaFree(t->packed);
+        cudaFree(t->scales);
+        delete t;
+        return g4::cuda_error(e, "g4_ple_table_create: cudaMalloc");
+    }
+    if (packed_u8) {
+        st = copy_in(t->packed, packed_u8, pbytes, src_on_device, ctx->stream);
+        if (!st) st = copy_in(t->scales, scales_bf16, sbytes, src_on_device, ctx->stream);
+        if (!st && !src_on_device) {
+            cudaError_t se = cudaStreamSynchronize(ctx->stream);
+            if (se != cudaSuccess) st = g4::cuda_error(se, "g4_ple_table_create: sync");
+        }
+        if (st) {
+            g4_ple_table_destroy(t);
+            return st;
+        }
+    }
+    *out = t;
+    return G4_OK;
+}
+
+g4_status g4_ple_table_upload_rows(g4_ctx* ctx, g4_ple_table* tab, int row_start, int rows,
+                                   const void* packed_u8, const void* scales_bf16,
+                                   int src_on_device) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!tab || !packed_u8 || !scales_bf16)
+        return g4::set_error(G4_ERR_INVALID, "g4_ple_table_upload_rows: null argument");
+    if (row_start < 0 || rows < 0 || row_start + rows > tab->vocab)
+        return g4::set_error(G4_ERR_RANGE, "g4_ple_table_upload_rows: rows [%d, %d) outside vocab %d",
+                             row_start, row_start + rows, tab->vocab);
+    const size_t prow = tab->width / 2, srow = (size_t)(tab->width / tab->group) * 2;
+    st = copy_in(tab->packed + (size_t)row_start * prow, packed_u8, (size_t)rows * prow, src_on_device,
+                 ctx->stream);
+    if (st) return st;
+    st = copy_in(reinterpret_cast<uint8_t*>(tab->scales) + (size_t)row_start * srow, scales_bf16,
+                 (size_t)rows * srow, src_on_device, ctx->stream);
+    if (st) return st;
+    if (!src_on_device) G4_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+    return G4_OK;
+}
+
+g4_status g4_ple_table_destroy(g4_ple_table* tab) {
+    if (!tab) return G4_OK;
+    if (tab->ctx) cudaSetDevice(tab->ctx->device);
+    cudaFree(tab->packed);
+    cudaFree(tab->scales);
+    delete tab;
+    return G4_OK;
+}
+
+g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids, int T,
+                        int ids_on_device, void* out, g4_dtype out_dtype) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!tab) return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: null table");
+    if (T < 0) return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: T = %d", T);
+    if (T == 0) return G4_OK;
+    if (!ids || !out) return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: null ids/out");
+    if (out_dtype != G4_F32 && out_dtype != G4_BF16)
+        return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: out dtype %d", (int)out_dtype);
+    if (reinterpret_cast<uintptr_t>(out) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: out must be 16-byte aligned");
+    const int32_t* d_ids = ids;
+    if (!ids_on_device) {
+        // gpu-runtime.js:463-470: integer ids in [0, vocab) or throw
+        for (int t = 0; t < T; ++t)
+            if (ids[t] < 0 || ids[t] >= tab->vocab)
+                return g4::set_error(G4_ERR_RANGE, "PLE token id out of range: %d", ids[t]);
+        if (ctx->d_ids_cap < (size_t)T) {
+            G4_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+            cudaFree(ctx->d_ids);
+            ctx->d_ids = nullptr;
+            ctx->d_ids_cap = 0;
+            size_t cap = T < 4096 ? 4096 : (size_t)T;
+            G4_CHECK_CUDA(cudaMalloc(&ctx->d_ids, cap * sizeof(int32_t)));
+            ctx->d_ids_cap = cap;
+        }
+        G4_CHECK_CUDA(cudaMemcpyAsync(ctx->d_ids, ids, (size_t)T * sizeof(int32_t),
+                                      cudaMemcpyHostToDevice, ctx->stream));
+        d_ids = ctx->d_ids;
+    }
+    const int gpr = tab->width / 32;
+    const long long total = (long long)T * gpr;
+    const int threads = 256;
+    const long long blocks = (total + threads - 1) / threads;
+    if (blocks > 0x7fffffffLL) return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: T too large");
+    const uint4* p = reinterpret_cast<const uint4*>(tab->packed);
+    if (out_dtype == G4_BF16)
+        ple_gather_kernel<false><<<(unsigned)blocks, threads, 0, ctx->stream>>>(
+            p, tab->scales, d_ids, T, tab->vocab, gpr, out, ctx->d_err);
+    else
+        ple_gather_kernel<true><<<(unsigned)blocks, threads, 0, ctx->stream>>>(
+            p, tab->scales, d_ids, T, tab->vocab, gpr, out, ctx->d_err);
+    G4_CHECK_LAUNCH("ple_gather_kernel");
+    return G4_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,165 @@
+/*
+ * g4w4.h -- C ABI of libg4w4.so, the sm_100a (B200) W4A16 hot path of gemma4-js.
+ *
+ * This header is the drop-in boundary.  Each entry point replaces one operator of
+ * the reference's WebGPU runtime (custom-webgpu/gpu-runtime.js, "GPUOps") or of the
+ * TFJS reference it was validated against; the replaced interface is cited above
+ * each declaration as path:line inside the gemma4-js project.
+ *
+ * Conventions
+ *   - Every call returns g4_status (0 = OK, negative = error) and never throws.
+ *     g4_last_error_string() gives the message of the last failing call on the
+ *     calling host thread (the reference's `throw new Error(...)` text).
+ *   - All device work is asynchronous on the context's CUDA stream, in issue order
+ *     (the reference relies on WebGPU queue order the same way).
+ *   - Tensor arguments are plain device pointers unless a parameter says "host".
+ *     Output buffers are caller-allocated (the reference's ops allocate their
+ *     outputs; a JS shim keeps that by allocating from its own pool).
+ *   - bf16 = IEEE bfloat16 bits in a uint16_t; row-major everywhere.
+ *   - One context per GPU per host thread.
+ */
+#ifndef G4W4_H
+#define G4W4_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t g4_status;
+
+#define G4_OK 0
+#define G4_ERR_INVALID (-1)     /* bad shape / argument / state (reference: throw)   */
+#define G4_ERR_OOM (-2)         /* cudaMalloc failed                                  */
+#define G4_ERR_CUDA (-3)        /* CUDA runtime/driver error                          */
+#define G4_ERR_TIMEOUT (-4)     /* a bounded device-side wait gave up                 */
+#define G4_ERR_UNSUPPORTED (-5) /* valid for the reference, not implemented here      */
+#define G4_ERR_RANGE (-6)       /* index out of range (token id, KV capacity)         */
+#define G4_ERR_DEVICE (-7)      /* device-side check failed (bad id seen by a kernel) */
+
+typedef enum { G4_F32 = 0, G4_BF16 = 1 } g4_dtype;
+
+typedef struct g4_ctx g4_ctx;
+typedef struct g4_linear g4_linear;
+typedef struct g4_ple_table g4_ple_table;
+typedef struct g4_kv g4_kv;
+
+/* ---------------------------------------------------------------- context --
+ * Replaces the WebGPU device + queue the runtime is constructed with
+ * (custom-webgpu/gpu-runtime.js:1296 `new GPUOps(device)`).
+ * `stream` is a cudaStream_t (NULL = the legacy default stream). */
+g4_status g4_ctx_create(int device, void* stream, g4_ctx** out);
+g4_status g4_ctx_destroy(g4_ctx* ctx);
+g4_status g4_ctx_set_stream(g4_ctx* ctx, void* stream);
+/* Waits for all work issued on the context stream (reference: queue.onSubmittedWorkDone). */
+g4_status g4_stream_sync(g4_ctx* ctx);
+/* Reads and clears the device-side error word that kernels set when a bounded wait
+ * times out or a kernel sees an invalid index.  Synchronises the stream.
+ * *flags receives the raw bit set (0 = clean); the status is G4_ERR_TIMEOUT or
+ * G4_ERR_DEVICE when a bit was set. */
+g4_status g4_ctx_check_device(g4_ctx* ctx, uint32_t* flags);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* g4_last_error_string(void);
+/* Library version string. */
+const char* g4_version(void);
+/* Number of kernels this library has launched in this process (all contexts). */
+uint64_t g4_kernel_launch_count(void);
+
+/* ----------------------------------------------------------- W4A16 linear --
+ * g4_linear_create replaces GPUW4Linear.load (custom-webgpu/gpu-runtime.js:1385-1392),
+ * which uploads `{base}.weight_packed` I32 [N, K/8] and `{base}.weight_scale`
+ * BF16 [N, K/group] as raw bytes.  Same inputs and meaning: nibble j of word w of
+ * row n holds column 8w+j, value (nibble - 8) (official-w4a16.js:15-19, :84-96).
+ * The weights are copied (from host when src_on_device == 0) and re-laid out on
+ * the device for the kernels; the caller's buffers can be freed afterwards.
+ * group must be 32 (the compressed-tensors group size of the checkpoint);
+ * K must be a multiple of 32. */
+g4_status g4_linear_create(g4_ctx* ctx, const void* packed_i32, const void* scales_bf16,
+                           int K, int N, int group, int src_on_device, g4_linear** out);
+g4_status g4_linear_destroy(g4_linear* lin);
+/* K, N of a linear. */
+g4_status g4_linear_shape(const g4_linear* lin, int* K, int* N);
+
+/* y[M,N] = x[M,K] . dequant(W)^T.  Replaces GPUOps.w4 (custom-webgpu/gpu-runtime.js:1316-1324,
+ * W4_SHADER :1068-1102) and OfficialW4A16Linear.apply
+ * (browser-tfjs-webgl-distribution/runtime/official-quantized-linear.js:82-128).
+ * x bf16, FP32 accumulation, y in y_dtype (G4_BF16 or G4_F32).
+ * M <= 16 runs the split-K decode GEMV; larger M runs the tcgen05 GEMM.
+ * M = 0 is a no-op. */
+g4_status g4_linear_w4a16(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
+                          void* y, g4_dtype y_dtype);
+/* Forces one implementation (0 = auto, 1 = decode GEMV, 2 = tcgen05 GEMM) for tests
+ * and benchmarks.  The GEMV accepts any M (it runs M in slices of 16). */
+g4_status g4_linear_w4a16_impl(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
+                               void* y, g4_dtype y_dtype, int impl);
+
+/* Dequantises rows [row_start, row_start+row_count) of the weight into out
+ * [row_count, K]: f32 = (nibble-8) * f32(scale) exactly as dequantizeOfficialW4A16Rows
+ * (browser-tfjs-webgl-distribution/runtime/official-w4a16.js:50-101); G4_BF16 = the
+ * round-to-nearest-even of that value (roundFloat32ToBF16, official-w4a16.js:34-48).
+ * Reads the device layout, so it also proves the re-layout is lossless. */
+g4_status g4_linear_dequant(g4_ctx* ctx, const g4_linear* lin, int row_start, int row_count,
+                            void* out, g4_dtype out_dtype);
+
+/* ------------------------------------------------------------ PLE table --
+ * Replaces the shard bundle readers (custom-webgpu/gpu-runtime.js:487-527 local,
+ * :798-826 remote; LocalPleW4ShardReader ple-w4-shard-reader.js:65-104).
+ * packed: [vocab, width/2] bytes, low nibble = even column, two's complement
+ * nibble in [-8,7] (data range [-7,7]); scales: [vocab, width/group] bf16.
+ * These are the shard files' "packed block" and "scale block" with the shards of
+ * row_sharded_packed_then_scales concatenated in row order.  Copied to the device. */
+g4_status g4_ple_table_create(g4_ctx* ctx, const void* packed_u8, const void* scales_bf16,
+                              int vocab, int width, int group, int src_on_device,
+                              g4_ple_table** out);
+/* Adds rows [row_start, row_start+rows) of a table created with packed_u8 == NULL
+ * (one shard at a time, as the reference streams shards). */
+g4_status g4_ple_table_upload_rows(g4_ctx* ctx, g4_ple_table* tab, int row_start, int rows,
+                                   const void* packed_u8, const void* scales_bf16,
+                                   int src_on_device);
+g4_status g4_ple_table_destroy(g4_ple_table* tab);
+
+/* out[T, width] = dequant(table[ids[t]]).  Replaces reader.pleRowsToGpu(device, ids)
+ * (custom-webgpu/gpu-runtime.js:905, :993, :1050 -> _dequantRowsToGpu :265-335, WGSL :218-256).
+ * ids: int32 [T], on the host (ids_on_device == 0: validated on the host, throws
+ * "PLE token id out of range" like gpu-runtime.js:466-470) or on the device
+ * (out-of-range ids give zero rows and raise the device error flag).
+ * out_dtype G4_F32: bit-identical to q*scale (ple-w4-shard-reader.js:89-95);
+ * G4_BF16: bit-identical to round-to-nearest-even of that product. */
+g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids, int T,
+                        int ids_on_device, void* out, g4_dtype out_dtype);
+
+/* -------------------------------------------------------------- KV cache --
+ * Replaces KVCache (custom-webgpu/gemma4-webgpu.js:122-137): per-layer K and V
+ * [capacity, hd], here in bf16.  Positions are absolute: slot = position. */
+g4_status g4_kv_create(g4_ctx* ctx, int hd, int capacity, g4_kv** out);
+g4_status g4_kv_destroy(g4_kv* kv);
+/* Appends rows of K (post k-norm + RoPE) and V (post RMS) at start_pos, which must
+ * equal the cache length (gemma4-webgpu.js:128-135, same errors).  src_dtype is
+ * the dtype of k and v (f32 like the reference, or bf16); the cache stores bf16. */
+g4_status g4_kv_append(g4_ctx* ctx, g4_kv* kv, const void* k, const void* v, int rows,
+                       int start_pos, g4_dtype src_dtype);
+/* Cache length, hd and capacity. */
+g4_status g4_kv_info(const g4_kv* kv, int* length, int* hd, int* capacity);
+/* Resets the cache length to 0 (gemma4-webgpu.js:193-196 resetCache). */
+g4_status g4_kv_reset(g4_kv* kv);
+/* Device pointers of the K and V storage ([capacity, hd] bf16). */
+g4_status g4_kv_buffers(const g4_kv* kv, void** k, void** v);
+
+/* GQA attention of `rows` query rows against one KV head.  Replaces GPUOps.attention
+ * (custom-webgpu/gpu-runtime.js:1357-1365: QK_SHADER :1204-1221, SOFTMAX_SHADER
+ * :1223-1234, ATTN_OUT_SHADER :1236-1248) and scaledDotProductAttention
+ * (browser-tfjs-webgl-distribution/runtime/official-w4a16-layer0.js:30-62).
+ * q: bf16 [rows, heads, hd] (post q-norm + RoPE), out: bf16 [rows, heads, hd].
+ * Logit scale 1.0.  Query row r sits at position qpos0 + r and sees keys
+ * j < keylen with j <= qpos0 + r and, when sliding, j + window > qpos0 + r.
+ * Requires heads <= 8, hd in {64,128,256,512}, keylen <= cache length and
+ * qpos0 + rows <= keylen (every row then sees at least its own key). */
+g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
+                       int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* G4W4_H */

@@ -1,0 +1,94 @@
+"""W4A16 linear on the GPU through the C ABI: bit-exact dequant, GEMV / GEMM within 1e-2."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_round, golden, max_rel
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2  # max|y - ref| / max|ref|, BF16 out, FP32 accumulate
+
+
+def make_weights(oracle, K, N, seed, scale_sigma=0.02):
+    rng = np.random.default_rng(seed)
+    packed = rng.integers(0, 2**32, size=(N, K // 8), dtype=np.uint64).astype(np.uint32).view(np.int32)
+    scales = oracle.f32_to_bf16_bits(np.abs(rng.normal(0, scale_sigma, (N, K // 32))).astype(np.float32))
+    return packed, scales
+
+
+def test_golden_known_answers(rt, ctx):
+    g = golden("linear_w4_golden.npz")
+    lin = rt.W4Linear(ctx, g["packed"], g["scales"])
+    out = lin.dequant().cpu().numpy()
+    assert np.array_equal(out, g["expected_f32"])
+
+
+@pytest.mark.parametrize("K,N", [(32, 8), (96, 24), (256, 40), (1536, 6144), (6144, 1536), (256, 1536)])
+def test_dequant_bit_exact(rt, ctx, oracle, K, N):
+    packed, scales = make_weights(oracle, K, N, K + N)
+    lin = rt.W4Linear(ctx, packed, scales)
+    ref = oracle.dequant_w4a16_rows(packed, scales)
+    got = lin.dequant(dtype=torch.float32).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+    got16 = lin.dequant(dtype=torch.bfloat16).cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got16, oracle.f32_to_bf16_bits(ref))
+    r0 = N // 3
+    part = lin.dequant(r0, min(5, N - r0)).cpu().numpy()
+    assert np.array_equal(part, ref[r0:r0 + 5])
+
+
+def test_device_source_weights(rt, ctx, oracle):
+    packed, scales = make_weights(oracle, 128, 48, 3)
+    a = rt.W4Linear(ctx, packed, scales)
+    b = rt.W4Linear(ctx, torch.from_numpy(packed).cuda(), torch.from_numpy(scales.view(np.int16)).cuda())
+    assert torch.equal(a.dequant(), b.dequant())
+
+
+def _run(rt, ctx, ops, oracle, K, N, M, impl, seed, out_dtype=torch.bfloat16):
+    packed, scales = make_weights(oracle, K, N, seed)
+    lin = rt.W4Linear(ctx, packed, scales, name=f"w{K}x{N}")
+    rng = np.random.default_rng(seed + 1)
+    x = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    y = ops.w4(lin, xt, M, out_dtype=out_dtype, impl=impl).float().cpu().numpy()
+    ctx.check_device()
+    ref = oracle.linear_w4a16(x, packed, scales, nthreads=8)
+    return y, ref
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 7, 8, 9, 16])
+@pytest.mark.parametrize("K,N", [(1536, 6144), (6144, 1536), (96, 40), (256, 1536), (1536, 8960)])
+def test_gemv_matches_oracle(rt, ctx, ops, oracle, K, N, M):
+    y, ref = _run(rt, ctx, ops, oracle, K, N, M, impl=1, seed=K * 7 + N + M)
+    assert max_rel(y, ref) < TOL
+
+
+def test_gemv_large_m_slices(rt, ctx, ops, oracle):
+    y, ref = _run(rt, ctx, ops, oracle, 512, 256, 37, impl=1, seed=5)
+    assert max_rel(y, ref) < TOL
+
+
+def test_gemv_f32_output(rt, ctx, ops, oracle):
+    y, ref = _run(rt, ctx, ops, oracle, 1536, 6144, 4, impl=1, seed=11, out_dtype=torch.float32)
+    assert max_rel(y, ref) < 2e-3
+
+
+def test_config1_gemv(rt, ctx, ops, oracle):
+    """x [1,1536] ~ N(0,1) bf16, W int4 uniform, scales |N(0,0.02)|, N=6144, seed 0."""
+    y, ref = _run(rt, ctx, ops, oracle, 1536, 6144, 1, impl=1, seed=0)
+    assert max_rel(y, ref) < TOL
+    # the dot products use exact int4 x bf16 products: error comes from f32 sums only
+    assert max_rel(y, ref) < 4e-3
+
+
+def test_linear_errors(rt, ctx, ops, oracle, g4):
+    packed, scales = make_weights(oracle, 64, 16, 1)
+    lin = rt.W4Linear(ctx, packed, scales)
+    with pytest.raises(g4.G4Error):
+        ops.w4(lin, torch.zeros((2, 64), dtype=torch.float32, device="cuda"), 2)
+    with pytest.raises(g4.G4Error, match="expected"):
+        ops.w4(lin, torch.zeros((2, 60), dtype=torch.bfloat16, device="cuda"), 2)
+    with pytest.raises(g4.G4Error, match="only 32"):
+        rt.W4Linear(ctx, make_weights(oracle, 128, 16, 2)[0], np.zeros((16, 2), np.uint16))
+    assert ops.w4(lin, torch.zeros((0, 64), dtype=torch.bfloat16, device="cuda"), 0).shape == (0, 16)
