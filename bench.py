@@ -188,7 +188,7 @@ PLE_BYTES = 4096 * (4480 + 560) + 4096 * 4 + 4096 * 8960 * 2   # 94,060,544 B pe
 def run_ple(args, torch, rt, ctx, dist, peaks):
     lib = importlib.import_module("gemma4-js_b200._lib").load()
     K, W = args.steps, args.warmup
-    tab, ids, outs = ple_setup(torch, rt, ctx, K + W)
+    tab, ids, outs = ple_setup(torch, rt, ctx, K + W, vocab=args.vocab)
     T = 4096
 
     def launch(i):
@@ -209,7 +209,7 @@ def run_ple(args, torch, rt, ctx, dist, peaks):
     value = gbs * dist.world
 
     # e2e through the public API: pinned host ids -> device, gather, bf16 rows -> pinned host
-    hid = [torch.randint(0, 262144, (T,), dtype=torch.int32).pin_memory() for _ in range(2)]
+    hid = [torch.randint(0, args.vocab, (T,), dtype=torch.int32).pin_memory() for _ in range(2)]
     dev_ids = torch.empty(T, dtype=torch.int32, device="cuda")
     hout = torch.empty((T, 8960), dtype=torch.bfloat16).pin_memory()
     e2e_steps = max(3, min(K, 20))
@@ -237,7 +237,7 @@ def run_ple(args, torch, rt, ctx, dist, peaks):
         "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded int4 table, uniform ids)",
-        "config": {"workload": "config2_ple_gather", "tokens_per_step_per_gpu": T, "table": [262144, 8960],
+        "config": {"workload": "config2_ple_gather", "tokens_per_step_per_gpu": T, "table": [args.vocab, 8960],
                    "out": "bf16 [4096,35,256]",
                    "l2": "fresh random ids each step over a 1.32 GB table; 3 rotating 73 MB outputs (> 126 MB L2)"},
         "roofline": {"bound": "hbm", "kernel": "ple_gather_kernel", "achieved": round(gbs, 1), "peak": peak,
@@ -253,7 +253,7 @@ def run_ple(args, torch, rt, ctx, dist, peaks):
 def run_gemv(args, torch, rt, ctx, dist, peaks):
     lib = importlib.import_module("gemma4-js_b200._lib").load()
     K, W = args.steps, args.warmup
-    Kd, N, copies = 1536, 6144, 64
+    Kd, N, copies = 1536, 6144, args.copies or 64
     gen = torch.Generator(device="cuda").manual_seed(0)
     lins = []
     for c in range(copies):
@@ -295,7 +295,7 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
 def run_attn(args, torch, rt, ctx, dist, peaks):
     K, W = args.steps, args.warmup
     hd, keylen = 256, 4096
-    copies = 40  # 40 x 8 MB of K/V = 320 MB > L2
+    copies = args.copies or 40  # 40 x 8 MB of K/V = 320 MB > L2
     gen = torch.Generator(device="cuda").manual_seed(0)
     caches = []
     for c in range(copies):
@@ -405,6 +405,8 @@ def main():
     ap.add_argument("--workload", default="ple", choices=["ple", "gemv", "attn"])
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--vocab", type=int, default=262144, help="ple: table rows (smaller for ncu captures)")
+    ap.add_argument("--copies", type=int, default=0, help="gemv/attn: rotating weight / KV copies")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

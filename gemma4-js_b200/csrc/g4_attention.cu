@@ -238,26 +238,27 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     }
 }
 
-// Merges the split-KV partials of one query row (log-sum-exp weights).
+// Merges the split-KV partials (log-sum-exp weights).  One CTA per (row, head), one
+// thread per output column; the split loop is unrolled so its loads overlap.
 template <int HD>
-__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
-                                    int nsplit, int heads, uint16_t* __restrict__ out) {
-    const int r = blockIdx.x;
-    for (int idx = threadIdx.x; idx < heads * HD; idx += blockDim.x) {
-        const int h = idx / HD, d = idx - h * HD;
-        float m = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) m = fmaxf(m, part_ml[((size_t)r * nsplit + s) * 8 + h].x);
-        const float mu = m == -INFINITY ? 0.f : m;
-        float l = 0.f, acc = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-            const size_t pi = ((size_t)r * nsplit + s) * 8 + h;
-            const float2 ml = part_ml[pi];
-            const float f = exp2f(ml.x - mu);
-            l += f * ml.y;
-            acc += f * part_o[pi * HD + d];
-        }
-        out[((size_t)r * heads + h) * HD + d] = (uint16_t)f32_to_bf16_bits(acc / l);
+__global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restrict__ part_o,
+                                                          const float2* __restrict__ part_ml, int nsplit,
+                                                          int heads, uint16_t* __restrict__ out) {
+    const int r = blockIdx.x / heads, h = blockIdx.x - r * heads, d = threadIdx.x;
+    const float2* ml = part_ml + (size_t)r * nsplit * 8 + h;
+    const float* po = part_o + ((size_t)r * nsplit * 8 + h) * HD + d;
+    float m = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, __ldg(&ml[(size_t)s * 8].x));
+    const float mu = m == -INFINITY ? 0.f : m;
+    float l = 0.f, acc = 0.f;
+#pragma unroll 8
+    for (int s = 0; s < nsplit; ++s) {
+        const float2 v = __ldg(&ml[(size_t)s * 8]);
+        const float f = exp2f(v.x - mu);
+        l += f * v.y;
+        acc += f * __ldg(po + (size_t)s * 8 * HD);
     }
+    out[((size_t)r * heads + h) * HD + d] = (uint16_t)f32_to_bf16_bits(acc / l);
 }
 
 // Appends rows to the bf16 cache, rounding f32 input to nearest even.
@@ -314,7 +315,7 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     attn_decode_kernel<HD><<<dim3(nsplit, rows), C::THREADS, C::SMEM, ctx->stream>>>(km, vm, p);
     G4_CHECK_LAUNCH("attn_decode_kernel");
     if (nsplit > 1) {
-        attn_combine_kernel<HD><<<rows, 256, 0, ctx->stream>>>(p.part_o, p.part_ml, nsplit, heads, out);
+        attn_combine_kernel<HD><<<rows * heads, HD, 0, ctx->stream>>>(p.part_o, p.part_ml, nsplit, heads, out);
         G4_CHECK_LAUNCH("attn_combine_kernel");
     }
     return G4_OK;

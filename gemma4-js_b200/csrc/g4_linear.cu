@@ -112,109 +112,125 @@ __global__ void dequant_kernel(g4_linear_dev L, int row_start, int row_count, vo
     }
 }
 
-__device__ __forceinline__ uint4 ld_stream_u4(const uint4* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
+constexpr int kGemvWarps = 4;
+constexpr int kGemvPass = 32;  // 512-byte blocks staged per pass (16 KB of weights)
+
+// Shared-memory plan of one GEMV CTA: P = blocks staged per pass, M activation rows.
+//   [0,128) mbarrier | P*512 weight blocks | P*64 scale blocks | M rows of P*128+16 bytes
+// The cross-warp partials reuse the weight area once the last pass is consumed.
+__host__ __device__ constexpr int gemv_xstride(int P) { return P * 128 + 16; }  // +16: rows not bank-aliased
+__host__ __device__ constexpr int gemv_smem_bytes(int P, int M) {
+    return 128 + P * 576 + M * gemv_xstride(P) > 128 + 2 * 4 * 32 * 4 * 4 ? 128 + P * 576 + M * gemv_xstride(P)
+                                                                         : 128 + 2 * 4 * 32 * 4 * 4;
 }
 
-constexpr int kGemvWarps = 4;
-constexpr int kGemvUnroll = 4;
-
-// Split-K decode GEMV.  CTA (nt, s) owns rows 16*nt..+15 and the s-th slice of the
-// K chunks; its 4 warps interleave over the slice's 512-byte blocks.  Partial tiles
+// Split-K decode GEMV (M <= 16).  CTA (nt, s) owns the 16 weight rows of tile nt and
+// the s-th slice of their K blocks.  One thread stages the slice's weight blocks,
+// scales and activation rows into shared memory with bulk (TMA) copies on one
+// mbarrier; the 4 warps then run dequant + mma.m16n8k16 from shared memory.  Partials
 // are summed across warps in shared memory and across the S CTAs of the cluster
-// through distributed shared memory, so no global scratch and no atomics are used.
+// through distributed shared memory: no global scratch, no atomics.
 // kNB = number of 8-row activation tiles (1: M <= 8, 2: M <= 16).
 template <int kNB>
-__global__ void __launch_bounds__(kGemvWarps * 32, 4)
+__global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ldx,
-                  void* __restrict__ y, int ldy, int y_f32, int chunks_per_split) {
-    __shared__ float red[kGemvWarps][kNB * 4][32];
+                  void* __restrict__ y, int ldy, int y_f32, int chunks_per_split, uint32_t* err) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int P = min(chunks_per_split, kGemvPass);
+    const int xstride = gemv_xstride(P);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
+    uint8_t* wsm = sm + 128;
+    uint8_t* ssm = wsm + P * 512;
+    uint8_t* xsm = ssm + P * 64;
+    float* red = reinterpret_cast<float*>(wsm);  // [warps][kNB*4][32], after the last pass
+
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int nt = blockIdx.x;
-    const int split = blockIdx.y;
+    const int nt = blockIdx.x, split = blockIdx.y;
     const int c_begin = split * chunks_per_split;
     const int c_end = min(L.Kc, c_begin + chunks_per_split);
 
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
     float acc[kNB][4];
 #pragma unroll
-    for (int j = 0; j < kNB; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+    for (int j = 0; j < kNB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
 
-    const uint4* wbase = L.wfrag + (size_t)nt * L.Kc * 32 + lane;
-    const uint2* sbase = L.sfrag + (size_t)nt * L.Kc * 8 + g;
-
-    for (int c0 = c_begin + warp; c0 < c_end; c0 += kGemvWarps * kGemvUnroll) {
-        uint4 wv[kGemvUnroll];
-        uint2 sv[kGemvUnroll];
-        uint4 xv[kGemvUnroll][kNB][2];
-        // ---- issue every load of up to kGemvUnroll chunks before any math ----
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            const int c = c0 + u * kGemvWarps;
-            const bool cv = c < c_end;
-            wv[u] = cv ? ld_stream_u4(wbase + (size_t)c * 32) : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
-            sv[u] = cv ? __ldg(sbase + (size_t)c * 8) : make_uint2(0, 0);
-#pragma unroll
-            for (int j = 0; j < kNB; ++j) {
-                const int b = j * 8 + g;
+    bool ok = true;
+    uint32_t phase = 0;
+    for (int p0 = c_begin; p0 < c_end && ok; p0 += kGemvPass, phase ^= 1) {
+        const int nch = min(kGemvPass, c_end - p0);
+        const int k0 = p0 * 64;
+        const int klen = min(L.K, (p0 + nch) * 64) - k0;  // valid activation columns
+        if (threadIdx.x == 0) {
+            const uint32_t bytes = nch * 512 + nch * 64 + M * klen * 2;
+            mbar_arrive_expect_tx(bar, bytes);
+            const size_t blk = (size_t)nt * L.Kc + p0;
+            bulk_load(wsm, L.wfrag + blk * 32, nch * 512, bar);
+            bulk_load(ssm, L.sfrag + blk * 8, nch * 64, bar);
+            for (int b = 0; b < M; ++b)
+                bulk_load(xsm + b * xstride, x + (size_t)b * ldx + k0, klen * 2, bar);
+        }
+        // Zero the activation tail past K inside the last block (K % 64 == 32).
+        if (klen < nch * 64)
+            for (int i = threadIdx.x; i < M * 32; i += blockDim.x)
+                reinterpret_cast<uint16_t*>(xsm + (i >> 5) * xstride)[klen + (i & 31)] = 0;
+        ok = mbar_wait(bar, phase, err);
+        __syncthreads();
+        if (ok) {
+            for (int c = warp; c < nch; c += kGemvWarps) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wsm + c * 512 + lane * 16);
+                const uint2 sv = *reinterpret_cast<const uint2*>(ssm + c * 64 + g * 8);
+                const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
                 for (int G = 0; G < 2; ++G) {
-                    const int k = c * 64 + G * 32 + t * 8;
-                    xv[u][j][G] = (cv && b < M && k < L.K)
-                                      ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)b * ldx + k))
-                                      : make_uint4(0, 0, 0, 0);
+                    const uint32_t w0 = wq[2 * G], w1 = wq[2 * G + 1];
+                    const uint32_t a0[4] = {int4pair_to_bf16x2(w0), int4pair_to_bf16x2(w1),
+                                            int4pair_to_bf16x2(w0 >> 4), int4pair_to_bf16x2(w1 >> 4)};
+                    const uint32_t a1[4] = {int4pair_to_bf16x2(w0 >> 8), int4pair_to_bf16x2(w1 >> 8),
+                                            int4pair_to_bf16x2(w0 >> 12), int4pair_to_bf16x2(w1 >> 12)};
+                    const uint32_t sw = G ? sv.y : sv.x;
+                    const float s_lo = bf16_bits_to_f32(sw & 0xFFFFu), s_hi = bf16_bits_to_f32(sw >> 16);
+#pragma unroll
+                    for (int j = 0; j < kNB; ++j) {
+                        const int b = j * 8 + g;
+                        uint4 xg = make_uint4(0, 0, 0, 0);
+                        if (b < M)
+                            xg = *reinterpret_cast<const uint4*>(xsm + b * xstride +
+                                                                 (c * 64 + G * 32 + t * 8) * 2);
+                        const uint32_t b0[2] = {xg.x, xg.y}, b1[2] = {xg.z, xg.w};
+                        float d[4];
+                        const float z[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma_bf16_16816(d, a0, b0, z);
+                        mma_bf16_16816(d, a1, b1, d);
+                        acc[j][0] = fmaf(s_lo, d[0], acc[j][0]);
+                        acc[j][1] = fmaf(s_lo, d[1], acc[j][1]);
+                        acc[j][2] = fmaf(s_hi, d[2], acc[j][2]);
+                        acc[j][3] = fmaf(s_hi, d[3], acc[j][3]);
+                    }
                 }
             }
         }
-        // ---- dequant + tensor-core dot per 32-column group ----
-#pragma unroll
-        for (int u = 0; u < kGemvUnroll; ++u) {
-            const uint32_t wq[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-#pragma unroll
-            for (int G = 0; G < 2; ++G) {
-                const uint32_t w0 = wq[2 * G], w1 = wq[2 * G + 1];
-                const uint32_t a0[4] = {int4pair_to_bf16x2(w0), int4pair_to_bf16x2(w1),
-                                        int4pair_to_bf16x2(w0 >> 4), int4pair_to_bf16x2(w1 >> 4)};
-                const uint32_t a1[4] = {int4pair_to_bf16x2(w0 >> 8), int4pair_to_bf16x2(w1 >> 8),
-                                        int4pair_to_bf16x2(w0 >> 12), int4pair_to_bf16x2(w1 >> 12)};
-                const uint32_t sw = G ? sv[u].y : sv[u].x;
-                const float s_lo = bf16_bits_to_f32(sw & 0xFFFFu), s_hi = bf16_bits_to_f32(sw >> 16);
-#pragma unroll
-                for (int j = 0; j < kNB; ++j) {
-                    const uint4 xg = xv[u][j][G];
-                    const uint32_t b0[2] = {xg.x, xg.y}, b1[2] = {xg.z, xg.w};
-                    float d[4];
-                    const float z[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma_bf16_16816(d, a0, b0, z);
-                    mma_bf16_16816(d, a1, b1, d);
-                    acc[j][0] = fmaf(s_lo, d[0], acc[j][0]);
-                    acc[j][1] = fmaf(s_lo, d[1], acc[j][1]);
-                    acc[j][2] = fmaf(s_hi, d[2], acc[j][2]);
-                    acc[j][3] = fmaf(s_hi, d[3], acc[j][3]);
-                }
-            }
-        }
+        __syncthreads();  // the buffers are refilled by the next pass
     }
 
-    // ---- reduce the 4 warps of the CTA ----
+    // ---- reduce the warps of the CTA ----
 #pragma unroll
     for (int j = 0; j < kNB; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[warp][j * 4 + e][lane] = acc[j][e];
+        for (int e = 0; e < 4; ++e) red[(warp * kNB * 4 + j * 4 + e) * 32 + lane] = acc[j][e];
     __syncthreads();
     if (warp == 0) {
 #pragma unroll
         for (int q = 0; q < kNB * 4; ++q) {
-            float s = red[0][q][lane];
+            float s = red[q * 32 + lane];
 #pragma unroll
-            for (int w2 = 1; w2 < kGemvWarps; ++w2) s += red[w2][q][lane];
-            red[0][q][lane] = s;
+            for (int w2 = 1; w2 < kGemvWarps; ++w2) s += red[(w2 * kNB * 4 + q) * 32 + lane];
+            red[q * 32 + lane] = s;
         }
     }
     // ---- reduce the S CTAs of the cluster through distributed shared memory ----
@@ -225,15 +241,13 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         if (split == 0 && warp == 0) {
 #pragma unroll
             for (int q = 0; q < kNB * 4; ++q) {
-                float s = red[0][q][lane];
-                for (int r = 1; r < S; ++r) s += cluster.map_shared_rank(&red[0][q][lane], r)[0];
-                red[0][q][lane] = s;
+                float s = red[q * 32 + lane];
+                for (int r = 1; r < S; ++r) s += cluster.map_shared_rank(&red[q * 32 + lane], r)[0];
+                red[q * 32 + lane] = s;
             }
         }
         cluster.sync();
         if (split != 0) return;
-    } else {
-        __syncthreads();
     }
     if (warp != 0) return;
 #pragma unroll
@@ -243,7 +257,7 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
             const int row = nt * 16 + g + ((e & 2) ? 8 : 0);
             const int b = j * 8 + 2 * t + (e & 1);
             if (row < L.N && b < M) {
-                const float v = red[0][j * 4 + e][lane];
+                const float v = red[(j * 4 + e) * 32 + lane];
                 if (y_f32)
                     reinterpret_cast<float*>(y)[(size_t)b * ldy + row] = v;
                 else
@@ -260,16 +274,26 @@ namespace g4 {
 g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y,
                       int y_f32) {
     const g4_linear_dev& L = lin->dev;
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           gemv_smem_bytes(kGemvPass, 8)));
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           gemv_smem_bytes(kGemvPass, 16)));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    // Split K over a cluster until there are ~2 CTAs per SM, keeping >= 4 blocks per CTA.
+    int S = 1;
+    while (S < 8 && ((L.NT * S < 2 * ctx->num_sms && (L.Kc + 2 * S - 1) / (2 * S) >= 4) ||
+                     (L.Kc + S - 1) / S > kGemvPass))
+        S *= 2;
+    const int cps = (L.Kc + S - 1) / S;
     for (int m0 = 0; m0 < M; m0 += 16) {
         const int mm = (M - m0) < 16 ? (M - m0) : 16;
-        int S = 1;
-        const int target = ctx->num_sms * 4;
-        while (L.NT * S < target && S < 8 && L.Kc >= 2 * S * kGemvWarps) S *= 2;
-        const int cps = (L.Kc + S - 1) / S;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(L.NT, S, 1);
         cfg.blockDim = dim3(kGemvWarps * 32, 1, 1);
-        cfg.dynamicSmemBytes = 0;
+        cfg.dynamicSmemBytes = gemv_smem_bytes(cps < kGemvPass ? cps : kGemvPass, mm);
         cfg.stream = ctx->stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -283,9 +307,9 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
                          : (void*)(reinterpret_cast<uint16_t*>(y) + (size_t)m0 * L.N);
         cudaError_t e;
         if (mm <= 8)
-            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<1>, L, xs, mm, L.K, ys, L.N, y_f32, cps);
+            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<1>, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
         else
-            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<2>, L, xs, mm, L.K, ys, L.N, y_f32, cps);
+            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<2>, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
         if (e != cudaSuccess) return cuda_error(e, "gemv_w4a16_kernel");
         count_launch();
     }
