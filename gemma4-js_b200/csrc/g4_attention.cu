@@ -239,26 +239,57 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 }
 
 // Merges the split-KV partials (log-sum-exp weights).  One CTA per (row, head), one
-// thread per output column; the split loop is unrolled so its loads overlap.
+// thread per output column.  The per-split (m, l) pairs are read once, in parallel,
+// into shared memory; the column loop then issues its loads independently.
+constexpr int kMaxSplits = 1024;
+
 template <int HD>
 __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restrict__ part_o,
                                                           const float2* __restrict__ part_ml, int nsplit,
                                                           int heads, uint16_t* __restrict__ out) {
+    __shared__ float s_w[kMaxSplits];
+    __shared__ float s_red[HD / 32];
     const int r = blockIdx.x / heads, h = blockIdx.x - r * heads, d = threadIdx.x;
     const float2* ml = part_ml + (size_t)r * nsplit * 8 + h;
-    const float* po = part_o + ((size_t)r * nsplit * 8 + h) * HD + d;
-    float m = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) m = fmaxf(m, __ldg(&ml[(size_t)s * 8].x));
-    const float mu = m == -INFINITY ? 0.f : m;
-    float l = 0.f, acc = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < nsplit; ++s) {
-        const float2 v = __ldg(&ml[(size_t)s * 8]);
-        const float f = exp2f(v.x - mu);
-        l += f * v.y;
-        acc += f * __ldg(po + (size_t)s * 8 * HD);
+    float mloc = -INFINITY;
+    for (int s = d; s < nsplit; s += HD) {
+        const float m = __ldg(&ml[(size_t)s * 8].x);
+        s_w[s] = m;
+        mloc = fmaxf(mloc, m);
     }
-    out[((size_t)r * heads + h) * HD + d] = (uint16_t)f32_to_bf16_bits(acc / l);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
+    if ((d & 31) == 0) s_red[d >> 5] = mloc;
+    __syncthreads();
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) m = fmaxf(m, s_red[i]);
+    const float mu = m == -INFINITY ? 0.f : m;
+    __syncthreads();
+    float lloc = 0.f;
+    for (int s = d; s < nsplit; s += HD) {
+        const float f = exp2f(s_w[s] - mu);
+        lloc += f * __ldg(&ml[(size_t)s * 8].y);
+        s_w[s] = f;
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lloc += __shfl_xor_sync(0xffffffffu, lloc, off);
+    if ((d & 31) == 0) s_red[d >> 5] = lloc;
+    __syncthreads();
+    float l = 0.f;
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) l += s_red[i];
+    const float* po = part_o + ((size_t)r * nsplit * 8 + h) * HD + d;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= nsplit; s += 4) {
+        acc0 += s_w[s] * __ldg(po + (size_t)s * 8 * HD);
+        acc1 += s_w[s + 1] * __ldg(po + (size_t)(s + 1) * 8 * HD);
+        acc2 += s_w[s + 2] * __ldg(po + (size_t)(s + 2) * 8 * HD);
+        acc3 += s_w[s + 3] * __ldg(po + (size_t)(s + 3) * 8 * HD);
+    }
+    for (; s < nsplit; ++s) acc0 += s_w[s] * __ldg(po + (size_t)s * 8 * HD);
+    out[((size_t)r * heads + h) * HD + d] = (uint16_t)f32_to_bf16_bits(((acc0 + acc1) + (acc2 + acc3)) / l);
 }
 
 // Appends rows to the bf16 cache, rounding f32 input to nearest even.
@@ -286,6 +317,7 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     const int tiles_per_split = (ntiles + nsplit - 1) / nsplit;
     nsplit = (ntiles + tiles_per_split - 1) / tiles_per_split;
     if (nsplit < 1) nsplit = 1;
+    if (nsplit > kMaxSplits) return g4::set_error(G4_ERR_UNSUPPORTED, "attention: %d key splits", nsplit);
 
     AttnParams p{};
     p.q = q;
