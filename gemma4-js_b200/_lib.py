@@ -65,6 +65,7 @@ SIGNATURES = {
     "g4_kv_reset": (_S, [_P]),
     "g4_kv_buffers": (_S, [_P, _PP, _PP]),
     "g4_attention": (_S, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "g4_attention_noalloc": (_S, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
 }
 
 _lib = None

@@ -10,6 +10,8 @@
 // (split-KV) and merged by a small combine kernel through a scratch buffer.
 #include <stdio.h>
 
+#include <mutex>
+
 #include "g4_attention.cuh"
 #include "g4_common.cuh"
 
@@ -304,7 +306,7 @@ __global__ void kv_append_f32_kernel(const float* __restrict__ k, const float* _
 template <int HD>
 g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& vm, const uint16_t* q,
                         int rows, int heads, int keylen, int qpos0, int sliding, int window, uint16_t* out,
-                        int kv_row0) {
+                        int kv_row0, void* fixed_scratch = nullptr, size_t fixed_bytes = 0) {
     using C = AttnCfg<HD>;
     // Longest key range of any row decides the split.
     const int qp_last = qpos0 + rows - 1;
@@ -334,10 +336,20 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     if (nsplit > 1) {
         const size_t ob = (size_t)rows * nsplit * 8 * HD * sizeof(float);
         const size_t mb = (size_t)rows * nsplit * 8 * sizeof(float2);
-        g4_status st = g4::ensure_workspace(ctx, ob + mb + 256);
-        if (st) return st;
-        p.part_o = static_cast<float*>(ctx->ws);
-        p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(ctx->ws) + ((ob + 255) & ~size_t(255)));
+        void* scratch = fixed_scratch;
+        if (scratch) {
+            if (ob + mb + 256 > fixed_bytes)
+                return g4::set_error(G4_ERR_RANGE,
+                                     "attention: %d rows x %d key splits need %zu bytes of scratch; the static "
+                                     "scratch of g4_attention_noalloc holds %zu bytes",
+                                     rows, nsplit, ob + mb + 256, fixed_bytes);
+        } else {
+            g4_status st = g4::ensure_workspace(ctx, ob + mb + 256);
+            if (st) return st;
+            scratch = ctx->ws;
+        }
+        p.part_o = static_cast<float*>(scratch);
+        p.part_ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + ((ob + 255) & ~size_t(255)));
     }
     static std::atomic<uint64_t> attr_set{0};
     if (!(attr_set.load() & (1ull << ctx->device))) {
@@ -368,12 +380,13 @@ g4_status make_kv_maps(g4_kv* kv) {
 }
 
 g4_status launch_attention(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows, int heads,
-                           int keylen, int qpos0, int sliding, int window, uint16_t* out) {
+                           int keylen, int qpos0, int sliding, int window, uint16_t* out, void* fixed_scratch,
+                           size_t fixed_bytes) {
     switch (kv->hd) {
-        case 64: return launch_attn_t<64>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
-        case 128: return launch_attn_t<128>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
-        case 256: return launch_attn_t<256>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
-        case 512: return launch_attn_t<512>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0);
+        case 64: return launch_attn_t<64>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
+        case 128: return launch_attn_t<128>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
+        case 256: return launch_attn_t<256>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
+        case 512: return launch_attn_t<512>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
         default: return set_error(G4_ERR_UNSUPPORTED, "attention: head dim %d (64/128/256/512 supported)", kv->hd);
     }
 }
@@ -497,4 +510,66 @@ g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int row
                                 sliding ? 1 : 0, window, static_cast<uint16_t*>(out_bf16));
 }
 
+
 }  // extern "C"
+
+// ------------------------------------------------ attention without allocation --
+//
+// Some callers cannot let a library call cudaMalloc: hosts that hand every byte of
+// device memory to their own pool at start-up (as a WebGPU-style runtime does), and
+// serving loops where cudaMalloc's implicit device-wide synchronisation would stall
+// the other streams.  g4_attention grows a context workspace with cudaMalloc when a
+// long key range is split across CTAs; g4_attention_noalloc instead keeps the split
+// partials in the fixed array below, which every GPU that loads this library holds
+// (8 MiB) until the process exits.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;
+__device__ __align__(256) uint8_t g_attn_noalloc_scratch[kNoAllocScratchBytes];
+
+// In host code g_attn_noalloc_scratch names a host-side shadow, not device memory, so
+// its device address is looked up once per device (with that device current) and cached.
+g4_status noalloc_scratch(int device, void** out) {
+    static std::mutex mu;
+    static void* ptrs[64] = {};
+    if (device < 0 || device >= 64) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: device %d", device);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+        if (e != cudaSuccess) return g4::cuda_error(e, "g4_attention_noalloc: cudaGetSymbolAddress");
+        ptrs[device] = p;
+    }
+    *out = ptrs[device];
+    return G4_OK;
+}
+
+}  // namespace
+
+extern "C" g4_status g4_attention_noalloc(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
+                                          int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!kv || !q_bf16 || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: null argument");
+    if (rows < 0) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: rows %d", rows);
+    if (rows == 0) return G4_OK;
+    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: hd %d != cache hd %d", hd, kv->hd);
+    if (heads < 1 || heads > 8)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_attention_noalloc: %d heads per KV head (1..8 supported)", heads);
+    if (keylen < 1 || keylen > kv->length)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: keylen %d outside cache length %d", keylen,
+                             kv->length);
+    if (qpos0 < 0 || qpos0 + rows > keylen)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: query positions [%d,%d) not below keylen %d",
+                             qpos0, qpos0 + rows, keylen);
+    if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: window %d", window);
+    if (reinterpret_cast<uintptr_t>(q_bf16) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: q must be 16-byte aligned");
+    void* scratch = nullptr;
+    st = noalloc_scratch(ctx->device, &scratch);
+    if (st) return st;
+    return g4::launch_attention(ctx, kv, 0, static_cast<const uint16_t*>(q_bf16), rows, heads, keylen, qpos0,
+                                sliding ? 1 : 0, window, static_cast<uint16_t*>(out_bf16), scratch,
+                                kNoAllocScratchBytes);
+}

@@ -159,6 +159,25 @@ g4_status g4_kv_buffers(const g4_kv* kv, void** k, void** v);
 g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
                        int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16);
 
+/* g4_attention for callers that cannot allocate device memory.  No counterpart in the
+ * reference: its WebGPU runtime allocates a buffer for every op.  g4_attention splits a
+ * long key range across CTAs and keeps the partial results in a context workspace that
+ * it grows with cudaMalloc; callers whose device memory is all handed to their own pool,
+ * or whose serving loop cannot absorb cudaMalloc's implicit device synchronisation, use
+ * this entry point instead.  Same arguments, same checks, same result.
+ *   - It allocates nothing: the partials go to one fixed 8 MiB device array compiled
+ *     into the library, which every GPU that loads the library keeps until exit.
+ *   - A split that needs more than 8 MiB (rows x key splits x 8 heads x (hd+2) x 4 B)
+ *     is rejected with G4_ERR_RANGE and a message giving both sizes.  Single-row decode
+ *     fits at every key length and head dim.
+ *   - The first call on a device looks up the array's device address (with that device
+ *     current), so make that first call before any stream capture.
+ *   - Every call, on every context and stream of a device, shares the one array and
+ *     overwrites it; calls that overlap on the GPU race.  Nothing in it needs to start
+ *     at zero: each call writes every partial it reads. */
+g4_status g4_attention_noalloc(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
+                               int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16);
+
 #ifdef __cplusplus
 }
 #endif
