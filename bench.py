@@ -333,6 +333,67 @@ def run_attn(args, torch, rt, ctx, dist, peaks):
     }
 
 
+def run_gemm(args, torch, rt, ctx, dist, peaks):
+    """M in {16,128,512,2048} x (K,N) in {(1536,6144), (6144,1536), (1536,262144)}."""
+    lib = importlib.import_module("gemma4-js_b200._lib").load()
+    K_steps, W = args.steps, args.warmup
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    points, clk = [], ClockSampler(dist.local)
+    n0 = rt.launch_count()
+    clk.start()
+    tot_flop, tot_s = 0.0, 0.0
+    for (Kd, N) in [(1536, 6144), (6144, 1536), (1536, 262144)]:
+        wbytes = N * Kd // 2 + N * Kd // 16
+        copies = max(1, min(32, (256 << 20) // wbytes + 1))   # > 126 MB of weights per rotation
+        lins = []
+        for c in range(copies):
+            packed = torch.randint(-2**31, 2**31 - 1, (N, Kd // 8), device="cuda", dtype=torch.int32, generator=gen)
+            sc = torch.randn((N, Kd // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+            lins.append(rt.W4Linear(ctx, packed, sc))
+            del packed, sc
+        for M in (16, 128, 512, 2048):
+            x = torch.randn((M, Kd), device="cuda", generator=gen).to(torch.bfloat16)
+            y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+
+            def launch(i, M=M, x=x, y=y):
+                st = lib.g4_linear_w4a16(ctx.handle, lins[i % copies].handle, C.c_void_p(x.data_ptr()), M,
+                                         C.c_void_p(y.data_ptr()), 1)
+                if st:
+                    raise RuntimeError(lib.g4_last_error_string())
+
+            steps = max(3, min(K_steps, 20 if N > 100000 else K_steps))
+            ms = time_graph(torch, ctx, launch, steps, W, dist)
+            per = ms / 1e3 / steps
+            flop = 2.0 * M * Kd * N
+            byts = wbytes + 2 * M * Kd + 2 * M * N
+            ideal = max(flop / (peaks["bf16_tflops"] * 1e12), byts / (peaks["hbm_gbs"] * 1e9))
+            points.append({"M": M, "K": Kd, "N": N, "us": round(per * 1e6, 2), "tflops": round(flop / per / 1e12, 1),
+                           "gbs": round(byts / per / 1e9, 1), "frac_of_roofline": round(ideal / per, 3),
+                           "kernel": "gemv" if M <= 16 else "tcgen05"})
+            if M >= 512:
+                tot_flop += flop
+                tot_s += per
+            del x, y
+        del lins
+        torch.cuda.empty_cache()
+    clocks = clk.stop()
+    ctx.check_device()
+    tf = tot_flop / tot_s / 1e12
+    peak = peaks["bf16_tflops"]
+    best = max((p for p in points if p["M"] >= 512), key=lambda p: p["tflops"])
+    return {
+        "metric": "W4A16 prefill GEMM TFLOP/s (config 3, M >= 512 aggregate)", "value": round(tf * dist.world, 2),
+        "unit": "TFLOP/s", "n_gpus": dist.world, "steps": K_steps, "warmup": W,
+        "ms_per_step": round(tot_s * 1e3, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "config3_gemm_sweep", "l2": "rotating weight copies (> 256 MB per rotation)"},
+        "roofline": {"bound": "tensor", "kernel": "gemm_w4a16_tcgen05_kernel", "achieved": round(best["tflops"], 1),
+                     "peak": peak, "unit": "TFLOP/s", "frac": round(best["tflops"] / peak, 4),
+                     "peak_source": peaks["source"], "traffic": None, "point": best},
+        "sweep": points, "gpu_launches": rt.launch_count() - n0, "clocks": clocks,
+    }
+
+
 # ------------------------------------------------------------ CPU baseline --
 def native_oracle():
     """The oracle's C restatement built for this host's CPU (-march=native)."""
@@ -402,7 +463,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ple", choices=["ple", "gemv", "attn"])
+    ap.add_argument("--workload", default="ple", choices=["ple", "gemv", "attn", "gemm"])
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--vocab", type=int, default=262144, help="ple: table rows (smaller for ncu captures)")
@@ -421,7 +482,7 @@ def main():
     rt = importlib.import_module("gemma4-js_b200.runtime")
     ctx = rt.Context(dist.local)
     peaks = load_peaks()
-    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn}[args.workload]
+    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn, "gemm": run_gemm}[args.workload]
     line = fn(args, torch, rt, ctx, dist, peaks)
     if dist.rank == 0:
         print(json.dumps(line), flush=True)

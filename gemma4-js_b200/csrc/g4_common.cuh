@@ -79,8 +79,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2_bits(float lo, float hi) {
 }
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
 
-// Bounded spin budget for every wait on a flag or mbarrier (about 1-2 s).
-constexpr uint32_t kSpinLimit = 1u << 26;
+// Bounded spin budget for every wait on a flag or mbarrier (4M polls: well under a
+// few seconds even when every poll suspends; normal waits take microseconds).
+constexpr uint32_t kSpinLimit = 1u << 22;
 
 __device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bit) {
     if (err) atomicOr(err, bit);
@@ -125,6 +126,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
         if (mbar_try_wait(bar, parity)) return true;
     raise_error(err, G4_DEVERR_TIMEOUT);
     return false;
+}
+
+// Warp-uniform variant: every lane of the warp gets the same answer.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* err) {
+    const bool ok = mbar_wait(bar, parity, err);
+    return __all_sync(0xffffffffu, ok);
 }
 
 // ---- TMA / bulk copies ----

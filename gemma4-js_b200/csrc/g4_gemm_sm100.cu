@@ -1,9 +1,331 @@
-// g4_gemm_sm100.cu -- tcgen05 prefill GEMM (placeholder until the kernel lands).
+// g4_gemm_sm100.cu -- W4A16 prefill GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Y[M, N] = X[M, K] . dequant(W)[N, K]^T, X bf16, FP32 accumulation in TMEM, Y bf16/f32.
+// Replaces GPUOps.w4 for many rows (custom-webgpu/gpu-runtime.js:1316-1324; the
+// reference runs one WGSL thread per output over all of K, W4_SHADER :1068-1102).
+//
+// One CTA computes a 128 x 256 tile of Y:
+//   warp 0      TMA producer: X tile [128 x 64] (128B swizzle, the UMMA K-major
+//               canonical layout) + the tile's 16 int4 weight blocks (16 x 512 B)
+//               + their scales (16 x 64 B) into a 4-stage ring.
+//   warp 1      TMEM allocator and MMA issuer: one thread issues tcgen05.mma
+//               (M = 128, N = 256, K = 16) x 4 per 64-column step into a 256-column
+//               FP32 accumulator in TMEM, and tcgen05.commit frees the stages.
+//   warps 2..9  dequant producers: int4 -> bf16 (exact q, times the bf16 scale with one
+//               rounding: the compressed-tensors bf16 materialisation, roundFloat32ToBF16
+//               of q*s, official-w4a16.js:34-48, :95) written straight into the swizzled
+//               K-major B operand, 2 stages; then the epilogue: tcgen05.ld of their TMEM
+//               lane quarter, convert, store.
+// Every wait is bounded; a timeout raises the context's device error word and the
+// kernel winds down (TMEM is always freed).
+#include <stdio.h>
+
 #include "g4_linear.cuh"
 
-namespace g4 {
-bool gemm_supported(const g4_linear*, int) { return false; }
-g4_status launch_gemm(g4_ctx*, const g4_linear*, const uint16_t*, int, void*, int) {
-    return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM not built");
+namespace {
+
+using namespace g4dev;
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int kStages = 4;      // X + raw weight ring
+constexpr int kBStages = 2;     // dequantised B ring
+constexpr int kDqWarps = 8;
+constexpr int kThreads = (2 + kDqWarps) * 32;
+constexpr int kABytes = BM * BK * 2;           // 16 KB
+constexpr int kRawBytes = (BN / 16) * 512;      // 8 KB
+constexpr int kScBytes = (BN / 16) * 64;        // 1 KB
+constexpr int kBBytes = BN * BK * 2;            // 32 KB
+constexpr int kTmemCols = 256;
+// [A stages][B stages][raw stages][scale stages][barriers]
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kABytes;
+constexpr int kOffRaw = kOffB + kBStages * kBBytes;
+constexpr int kOffSc = kOffRaw + kStages * kRawBytes;
+constexpr int kOffBar = kOffSc + kStages * kScBytes;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + alignment slack
+
+// ---- tcgen05 wrappers ----
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
 }
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// 32 lanes x 32 consecutive columns of 32-bit data.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);       // start address
+    d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
+    d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
+    d |= (uint64_t)2 << 61;                         // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor: D f32, A = B = bf16, both K-major, M = 128, N = 256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+struct GemmParams {
+    void* y;
+    int M, N, K, ldy, y_f32, ktiles;
+    uint32_t* err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                          const __grid_constant__ CUtensorMap smap, GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* load_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* load_empty = load_full + kStages;
+    uint64_t* b_full = load_empty + kStages;
+    uint64_t* b_empty = b_full + kBStages;
+    uint64_t* acc_full = b_empty + kBStages;
+    uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mb = blockIdx.x, nb = blockIdx.y;
+    const int KT = p.ktiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&load_full[s], 1);
+            mbar_init(&load_empty[s], 1 + kDqWarps);
+        }
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(&b_full[s], kDqWarps);
+            mbar_init(&b_empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_base_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_base_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tensor_map(&xmap);
+            prefetch_tensor_map(&wmap);
+            prefetch_tensor_map(&smap);
+            int issued = 0;
+            for (int kt = 0; kt < KT; ++kt) {
+                const int s = kt % kStages;
+                if (kt >= kStages && !mbar_wait(&load_empty[s], ((kt / kStages) - 1) & 1, p.err)) break;
+                mbar_arrive_expect_tx(&load_full[s], kABytes + kRawBytes + kScBytes);
+                tma_load_2d(smem + kOffA + s * kABytes, &xmap, &load_full[s], kt * BK, mb * BM);
+                tma_load_2d(smem + kOffRaw + s * kRawBytes, &wmap, &load_full[s], kt * 128, nb * (BN / 16));
+                tma_load_2d(smem + kOffSc + s * kScBytes, &smap, &load_full[s], kt * 16, nb * (BN / 16));
+                issued = kt + 1;
+            }
+            // Drain: our copies must land before the CTA can exit.
+            for (int kt = issued > kStages ? issued - kStages : 0; kt < issued; ++kt)
+                mbar_wait(&load_full[kt % kStages], (kt / kStages) & 1, p.err);
+        }
+    } else if (warp == 1) {
+        // -------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            bool ok = true;
+            for (int kt = 0; kt < KT && ok; ++kt) {
+                const int s = kt % kStages, sb = kt % kBStages;
+                ok = mbar_wait(&load_full[s], (kt / kStages) & 1, p.err) &&
+                     mbar_wait(&b_full[sb], (kt / kBStages) & 1, p.err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(smem + kOffA + s * kABytes);
+                const uint32_t b0 = smem_u32(smem + kOffB + sb * kBBytes);
+#pragma unroll
+                for (int ks = 0; ks < BK / 16; ++ks)
+                    tc_mma_bf16(tmem, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), kIdesc,
+                                (kt > 0 || ks > 0) ? 1u : 0u);
+                tc_commit(&load_empty[s]);  // X stage consumed
+                tc_commit(&b_empty[sb]);    // B stage consumed
+            }
+            tc_commit(acc_full);  // accumulator complete (or abandoned after a timeout)
+        }
+    } else {
+        // ----------------------------------------------------- dequant producers
+        const int wd = warp - 2;  // 0..7: n-tiles 2wd, 2wd+1 of this CTA's 16
+        const int g = lane >> 2, t = lane & 3;
+        bool ok = true;
+        for (int kt = 0; kt < KT && ok; ++kt) {
+            const int s = kt % kStages, sb = kt % kBStages;
+            ok = mbar_wait_warp(&load_full[s], (kt / kStages) & 1, p.err);
+            if (ok && kt >= kBStages) ok = mbar_wait_warp(&b_empty[sb], ((kt / kBStages) - 1) & 1, p.err);
+            if (!ok) break;
+            const uint8_t* raw = smem + kOffRaw + s * kRawBytes;
+            const uint8_t* sc = smem + kOffSc + s * kScBytes;
+            uint8_t* bt = smem + kOffB + sb * kBBytes;
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int j = 2 * wd + e;
+                const uint4 wv = *reinterpret_cast<const uint4*>(raw + j * 512 + lane * 16);
+                const uint2 sv = *reinterpret_cast<const uint2*>(sc + j * 64 + g * 8);
+                const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};  // (r0,G0) (r1,G0) (r0,G1) (r1,G1)
+                const uint32_t sq[4] = {__byte_perm(sv.x, 0, 0x1010), __byte_perm(sv.x, 0, 0x3232),
+                                        __byte_perm(sv.y, 0, 0x1010), __byte_perm(sv.y, 0, 0x3232)};
+#pragma unroll
+                for (int qq = 0; qq < 4; ++qq) {
+                    // odd rows take the other group first: the 8 lanes of a store phase then
+                    // cover 8 distinct 16-byte bank groups
+                    const bool odd = g & 1;
+                    const int q = odd ? (qq ^ 2) : qq;
+                    const int hi = q & 1, G = q >> 1;
+                    const uint32_t wsel = odd ? wq[qq ^ 2] : wq[qq];  // static indices: stays in registers
+                    const uint32_t ssel = odd ? sq[qq ^ 2] : sq[qq];
+                    uint32_t o[4];
+#pragma unroll
+                    for (int pp = 0; pp < 4; ++pp) {
+                        const uint32_t qv = int4pair_to_bf16x2(wsel >> (4 * pp));
+                        asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o[pp]) : "r"(qv), "r"(ssel));
+                    }
+                    const int n = 16 * j + g + 8 * hi;  // row of the B tile
+                    const int c16 = 4 * G + t;          // 16-byte chunk along K
+                    uint8_t* dst = bt + (n >> 3) * 1024 + (n & 7) * 128 + ((c16 ^ (n & 7)) << 4);
+                    *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+                }
+            }
+            fence_proxy_async_smem();  // make the generic stores visible to the tensor core
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&b_full[sb]);
+                mbar_arrive(&load_empty[s]);
+            }
+        }
+        // ------------------------------------------------------------- epilogue
+        if (mbar_wait_warp(acc_full, 0, p.err)) {
+            tc_fence_after();
+            const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
+            const int col0 = (warp < 6) ? 0 : 128; // two warps per lane quarter
+            const int row = mb * BM + quarter * 32 + lane;
+#pragma unroll 1
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c), r);
+                tmem_ld_wait();
+                const int n0 = nb * BN + col0 + c;
+                if (row < p.M && n0 < p.N) {
+                    if (p.y_f32) {
+                        float* yr = reinterpret_cast<float*>(p.y) + (size_t)row * p.ldy + n0;
+                        if (n0 + 32 <= p.N) {
+#pragma unroll
+                            for (int i = 0; i < 32; i += 4)
+                                *reinterpret_cast<uint4*>(yr + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+                        } else {
+                            const int lim = p.N - n0;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (i < lim) yr[i] = __uint_as_float(r[i]);
+                        }
+                    } else {
+                        uint16_t* yr = reinterpret_cast<uint16_t*>(p.y) + (size_t)row * p.ldy + n0;
+                        uint32_t h[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                            h[i] = *reinterpret_cast<uint32_t*>(&b2);
+                        }
+                        if (n0 + 32 <= p.N) {
+#pragma unroll
+                            for (int i = 0; i < 16; i += 4)
+                                *reinterpret_cast<uint4*>(yr + 2 * i) = make_uint4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+                        } else {
+                            const int lim = p.N - n0;
+#pragma unroll
+                            for (int i = 0; i < 32; ++i)
+                                if (i < lim) yr[i] = (uint16_t)(h[i >> 1] >> ((i & 1) * 16));
+                        }
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+namespace g4 {
+
+bool gemm_supported(const g4_linear* lin, int M) {
+    // row pitches of X (K bf16) and Y (N values) must allow 16-byte vector access
+    return M >= 1 && lin->dev.K % 32 == 0 && lin->dev.N % 8 == 0;
+}
+
+g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32) {
+    const g4_linear_dev& L = lin->dev;
+    if (!gemm_supported(lin, M)) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: shape K=%d N=%d", L.K, L.N);
+    CUtensorMap xmap;
+    g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
+                                        (uint64_t)L.K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_w4a16_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kSmemBytes));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    GemmParams p{};
+    p.y = y;
+    p.M = M;
+    p.N = L.N;
+    p.K = L.K;
+    p.ldy = L.N;
+    p.y_f32 = y_f32;
+    p.ktiles = L.Kc;
+    p.err = ctx->d_err;
+    const dim3 grid((M + BM - 1) / BM, (L.N + BN - 1) / BN);
+    if (grid.y > 65535) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: N=%d too large", L.N);
+    gemm_w4a16_tcgen05_kernel<<<grid, kThreads, kSmemBytes, ctx->stream>>>(xmap, lin->wmap, lin->smap, p);
+    G4_CHECK_LAUNCH("gemm_w4a16_tcgen05_kernel");
+    return G4_OK;
+}
+
+g4_status make_linear_maps(g4_linear* lin) {
+    g4_linear_dev& L = lin->dev;
+    // weight blocks as uint32 [NT rows][Kc * 128]; one box = 16 n-tiles x one 512-byte block
+    g4_status st = encode_tensor_map_2d(&lin->wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, L.wfrag, (uint64_t)L.Kc * 128,
+                                        L.NT, (uint64_t)L.Kc * 512, 128, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
+    return encode_tensor_map_2d(&lin->smap, CU_TENSOR_MAP_DATA_TYPE_UINT32, L.sfrag, (uint64_t)L.Kc * 16, L.NT,
+                                (uint64_t)L.Kc * 64, 16, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 }  // namespace g4

@@ -367,6 +367,11 @@ g4_status g4_linear_create(g4_ctx* ctx, const void* packed_i32, const void* scal
         g4_linear_destroy(lin);
         return g4::cuda_error(e, "g4_linear_create");
     }
+    st = g4::make_linear_maps(lin);
+    if (st) {
+        g4_linear_destroy(lin);
+        return st;
+    }
     *out = lin;
     return G4_OK;
 }

@@ -13,6 +13,8 @@ struct g4_linear_dev {
 struct g4_linear {
     g4_ctx* ctx = nullptr;
     g4_linear_dev dev;
+    CUtensorMap wmap;  // wfrag as uint32 [NT][Kc*128], boxes of 16 tiles x one 512-byte block
+    CUtensorMap smap;  // sfrag as uint32 [NT][Kc*16],  boxes of 16 tiles x one 64-byte block
 };
 
 namespace g4 {
@@ -20,4 +22,5 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
 // tcgen05 prefill GEMM (g4_gemm_sm100.cu)
 bool gemm_supported(const g4_linear* lin, int M);
 g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32);
+g4_status make_linear_maps(g4_linear* lin);
 }  // namespace g4

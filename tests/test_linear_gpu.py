@@ -92,3 +92,52 @@ def test_linear_errors(rt, ctx, ops, oracle, g4):
     with pytest.raises(g4.G4Error, match="only 32"):
         rt.W4Linear(ctx, make_weights(oracle, 128, 16, 2)[0], np.zeros((16, 2), np.uint16))
     assert ops.w4(lin, torch.zeros((0, 64), dtype=torch.bfloat16, device="cuda"), 0).shape == (0, 16)
+
+
+GEMM_SHAPES = [(1536, 6144), (6144, 1536), (256, 1536), (96, 40), (1536, 8960), (2048, 264)]
+
+
+@pytest.mark.parametrize("M", [1, 17, 128, 200, 512])
+@pytest.mark.parametrize("K,N", GEMM_SHAPES)
+def test_tcgen05_gemm_matches_oracle(rt, ctx, ops, oracle, K, N, M):
+    y, ref = _run(rt, ctx, ops, oracle, K, N, M, impl=2, seed=K * 3 + N + M)
+    assert max_rel(y, ref) < TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 1536, 6144), (130, 6144, 1536), (64, 96, 40)])
+def test_tcgen05_gemm_vs_torch_fp32_on_bf16_weights(rt, ctx, ops, oracle, M, K, N):
+    """The GEMM multiplies bf16 activations by the bf16 materialisation of the weights
+    (RNE of q*s) with FP32 accumulation: a torch fp32 matmul of the same operands must
+    agree to FP32 summation-order noise."""
+    packed, scales = make_weights(oracle, K, N, M + K + N)
+    lin = rt.W4Linear(ctx, packed, scales)
+    x = torch.randn((M, K), device="cuda", generator=torch.Generator(device="cuda").manual_seed(M)).to(torch.bfloat16)
+    y = ops.w4(lin, x, M, out_dtype=torch.float32, impl=2)
+    ref = x.float() @ lin.dequant(dtype=torch.bfloat16).float().T
+    ctx.check_device()
+    assert max_rel(y.cpu().numpy(), ref.cpu().numpy()) < 1e-4
+
+
+def test_tcgen05_gemm_config3_shapes(rt, ctx, ops, oracle):
+    """BASELINE config 3 shapes at M = 128 (the full sweep runs in bench.py)."""
+    for K, N in [(1536, 6144), (6144, 1536)]:
+        y, ref = _run(rt, ctx, ops, oracle, K, N, 128, impl=2, seed=99 + K)
+        assert max_rel(y, ref) < TOL
+
+
+def test_tcgen05_gemm_lm_head_shape_property(rt, ctx, ops):
+    """(K, N) = (1536, 262144) at M = 512: too large for the oracle in seconds, so check
+    against the GEMV (an independent kernel) on a row subset and linearity in x."""
+    K, N, M = 1536, 262144, 512
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    packed = torch.randint(-2**31, 2**31 - 1, (N, K // 8), device="cuda", dtype=torch.int32, generator=gen)
+    sc = torch.randn((N, K // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+    lin = rt.W4Linear(ctx, packed, sc)
+    x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y = ops.w4(lin, x, M, out_dtype=torch.float32, impl=2)
+    rows = torch.tensor([0, 1, 127, 128, 300, 511], device="cuda")
+    yg = ops.w4(lin, x[rows].contiguous(), len(rows), out_dtype=torch.float32, impl=1)
+    assert max_rel(y[rows].cpu().numpy(), yg.cpu().numpy()) < TOL
+    y2 = ops.w4(lin, (x.float() * 2).to(torch.bfloat16), M, out_dtype=torch.float32, impl=2)
+    assert torch.equal(y2, y * 2)  # exact: scaling bf16 inputs by 2 scales every product exactly
+    ctx.check_device()
