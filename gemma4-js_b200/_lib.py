@@ -18,6 +18,11 @@ G4_OK = 0
 G4_F32 = 0
 G4_BF16 = 1
 
+
+class G4Rows(C.Structure):
+    """g4_rows: where the rows of a batch sit in their sequences (include/g4w4.h)."""
+    _fields_ = [("seq_pos", C.c_void_p), ("seq_base", C.c_int), ("rows_per_seq", C.c_int), ("pos0", C.c_int)]
+
 STATUS_NAMES = {
     0: "G4_OK", -1: "G4_ERR_INVALID", -2: "G4_ERR_OOM", -3: "G4_ERR_CUDA", -4: "G4_ERR_TIMEOUT",
     -5: "G4_ERR_UNSUPPORTED", -6: "G4_ERR_RANGE", -7: "G4_ERR_DEVICE",
@@ -36,6 +41,7 @@ class G4Error(RuntimeError):
 _P = C.c_void_p
 _I = C.c_int
 _S = C.c_int32
+_F = C.c_float
 _PP = C.POINTER(C.c_void_p)
 
 # name -> (restype, argtypes); every g4_status function raises G4Error through check().
@@ -66,6 +72,21 @@ SIGNATURES = {
     "g4_kv_buffers": (_S, [_P, _PP, _PP]),
     "g4_attention": (_S, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
     "g4_attention_noalloc": (_S, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "g4_attention_rows": (_S, [_P, _P, _P, _I, _I, _I, _P, _I, _I, _I, _P]),
+    "g4_rms": (_S, [_P, _P, _P, _I, _I, _F, _P, _I]),
+    "g4_add_scale": (_S, [_P, _P, _P, C.c_longlong, _F, _P]),
+    "g4_post_norm_add": (_S, [_P, _P, _P, _I, _P, _F, _P, _I, _I, _F, _P]),
+    "g4_embed": (_S, [_P, _P, _I, _I, _P, _I, _F, _P, _P]),
+    "g4_qkv_post": (_S, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P, _P, _I]),
+    "g4_gelu_mul": (_S, [_P, _P, _I, _I, _P]),
+    "g4_gelu_ple": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "g4_ple_mix": (_S, [_P, _P, _F, _P, _P, _I, _I, _I, _F, _P]),
+    "g4_softcap_argmax": (_S, [_P, _P, _I, _I, _F, _P, _P]),
+    "g4_advance_positions": (_S, [_P, _P, _I, _I, _I]),
+    "g4_dense_create": (_S, [_P, _P, _I, _I, _I, _PP]),
+    "g4_dense_destroy": (_S, [_P]),
+    "g4_dense_weights": (_S, [_P, _PP]),
+    "g4_dense_matmul": (_S, [_P, _P, _P, _I, _P]),
 }
 
 _lib = None

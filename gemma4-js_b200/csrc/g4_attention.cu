@@ -49,6 +49,12 @@ struct AttnParams {
     int heads, keylen, qpos0, sliding, window;
     int nsplit, split_keys;  // keys per split (multiple of KT)
     int kv_row0;             // first cache row of this sequence in the tensor map
+    // Device-side positions (g4_rows): when seq_pos is set, row r belongs to sequence
+    // seq = seq_base + r / rows_per_seq, sits at seq_pos[seq] + pos0 + r % rows_per_seq,
+    // sees keylen = seq_pos[seq] + pos0 + rows_per_seq keys, and the sequence's cache
+    // rows start at seq * seq_stride.
+    const int32_t* seq_pos;
+    int seq_base, rows_per_seq, pos0, seq_stride;
 };
 
 template <int HD>
@@ -65,8 +71,19 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.y, split = blockIdx.x;
-    const int qp = p.qpos0 + r;
-    const int hi = min(qp, p.keylen - 1);
+    int qp, keylen, kv_row0;
+    if (p.seq_pos) {
+        const int seq = p.seq_base + r / p.rows_per_seq;
+        const int base = p.seq_pos[seq] + p.pos0;
+        qp = base + r % p.rows_per_seq;
+        keylen = base + p.rows_per_seq;
+        kv_row0 = seq * p.seq_stride;
+    } else {
+        qp = p.qpos0 + r;
+        keylen = p.keylen;
+        kv_row0 = p.kv_row0;
+    }
+    const int hi = min(qp, keylen - 1);
     const int lo = p.sliding ? max(0, qp - p.window + 1) : 0;
     const int s_lo = lo + split * p.split_keys;
     const int s_hi = min(hi, s_lo + p.split_keys - 1);  // inclusive
@@ -93,7 +110,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                 if (t >= C::STAGES) ok = mbar_wait(&empty[s], ((t / C::STAGES) - 1) & 1, p.err);
                 if (!ok) break;
                 mbar_arrive_expect_tx(&full[s], 2 * C::TILE_BYTES);
-                const int y = p.kv_row0 + s_lo + t * C::KT;
+                const int y = kv_row0 + s_lo + t * C::KT;
 #pragma unroll
                 for (int b = 0; b < C::BOXES; ++b) {
                     tma_load_2d(kst + s * C::TILE_BYTES + b * C::BOX_BYTES, &kmap, &full[s], b * 64, y);
@@ -169,9 +186,15 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                     o[i][3] *= al1;
                 }
             }
-            // ---- P^T as the B operand: transpose the two 8x8 key blocks ----
-            const uint32_t pb[2] = {movmatrix_trans(pack_bf16x2_bits(p0, p1)),
-                                    movmatrix_trans(pack_bf16x2_bits(p2, p3))};
+            // ---- P^T as the B operand: transpose the two 8x8 key blocks.  P is split
+            // into a bf16 head and a bf16 tail (P = hi + lo to ~2^-16), so the P.V
+            // products keep almost f32 precision; the tensor cores have room for the
+            // second mma in this HBM-bound loop. ----
+            const uint32_t h01 = pack_bf16x2_bits(p0, p1), h23 = pack_bf16x2_bits(p2, p3);
+            const uint32_t l01 = pack_bf16x2_bits(p0 - bf16_bits_to_f32(h01 & 0xFFFFu), p1 - bf16_bits_to_f32(h01 >> 16));
+            const uint32_t l23 = pack_bf16x2_bits(p2 - bf16_bits_to_f32(h23 & 0xFFFFu), p3 - bf16_bits_to_f32(h23 >> 16));
+            const uint32_t pb[2] = {movmatrix_trans(h01), movmatrix_trans(h23)};
+            const uint32_t pl[2] = {movmatrix_trans(l01), movmatrix_trans(l23)};
             // ---- O^T[HD x 8] += V^T P^T ----
             {
                 const int key = warp * 16 + ((j >> 1) << 3) + rr;
@@ -180,6 +203,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                     uint32_t a[4];
                     ldmatrix_x4_trans(a, tile_addr<HD>(vb, key, mi * 16 + ((j & 1) << 3)));
                     mma_bf16_16816(o[mi], a, pb, o[mi]);
+                    mma_bf16_16816(o[mi], a, pl, o[mi]);
                 }
             }
             __syncwarp();
@@ -306,15 +330,23 @@ __global__ void kv_append_f32_kernel(const float* __restrict__ k, const float* _
 template <int HD>
 g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& vm, const uint16_t* q,
                         int rows, int heads, int keylen, int qpos0, int sliding, int window, uint16_t* out,
-                        int kv_row0, void* fixed_scratch = nullptr, size_t fixed_bytes = 0) {
+                        int kv_row0, void* fixed_scratch = nullptr, size_t fixed_bytes = 0,
+                        const g4_rows* map = nullptr, int seq_stride = 0) {
     using C = AttnCfg<HD>;
-    // Longest key range of any row decides the split.
-    const int qp_last = qpos0 + rows - 1;
-    int lmax = min(qp_last, keylen - 1) + 1;
-    if (sliding) lmax = min(lmax, window);
+    // Longest key range of any row decides the split.  With device-side positions the
+    // host does not know the lengths: plan for a full sequence (or a full window).
+    int lmax;
+    if (map) {
+        lmax = sliding ? min(window, seq_stride) : seq_stride;
+    } else {
+        const int qp_last = qpos0 + rows - 1;
+        lmax = min(qp_last, keylen - 1) + 1;
+        if (sliding) lmax = min(lmax, window);
+    }
     const int ntiles = (lmax + C::KT - 1) / C::KT;
     int nsplit = (2 * ctx->num_sms + rows - 1) / rows;
     nsplit = min(nsplit, max(1, (ntiles + 1) / 2));
+    if (map) nsplit = max(1, min((8 * ctx->num_sms + rows - 1) / rows, ntiles));
     nsplit = max(nsplit, 1);
     const int tiles_per_split = (ntiles + nsplit - 1) / nsplit;
     nsplit = (ntiles + tiles_per_split - 1) / tiles_per_split;
@@ -333,6 +365,13 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     p.nsplit = nsplit;
     p.split_keys = tiles_per_split * C::KT;
     p.kv_row0 = kv_row0;
+    if (map) {
+        p.seq_pos = map->seq_pos;
+        p.seq_base = map->seq_base;
+        p.rows_per_seq = map->rows_per_seq;
+        p.pos0 = map->pos0;
+        p.seq_stride = seq_stride;
+    }
     if (nsplit > 1) {
         const size_t ob = (size_t)rows * nsplit * 8 * HD * sizeof(float);
         const size_t mb = (size_t)rows * nsplit * 8 * sizeof(float2);
@@ -381,12 +420,12 @@ g4_status make_kv_maps(g4_kv* kv) {
 
 g4_status launch_attention(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows, int heads,
                            int keylen, int qpos0, int sliding, int window, uint16_t* out, void* fixed_scratch,
-                           size_t fixed_bytes) {
+                           size_t fixed_bytes, const g4_rows* map, int seq_stride) {
     switch (kv->hd) {
-        case 64: return launch_attn_t<64>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
-        case 128: return launch_attn_t<128>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
-        case 256: return launch_attn_t<256>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
-        case 512: return launch_attn_t<512>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes);
+        case 64: return launch_attn_t<64>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 128: return launch_attn_t<128>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 256: return launch_attn_t<256>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 512: return launch_attn_t<512>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
         default: return set_error(G4_ERR_UNSUPPORTED, "attention: head dim %d (64/128/256/512 supported)", kv->hd);
     }
 }
@@ -510,6 +549,24 @@ g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int row
                                 sliding ? 1 : 0, window, static_cast<uint16_t*>(out_bf16));
 }
 
+
+g4_status g4_attention_rows(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads, int hd,
+                            const g4_rows* map, int seq_stride, int sliding, int window, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!kv || !q_bf16 || !out_bf16 || !map || !map->seq_pos || map->rows_per_seq < 1)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention_rows: null argument");
+    if (rows < 0) return g4::set_error(G4_ERR_INVALID, "g4_attention_rows: rows %d", rows);
+    if (rows == 0) return G4_OK;
+    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "g4_attention_rows: hd %d != cache hd %d", hd, kv->hd);
+    if (heads < 1 || heads > 8)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_attention_rows: %d heads per KV head (1..8 supported)", heads);
+    if (seq_stride < 1 || (long long)(map->seq_base + (rows - 1) / map->rows_per_seq + 1) * seq_stride > kv->rows_total)
+        return g4::set_error(G4_ERR_RANGE, "g4_attention_rows: sequences beyond the cache (%d rows)", kv->rows_total);
+    if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "g4_attention_rows: window %d", window);
+    return g4::launch_attention(ctx, kv, 0, static_cast<const uint16_t*>(q_bf16), rows, heads, 0, 0, sliding ? 1 : 0,
+                                window, static_cast<uint16_t*>(out_bf16), nullptr, 0, map, seq_stride);
+}
 
 }  // extern "C"
 

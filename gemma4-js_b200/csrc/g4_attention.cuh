@@ -15,5 +15,6 @@ namespace g4 {
 g4_status make_kv_maps(g4_kv* kv);
 g4_status launch_attention(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows,
                            int heads, int keylen, int qpos0, int sliding, int window, uint16_t* out,
-                           void* fixed_scratch = nullptr, size_t fixed_bytes = 0);
+                           void* fixed_scratch = nullptr, size_t fixed_bytes = 0, const g4_rows* map = nullptr,
+                           int seq_stride = 0);
 }  // namespace g4

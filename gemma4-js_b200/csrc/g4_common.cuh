@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <string>
+#include <vector>
 
 #include "../../include/g4w4.h"
 
@@ -24,6 +25,7 @@ struct g4_ctx {
     uint32_t* d_err = nullptr;      // device error word (bit set, see G4_DEVERR_*)
     void* ws = nullptr;             // grow-only scratch for split-K / split-KV partials
     size_t ws_bytes = 0;
+    std::vector<void*> ws_retired;  // outgrown workspaces: kept until destroy (captured graphs may use them)
     int32_t* d_ids = nullptr;       // staging for host token ids
     size_t d_ids_cap = 0;
 };
@@ -39,7 +41,8 @@ g4_status cuda_error(cudaError_t e, const char* what);
 void count_launch(uint64_t n = 1);
 // Makes ctx->device current on this thread; returns G4_OK or an error.
 g4_status use_device(const g4_ctx* ctx);
-// Ensures ctx->ws holds at least `bytes` (grow-only; synchronises when it grows).
+// Ensures ctx->ws holds at least `bytes` (grow-only).  An outgrown buffer is retired,
+// not freed, so CUDA graphs captured with it stay valid until the context is destroyed.
 g4_status ensure_workspace(g4_ctx* ctx, size_t bytes);
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 g4_status encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,

@@ -43,14 +43,10 @@ g4_status ensure_workspace(g4_ctx* ctx, size_t bytes) {
     if (bytes <= ctx->ws_bytes) return G4_OK;
     size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
     want = (want + 4095) & ~size_t(4095);
-    if (ctx->ws) {
-        // The old buffer may still be read by queued kernels.
-        G4_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
-        G4_CHECK_CUDA(cudaFree(ctx->ws));
-        ctx->ws = nullptr;
-        ctx->ws_bytes = 0;
-    }
-    G4_CHECK_CUDA(cudaMalloc(&ctx->ws, want));
+    void* fresh = nullptr;
+    G4_CHECK_CUDA(cudaMalloc(&fresh, want));
+    if (ctx->ws) ctx->ws_retired.push_back(ctx->ws);  // queued kernels or captured graphs may still use it
+    ctx->ws = fresh;
     ctx->ws_bytes = want;
     return G4_OK;
 }
@@ -127,6 +123,7 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
     cudaStreamSynchronize(ctx->stream);
     cudaFree(ctx->d_err);
     cudaFree(ctx->ws);
+    for (void* p : ctx->ws_retired) cudaFree(p);
     cudaFree(ctx->d_ids);
     delete ctx;
     return G4_OK;

@@ -27,8 +27,8 @@ namespace {
 using namespace g4dev;
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kStages = 4;      // X + raw weight ring
-constexpr int kBStages = 2;     // dequantised B ring
+constexpr int kStages = 4;      // X (+ raw weight, or bf16 B) ring
+constexpr int kBStages = 2;     // dequantised B ring (W4 path)
 constexpr int kDqWarps = 8;
 constexpr int kThreads = (2 + kDqWarps) * 32;
 constexpr int kABytes = BM * BK * 2;           // 16 KB
@@ -36,13 +36,19 @@ constexpr int kRawBytes = (BN / 16) * 512;      // 8 KB
 constexpr int kScBytes = (BN / 16) * 64;        // 1 KB
 constexpr int kBBytes = BN * BK * 2;            // 32 KB
 constexpr int kTmemCols = 256;
-// [A stages][B stages][raw stages][scale stages][barriers]
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kABytes;
-constexpr int kOffRaw = kOffB + kBStages * kBBytes;
-constexpr int kOffSc = kOffRaw + kStages * kRawBytes;
-constexpr int kOffBar = kOffSc + kStages * kScBytes;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;  // + alignment slack
+
+// Shared-memory plan.  W4 path: [A x4][B x2][raw x4][scales x4][barriers];
+// bf16 path (B loaded by TMA, no dequant): [A x4][B x4][barriers].
+template <bool kW4>
+struct GemmSmem {
+    static constexpr int kBSt = kW4 ? kBStages : kStages;
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kABytes;
+    static constexpr int kOffRaw = kOffB + kBSt * kBBytes;
+    static constexpr int kOffSc = kOffRaw + (kW4 ? kStages * kRawBytes : 0);
+    static constexpr int kOffBar = kOffSc + (kW4 ? kStages * kScBytes : 0);
+    static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
+};
 
 // ---- tcgen05 wrappers ----
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -100,9 +106,15 @@ struct GemmParams {
     uint32_t* err;
 };
 
+// kW4 = true: B = dequant(int4 blocks) by the producer warps (wmap / smap = weight
+// blocks / scales).  kW4 = false: B is a bf16 [N, K] matrix loaded by TMA (wmap,
+// 128B swizzle), e.g. the tied bf16 LM head; smap is unused.
+template <bool kW4>
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
-                          const __grid_constant__ CUtensorMap smap, GemmParams p) {
+gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                    const __grid_constant__ CUtensorMap smap, GemmParams p) {
+    using L = GemmSmem<kW4>;
+    constexpr int kOffA = L::kOffA, kOffB = L::kOffB, kOffRaw = L::kOffRaw, kOffSc = L::kOffSc, kOffBar = L::kOffBar;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* load_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -119,7 +131,7 @@ gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&load_full[s], 1);
-            mbar_init(&load_empty[s], 1 + kDqWarps);
+            mbar_init(&load_empty[s], kW4 ? 1 + kDqWarps : 1);
         }
         for (int s = 0; s < kBStages; ++s) {
             mbar_init(&b_full[s], kDqWarps);
@@ -139,15 +151,21 @@ gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
         if (lane == 0) {
             prefetch_tensor_map(&xmap);
             prefetch_tensor_map(&wmap);
-            prefetch_tensor_map(&smap);
+            if (kW4) prefetch_tensor_map(&smap);
             int issued = 0;
             for (int kt = 0; kt < KT; ++kt) {
                 const int s = kt % kStages;
                 if (kt >= kStages && !mbar_wait(&load_empty[s], ((kt / kStages) - 1) & 1, p.err)) break;
-                mbar_arrive_expect_tx(&load_full[s], kABytes + kRawBytes + kScBytes);
-                tma_load_2d(smem + kOffA + s * kABytes, &xmap, &load_full[s], kt * BK, mb * BM);
-                tma_load_2d(smem + kOffRaw + s * kRawBytes, &wmap, &load_full[s], kt * 128, nb * (BN / 16));
-                tma_load_2d(smem + kOffSc + s * kScBytes, &smap, &load_full[s], kt * 16, nb * (BN / 16));
+                if constexpr (kW4) {
+                    mbar_arrive_expect_tx(&load_full[s], kABytes + kRawBytes + kScBytes);
+                    tma_load_2d(smem + kOffA + s * kABytes, &xmap, &load_full[s], kt * BK, mb * BM);
+                    tma_load_2d(smem + kOffRaw + s * kRawBytes, &wmap, &load_full[s], kt * 128, nb * (BN / 16));
+                    tma_load_2d(smem + kOffSc + s * kScBytes, &smap, &load_full[s], kt * 16, nb * (BN / 16));
+                } else {
+                    mbar_arrive_expect_tx(&load_full[s], kABytes + kBBytes);
+                    tma_load_2d(smem + kOffA + s * kABytes, &xmap, &load_full[s], kt * BK, mb * BM);
+                    tma_load_2d(smem + kOffB + s * kBBytes, &wmap, &load_full[s], kt * BK, nb * BN);
+                }
                 issued = kt + 1;
             }
             // Drain: our copies must land before the CTA can exit.
@@ -159,9 +177,9 @@ gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
         if (lane == 0) {
             bool ok = true;
             for (int kt = 0; kt < KT && ok; ++kt) {
-                const int s = kt % kStages, sb = kt % kBStages;
-                ok = mbar_wait(&load_full[s], (kt / kStages) & 1, p.err) &&
-                     mbar_wait(&b_full[sb], (kt / kBStages) & 1, p.err);
+                const int s = kt % kStages, sb = kW4 ? kt % kBStages : s;
+                ok = mbar_wait(&load_full[s], (kt / kStages) & 1, p.err);
+                if (kW4 && ok) ok = mbar_wait(&b_full[sb], (kt / kBStages) & 1, p.err);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(smem + kOffA + s * kABytes);
@@ -170,8 +188,8 @@ gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
                 for (int ks = 0; ks < BK / 16; ++ks)
                     tc_mma_bf16(tmem, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), kIdesc,
                                 (kt > 0 || ks > 0) ? 1u : 0u);
-                tc_commit(&load_empty[s]);  // X stage consumed
-                tc_commit(&b_empty[sb]);    // B stage consumed
+                tc_commit(&load_empty[s]);        // X (and bf16 B) stage consumed
+                if (kW4) tc_commit(&b_empty[sb]);  // dequantised B stage consumed
             }
             tc_commit(acc_full);  // accumulator complete (or abandoned after a timeout)
         }
@@ -180,7 +198,7 @@ gemm_w4a16_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid
         const int wd = warp - 2;  // 0..7: n-tiles 2wd, 2wd+1 of this CTA's 16
         const int g = lane >> 2, t = lane & 3;
         bool ok = true;
-        for (int kt = 0; kt < KT && ok; ++kt) {
+        for (int kt = 0; kW4 && kt < KT && ok; ++kt) {
             const int s = kt % kStages, sb = kt % kBStages;
             ok = mbar_wait_warp(&load_full[s], (kt / kStages) & 1, p.err);
             if (ok && kt >= kBStages) ok = mbar_wait_warp(&b_empty[sb], ((kt / kBStages) - 1) & 1, p.err);
@@ -298,8 +316,8 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     if (st) return st;
     static std::atomic<uint64_t> attr_set{0};
     if (!(attr_set.load() & (1ull << ctx->device))) {
-        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_w4a16_tcgen05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kSmemBytes));
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           GemmSmem<true>::kBytes));
         attr_set.fetch_or(1ull << ctx->device);
     }
     GemmParams p{};
@@ -313,8 +331,37 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     p.err = ctx->d_err;
     const dim3 grid((M + BM - 1) / BM, (L.N + BN - 1) / BN);
     if (grid.y > 65535) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: N=%d too large", L.N);
-    gemm_w4a16_tcgen05_kernel<<<grid, kThreads, kSmemBytes, ctx->stream>>>(xmap, lin->wmap, lin->smap, p);
-    G4_CHECK_LAUNCH("gemm_w4a16_tcgen05_kernel");
+    gemm_tcgen05_kernel<true><<<grid, kThreads, GemmSmem<true>::kBytes, ctx->stream>>>(xmap, lin->wmap, lin->smap, p);
+    G4_CHECK_LAUNCH("gemm_tcgen05_kernel<W4>");
+    return G4_OK;
+}
+
+g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, const uint16_t* x, int M,
+                           float* y) {
+    if (K % 8 != 0 || N % 8 != 0) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 bf16 GEMM: K=%d N=%d", K, N);
+    CUtensorMap xmap;
+    g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), K, M,
+                                        (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           GemmSmem<false>::kBytes));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    GemmParams p{};
+    p.y = y;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.ldy = N;
+    p.y_f32 = 1;
+    p.ktiles = (K + BK - 1) / BK;
+    p.err = ctx->d_err;
+    const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
+    if (grid.y > 65535) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 bf16 GEMM: N=%d too large", N);
+    gemm_tcgen05_kernel<false><<<grid, kThreads, GemmSmem<false>::kBytes, ctx->stream>>>(xmap, bmap, bmap, p);
+    G4_CHECK_LAUNCH("gemm_tcgen05_kernel<bf16>");
     return G4_OK;
 }
 

@@ -1,0 +1,388 @@
+// g4_glue.cu -- the row-wise operators of the reference runtime around the W4A16 path,
+// fused where the model graph chains them.
+//
+// Reference shaders (custom-webgpu/gpu-runtime.js): RMS_SHADER :1104-1118, ADD_SCALE
+// :1120-1128, SCALE :1130-1137, GELU_MUL :1139-1157, GELU_PLE :1159-1173, NORM_ROPE
+// :1175-1202, PLE_MIX :1250-1263, BF16_HEAD :1265-1277 and topK :1396-1425.  Each
+// kernel keeps the shader's f32 arithmetic; activations that feed a W4A16 linear or
+// the attention are emitted in bf16 (round to nearest even).
+//
+// Positions: rows of a batch map to sequences through (seq_base, rows_per_seq):
+// row r belongs to sequence seq_base + r / rows_per_seq at offset r % rows_per_seq,
+// and its absolute position is seq_pos[seq] + offset.  seq_pos lives on the device,
+// so a captured decode step replays correctly as positions advance.
+#include <stdio.h>
+
+#include "g4_common.cuh"
+#include "g4_glue.cuh"
+
+namespace {
+
+using namespace g4dev;
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float s = 0.f;
+    const int nw = blockDim.x >> 5;
+    for (int i = 0; i < nw; ++i) s += red[i];
+    return s;
+}
+
+__device__ __forceinline__ int row_position(const G4Rows& R, int r) {
+    const int seq = R.seq_base + r / R.rows_per_seq;
+    return (R.seq_pos ? R.seq_pos[seq] : 0) + R.pos0 + r % R.rows_per_seq;
+}
+__device__ __forceinline__ int row_seq(const G4Rows& R, int r) { return R.seq_base + r / R.rows_per_seq; }
+
+// gelu_tanh with the reference's clamp of the tanh argument to [-10, 10] (:1154).
+__device__ __forceinline__ float gelu_ref(float x) {
+    const float c = 0.7978845608028654f;
+    const float z = c * (x + 0.044715f * x * x * x);
+    const float t = tanhf(fminf(fmaxf(z, -10.f), 10.f));
+    return 0.5f * x * (1.f + t);
+}
+
+// RMS_SHADER: y = x * rsqrt(mean(x^2) + eps) * scale (scale optional).
+__global__ void __launch_bounds__(kRowThreads) rms_kernel(const float* __restrict__ x, const float* __restrict__ scale,
+                                                          int width, float eps, void* __restrict__ out, int out_bf16) {
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    const float* xr = x + (size_t)r * width;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) ss += xr[i] * xr[i];
+    const float inv = rsqrtf(block_sum(ss, red) / (float)width + eps);
+    for (int i = threadIdx.x; i < width; i += blockDim.x) {
+        const float v = xr[i] * inv * (scale ? scale[i] : 1.f);
+        if (out_bf16)
+            reinterpret_cast<uint16_t*>(out)[(size_t)r * width + i] = (uint16_t)f32_to_bf16_bits(v);
+        else
+            reinterpret_cast<float*>(out)[(size_t)r * width + i] = v;
+    }
+}
+
+// ADD_SCALE: y = (a + b) * s.
+__global__ void add_scale_kernel(const float* __restrict__ a, const float* __restrict__ b, long long n, float s,
+                                 float* __restrict__ y) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = (a[i] + b[i]) * s;
+}
+
+// RMS_SHADER + ADD_SCALE (+ the next RMS_SHADER) of one residual update:
+//   h = (h + rms(y) * w_post) * skip;  x = bf16(w_next ? rms(h) * w_next : h)
+__global__ void __launch_bounds__(kRowThreads) post_norm_add_kernel(float* __restrict__ h, const float* __restrict__ y,
+                                                                    int ldy, const float* __restrict__ w_post,
+                                                                    float skip, const float* __restrict__ w_next,
+                                                                    int width, float eps, uint16_t* __restrict__ x_out) {
+    __shared__ float red[32];
+    const int r = blockIdx.x;
+    float* hr = h + (size_t)r * width;
+    const float* yr = y + (size_t)r * ldy;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) ss += yr[i] * yr[i];
+    const float inv = rsqrtf(block_sum(ss, red) / (float)width + eps);
+    float ss2 = 0.f;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) {
+        const float v = (hr[i] + yr[i] * inv * w_post[i]) * skip;
+        hr[i] = v;
+        ss2 += v * v;
+    }
+    if (w_next) {
+        const float inv2 = rsqrtf(block_sum(ss2, red) / (float)width + eps);
+        for (int i = threadIdx.x; i < width; i += blockDim.x)
+            x_out[(size_t)r * width + i] = (uint16_t)f32_to_bf16_bits(hr[i] * inv2 * w_next[i]);
+    } else if (x_out) {
+        for (int i = threadIdx.x; i < width; i += blockDim.x)
+            x_out[(size_t)r * width + i] = (uint16_t)f32_to_bf16_bits(hr[i]);
+    }
+}
+
+// Token embedding rows (bf16) times `scale` (SCALE shader with sqrt(hidden)), f32
+// residual stream h and its bf16 copy x (the input of the top PLE projection).
+__global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __restrict__ table, int vocab, int width,
+                                                            const int32_t* __restrict__ ids, float scale,
+                                                            float* __restrict__ h, uint16_t* __restrict__ x,
+                                                            uint32_t* err) {
+    const int r = blockIdx.x;
+    const int id = ids[r];
+    const bool ok = (unsigned)id < (unsigned)vocab;
+    if (!ok && threadIdx.x == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
+    const uint16_t* er = table + (size_t)(ok ? id : 0) * width;
+    for (int i = threadIdx.x; i < width; i += blockDim.x) {
+        const float v = ok ? bf16_bits_to_f32(er[i]) * scale : 0.f;
+        h[(size_t)r * width + i] = v;
+        if (x) x[(size_t)r * width + i] = (uint16_t)f32_to_bf16_bits(v);
+    }
+}
+
+// NORM_ROPE_SHADER for the q heads and the k head of one row, RMS_SHADER (no scale)
+// for v; q goes to q_out (bf16 [rows, H, hd]); k and v are written straight into the
+// bf16 caches at the row's absolute position (KVCache.append, gemma4-webgpu.js:128-135).
+// One CTA per (row, head slot); slot < H: q head, H: k, H + 1: v.  Thread i owns
+// elements i and i + hd/2 (a rotation pair).
+__global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int hd, int has_kv,
+                                const float* __restrict__ qnorm, const float* __restrict__ knorm, float eps,
+                                int rope_angles, float rope_base, G4Rows R, uint16_t* __restrict__ q_out,
+                                uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cache_cap) {
+    __shared__ float red[32];
+    const int slot = blockIdx.x, r = blockIdx.y;
+    const int half = hd >> 1;
+    const int i = threadIdx.x;  // 0 .. half-1
+    const float* src = y + (size_t)r * ldy + (size_t)slot * hd;
+    const float a0 = src[i], a1 = src[i + half];
+    const float inv = rsqrtf(block_sum(a0 * a0 + a1 * a1, red) / (float)hd + eps);
+    const int pos = row_position(R, r);
+    if (slot == H + 1) {  // v: RMS without scale (official-w4a16-layer0.js:176-182)
+        uint16_t* dst = vcache + ((size_t)row_seq(R, r) * cache_cap + pos) * hd;
+        dst[i] = (uint16_t)f32_to_bf16_bits(a0 * inv);
+        dst[i + half] = (uint16_t)f32_to_bf16_bits(a1 * inv);
+        return;
+    }
+    const float* sc = slot < H ? qnorm : knorm;
+    const float x0 = a0 * inv * sc[i], x1 = a1 * inv * sc[i + half];
+    float sn = 0.f, cs = 1.f;
+    if (i < rope_angles) {
+        const float theta = (float)pos / powf(rope_base, 2.f * (float)i / (float)hd);
+        sn = sinf(theta);
+        cs = cosf(theta);
+    }
+    const float o0 = x0 * cs - x1 * sn, o1 = x1 * cs + x0 * sn;
+    uint16_t* dst = slot < H ? q_out + ((size_t)r * H + slot) * hd
+                             : kcache + ((size_t)row_seq(R, r) * cache_cap + pos) * hd;
+    dst[i] = (uint16_t)f32_to_bf16_bits(o0);
+    dst[i + half] = (uint16_t)f32_to_bf16_bits(o1);
+}
+
+// GELU_MUL over a fused [gate | up] projection: out = bf16(gelu(gate) * up).
+__global__ void gelu_mul_kernel(const float* __restrict__ gu, int inter, long long n, uint16_t* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long r = i / inter, c = i - r * inter;
+    const float* row = gu + r * 2 * inter;
+    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(row[c]) * row[inter + c]);
+}
+
+// GELU_PLE: out = bf16(gelu(gate) * per_layer[row, layer, :]).
+__global__ void gelu_ple_kernel(const float* __restrict__ gate, const float* __restrict__ per_layer, int layer,
+                                int layers, int dim, long long n, uint16_t* __restrict__ out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long r = i / dim, d = i - r * dim;
+    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(gate[i]) * per_layer[(r * layers + layer) * dim + d]);
+}
+
+// SCALE + PLE_MIX: p = proj * proj_scale; y = (rms(p) * norm + tok_ple * sqrt(dim)) / sqrt(2)
+// per (row, layer) segment of `dim`.  One CTA per segment, one thread per element.
+__global__ void ple_mix_kernel(const float* __restrict__ proj, float proj_scale, const float* __restrict__ norm,
+                               const float* __restrict__ tok_ple, int dim, float eps, float* __restrict__ out) {
+    __shared__ float red[32];
+    const size_t base = (size_t)blockIdx.x * dim;
+    const int d = threadIdx.x;
+    const float p = proj[base + d] * proj_scale;
+    const float inv = rsqrtf(block_sum(p * p, red) / (float)dim + eps);
+    out[base + d] = (p * inv * norm[d] + tok_ple[base + d] * sqrtf((float)dim)) * 0.7071067811865476f;
+}
+
+// softcap + argmax, pass 1: per (row, chunk) the largest tanh(v / cap) * cap and its
+// lowest index (topK keeps the first of equal values, gpu-runtime.js:1396-1425).
+constexpr int kArgChunk = 4096;
+__device__ __forceinline__ void arg_better(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const float* __restrict__ logits, int vocab, float cap,
+                                                             float2* __restrict__ part) {
+    __shared__ float sv[256];
+    __shared__ int si[256];
+    const int r = blockIdx.y, c = blockIdx.x;
+    const float* lr = logits + (size_t)r * vocab;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    const int end = min(vocab, (c + 1) * kArgChunk);
+    for (int i = c * kArgChunk + threadIdx.x; i < end; i += blockDim.x) {
+        const float raw = lr[i];
+        const float v = cap > 0.f ? tanhf(raw / cap) * cap : raw;
+        if (v == v) arg_better(bv, bi, v, i);  // skip NaN (topK skips non-finite logits)
+    }
+    sv[threadIdx.x] = bv;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+        if (threadIdx.x < o) arg_better(sv[threadIdx.x], si[threadIdx.x], sv[threadIdx.x + o], si[threadIdx.x + o]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) part[(size_t)r * gridDim.x + c] = make_float2(sv[0], __int_as_float(si[0]));
+}
+// pass 2: reduce the chunk partials of a row; write the id (and optionally the value).
+__global__ void __launch_bounds__(256) argmax_final_kernel(const float2* __restrict__ part, int nparts,
+                                                           int32_t* __restrict__ ids, float* __restrict__ vals) {
+    __shared__ float sv[256];
+    __shared__ int si[256];
+    const int r = blockIdx.x;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+        const float2 p = part[(size_t)r * nparts + i];
+        arg_better(bv, bi, p.x, __float_as_int(p.y));
+    }
+    sv[threadIdx.x] = bv;
+    si[threadIdx.x] = bi;
+    __syncthreads();
+    for (int o = 128; o > 0; o >>= 1) {
+        if (threadIdx.x < o) arg_better(sv[threadIdx.x], si[threadIdx.x], sv[threadIdx.x + o], si[threadIdx.x + o]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        ids[r] = si[0];
+        if (vals) vals[r] = sv[0];
+    }
+}
+
+// Advances the positions of sequences [seq_base, seq_base + nseq) by `by`.
+__global__ void advance_pos_kernel(int32_t* seq_pos, int seq_base, int nseq, int by) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < nseq) seq_pos[seq_base + i] += by;
+}
+
+inline unsigned blocks_for(long long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+extern "C" {
+
+g4_status g4_rms(g4_ctx* ctx, const float* x, const float* scale, int rows, int width, float eps, void* out,
+                 g4_dtype out_dtype) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || width <= 0 || !x || !out) return g4::set_error(G4_ERR_INVALID, "g4_rms: bad arguments");
+    if (rows == 0) return G4_OK;
+    rms_kernel<<<rows, kRowThreads, 0, ctx->stream>>>(x, scale, width, eps, out, out_dtype == G4_BF16);
+    G4_CHECK_LAUNCH("rms_kernel");
+    return G4_OK;
+}
+
+g4_status g4_add_scale(g4_ctx* ctx, const float* a, const float* b, long long n, float scale, float* y) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (n < 0 || !a || !b || !y) return g4::set_error(G4_ERR_INVALID, "g4_add_scale: bad arguments");
+    if (n == 0) return G4_OK;
+    add_scale_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(a, b, n, scale, y);
+    G4_CHECK_LAUNCH("add_scale_kernel");
+    return G4_OK;
+}
+
+g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const float* w_post, float skip,
+                           const float* w_next, int rows, int width, float eps, void* x_out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || width <= 0 || !h || !y || !w_post) return g4::set_error(G4_ERR_INVALID, "g4_post_norm_add: bad arguments");
+    if (rows == 0) return G4_OK;
+    post_norm_add_kernel<<<rows, kRowThreads, 0, ctx->stream>>>(h, y, ldy, w_post, skip, w_next, width, eps,
+                                                                static_cast<uint16_t*>(x_out_bf16));
+    G4_CHECK_LAUNCH("post_norm_add_kernel");
+    return G4_OK;
+}
+
+g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, const int32_t* ids_dev, int rows,
+                   float scale, float* h_out, void* x_out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || !table_bf16 || !ids_dev || !h_out) return g4::set_error(G4_ERR_INVALID, "g4_embed: bad arguments");
+    if (rows == 0) return G4_OK;
+    embed_kernel<<<rows, kRowThreads, 0, ctx->stream>>>(static_cast<const uint16_t*>(table_bf16), vocab, width,
+                                                        ids_dev, scale, h_out, static_cast<uint16_t*>(x_out_bf16),
+                                                        ctx->d_err);
+    G4_CHECK_LAUNCH("embed_kernel");
+    return G4_OK;
+}
+
+g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,
+                      const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
+                      int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || !y || !qnorm || !rows_map || !q_out_bf16 || (has_kv && (!knorm || !kcache_bf16 || !vcache_bf16)))
+        return g4::set_error(G4_ERR_INVALID, "g4_qkv_post: bad arguments");
+    if (hd % 64 != 0 || hd > 1024) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_qkv_post: hd %d", hd);
+    if (rows == 0) return G4_OK;
+    qkv_post_kernel<<<dim3(heads + (has_kv ? 2 : 0), rows), hd / 2, 0, ctx->stream>>>(
+        y, ldy, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map,
+        static_cast<uint16_t*>(q_out_bf16), static_cast<uint16_t*>(kcache_bf16), static_cast<uint16_t*>(vcache_bf16),
+        cache_cap);
+    G4_CHECK_LAUNCH("qkv_post_kernel");
+    return G4_OK;
+}
+
+g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || inter <= 0 || !gate_up || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_gelu_mul: bad arguments");
+    const long long n = (long long)rows * inter;
+    if (n == 0) return G4_OK;
+    gelu_mul_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(gate_up, inter, n, static_cast<uint16_t*>(out_bf16));
+    G4_CHECK_LAUNCH("gelu_mul_kernel");
+    return G4_OK;
+}
+
+g4_status g4_gelu_ple(g4_ctx* ctx, const float* gate, const float* per_layer, int layer, int layers, int dim,
+                      int rows, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || !gate || !per_layer || !out_bf16 || layer < 0 || layer >= layers)
+        return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple: bad arguments");
+    const long long n = (long long)rows * dim;
+    if (n == 0) return G4_OK;
+    gelu_ple_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(gate, per_layer, layer, layers, dim, n,
+                                                                 static_cast<uint16_t*>(out_bf16));
+    G4_CHECK_LAUNCH("gelu_ple_kernel");
+    return G4_OK;
+}
+
+g4_status g4_ple_mix(g4_ctx* ctx, const float* proj, float proj_scale, const float* norm, const float* tok_ple,
+                     int rows, int layers, int dim, float eps, float* out) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || !proj || !norm || !tok_ple || !out || dim > 1024 || dim % 32)
+        return g4::set_error(G4_ERR_INVALID, "g4_ple_mix: bad arguments");
+    if (rows == 0) return G4_OK;
+    ple_mix_kernel<<<rows * layers, dim, 0, ctx->stream>>>(proj, proj_scale, norm, tok_ple, dim, eps, out);
+    G4_CHECK_LAUNCH("ple_mix_kernel");
+    return G4_OK;
+}
+
+g4_status g4_softcap_argmax(g4_ctx* ctx, const float* logits, int rows, int vocab, float cap, int32_t* ids_out,
+                            float* vals_out) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || vocab <= 0 || !logits || !ids_out) return g4::set_error(G4_ERR_INVALID, "g4_softcap_argmax: bad arguments");
+    if (rows == 0) return G4_OK;
+    const int nparts = (vocab + kArgChunk - 1) / kArgChunk;
+    st = g4::ensure_workspace(ctx, (size_t)rows * nparts * sizeof(float2));
+    if (st) return st;
+    float2* part = static_cast<float2*>(ctx->ws);
+    argmax_partial_kernel<<<dim3(nparts, rows), 256, 0, ctx->stream>>>(logits, vocab, cap, part);
+    G4_CHECK_LAUNCH("argmax_partial_kernel");
+    argmax_final_kernel<<<rows, 256, 0, ctx->stream>>>(part, nparts, ids_out, vals_out);
+    G4_CHECK_LAUNCH("argmax_final_kernel");
+    return G4_OK;
+}
+
+g4_status g4_advance_positions(g4_ctx* ctx, int32_t* seq_pos, int seq_base, int nseq, int by) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!seq_pos || nseq < 0) return g4::set_error(G4_ERR_INVALID, "g4_advance_positions: bad arguments");
+    if (nseq == 0) return G4_OK;
+    advance_pos_kernel<<<blocks_for(nseq, 256), 256, 0, ctx->stream>>>(seq_pos, seq_base, nseq, by);
+    G4_CHECK_LAUNCH("advance_pos_kernel");
+    return G4_OK;
+}
+
+}  // extern "C"

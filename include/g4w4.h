@@ -45,6 +45,21 @@ typedef struct g4_ctx g4_ctx;
 typedef struct g4_linear g4_linear;
 typedef struct g4_ple_table g4_ple_table;
 typedef struct g4_kv g4_kv;
+typedef struct g4_dense g4_dense;
+
+/* Where the rows of a batch sit in their sequences.  Row r belongs to sequence
+ * seq_base + r / rows_per_seq; its absolute position is
+ *   (seq_pos ? seq_pos[seq] : 0) + pos0 + r % rows_per_seq.
+ * seq_pos is a device array (one entry per sequence), so a captured decode step
+ * stays valid as g4_advance_positions moves the sequences forward.
+ * Prefill of one sequence s: {seq_pos, s, T, 0}; batched decode: {seq_pos, 0, 1, 0};
+ * the reference's host-side position (startPos): {NULL, 0, rows, startPos}. */
+typedef struct {
+    const int32_t* seq_pos;
+    int seq_base;
+    int rows_per_seq;
+    int pos0;
+} g4_rows;
 
 /* ---------------------------------------------------------------- context --
  * Replaces the WebGPU device + queue the runtime is constructed with
@@ -177,6 +192,65 @@ g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int row
  *     at zero: each call writes every partial it reads. */
 g4_status g4_attention_noalloc(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
                                int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16);
+
+/* Attention with device-side positions (see g4_rows): row r of q attends to the cache
+ * rows of its sequence, seq * seq_stride .. + keylen, keylen = seq_pos[seq] + pos0 +
+ * rows_per_seq.  Same kernel and mask as g4_attention; the key split is planned for a
+ * full sequence (or window), so one launch stays valid for every position. */
+g4_status g4_attention_rows(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads, int hd,
+                            const g4_rows* map, int seq_stride, int sliding, int window, void* out_bf16);
+
+/* ------------------------------------------------------ row-wise operators --
+ * The rest of GPUOps (custom-webgpu/gpu-runtime.js:1325-1378), fused where the model
+ * graph (gemma4-webgpu.js:215-310) chains them.  f32 math as in the shaders; outputs
+ * that feed a W4A16 linear or the attention are bf16 (round to nearest even). */
+
+/* GPUOps.rms (RMS_SHADER :1104-1118): out = x * rsqrt(mean(x^2) + eps) * scale (scale may be NULL). */
+g4_status g4_rms(g4_ctx* ctx, const float* x, const float* scale, int rows, int width, float eps, void* out,
+                 g4_dtype out_dtype);
+/* GPUOps.addScale (ADD_SCALE :1120-1128): y = (a + b) * scale. */
+g4_status g4_add_scale(g4_ctx* ctx, const float* a, const float* b, long long n, float scale, float* y);
+/* rms + addScale (+ the next rms) of one residual update (gemma4-webgpu.js:264-273, :288-297, :302-307):
+ * h = (h + rms(y) * w_post) * skip; x_out = bf16(w_next ? rms(h) * w_next : h) (x_out may be NULL). */
+g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const float* w_post, float skip,
+                           const float* w_next, int rows, int width, float eps, void* x_out_bf16);
+/* Embedding rows times scale (gemma4-webgpu.js:199, :318 scale by sqrt(hidden)): h f32, x bf16 (may be NULL).
+ * ids on the device; an out-of-range id gives a zero row and raises the device error word. */
+g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, const int32_t* ids_dev, int rows,
+                   float scale, float* h_out, void* x_out_bf16);
+/* GPUOps.normRope (NORM_ROPE_SHADER :1175-1202) for the q heads and the k head, rms without scale
+ * for v, and KVCache.append (gemma4-webgpu.js:238-249): y f32 [rows, ldy] holds q (heads*hd),
+ * then k (hd), then v (hd); q_out bf16 [rows, heads, hd]; k and v go to the bf16 caches at
+ * row seq * cache_cap + position.  has_kv = 0 processes q only (KV-shared layers). */
+g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,
+                      const float* knorm, float eps, int rope_angles, float rope_base, const g4_rows* map,
+                      int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap);
+/* GPUOps.geluMul (GELU_MUL :1139-1157) over a fused [gate | up] projection [rows, 2*inter] -> bf16 [rows, inter]. */
+g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, void* out_bf16);
+/* GPUOps.geluPle (GELU_PLE :1159-1173): bf16(gelu(gate) * per_layer[row, layer, :]). */
+g4_status g4_gelu_ple(g4_ctx* ctx, const float* gate, const float* per_layer, int layer, int layers, int dim,
+                      int rows, void* out_bf16);
+/* GPUOps.scale + GPUOps.pleMix (SCALE :1130-1137, PLE_MIX :1250-1263, gemma4-webgpu.js:318-321):
+ * out = (rms(proj * proj_scale) * norm + tok_ple * sqrt(dim)) / sqrt(2) per [row, layer] segment. */
+g4_status g4_ple_mix(g4_ctx* ctx, const float* proj, float proj_scale, const float* norm, const float* tok_ple,
+                     int rows, int layers, int dim, float eps, float* out);
+/* Softcap and greedy pick (BF16_HEAD's tanh(x/cap)*cap :1275, topK :1396-1425 and
+ * gemma4-webgpu.js:465-478): per row the lowest index of the largest capped logit
+ * (non-finite logits skipped); vals_out may be NULL.  cap <= 0 disables the softcap. */
+g4_status g4_softcap_argmax(g4_ctx* ctx, const float* logits, int rows, int vocab, float cap, int32_t* ids_out,
+                            float* vals_out);
+/* seq_pos[seq_base .. seq_base + nseq) += by (device-side step counter of a decode loop). */
+g4_status g4_advance_positions(g4_ctx* ctx, int32_t* seq_pos, int seq_base, int nseq, int by);
+
+/* ------------------------------------------------------- bf16 dense (LM head) --
+ * The tied bf16 embedding used as the LM head (gemma4-webgpu.js:170-188, BF16_HEAD
+ * :1265-1277): w bf16 [N, K], copied to the device (NULL w: allocate only). */
+g4_status g4_dense_create(g4_ctx* ctx, const void* w_bf16, int K, int N, int src_on_device, g4_dense** out);
+g4_status g4_dense_destroy(g4_dense* d);
+/* Device pointer of the [N, K] bf16 weights (the embedding table for g4_embed). */
+g4_status g4_dense_weights(const g4_dense* d, void** w);
+/* y[M, N] f32 = x[M, K] bf16 . W^T (headChunk without the softcap, all chunks in one launch). */
+g4_status g4_dense_matmul(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, int M, float* y);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,148 @@
+"""Row-wise operators around the hot path (GPUOps.rms / addScale / normRope / geluMul /
+geluPle / pleMix, the tied bf16 head and the greedy pick) against the oracle's
+formulas, through the C ABI."""
+import ctypes as C
+import importlib
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_round, max_rel
+
+pytestmark = pytest.mark.gpu
+
+mo = importlib.import_module("oracle.model_oracle")
+L = importlib.import_module("gemma4-js_b200._lib")
+
+
+def P(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def g(seed):
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+def test_rms_and_add_scale(ctx):
+    x = torch.randn((5, 1536), device="cuda", generator=g(1)) * 3
+    sc = torch.rand(1536, device="cuda", generator=g(2)) + 0.5
+    out = torch.empty_like(x)
+    L.call("g4_rms", ctx.handle, P(x), P(sc), 5, 1536, C.c_float(1e-6), P(out), 0)
+    ref = mo.rms(x.cpu().numpy(), sc.cpu().numpy(), 1e-6)
+    assert max_rel(out.cpu().numpy(), ref) < 1e-5
+    outb = torch.empty((5, 1536), dtype=torch.bfloat16, device="cuda")
+    L.call("g4_rms", ctx.handle, P(x), None, 5, 1536, C.c_float(1e-6), P(outb), 1)
+    assert max_rel(outb.float().cpu().numpy(), mo.rms(x.cpu().numpy(), None, 1e-6)) < 5e-3
+    y = torch.empty_like(x)
+    L.call("g4_add_scale", ctx.handle, P(x), P(out), C.c_longlong(x.numel()), C.c_float(0.75), P(y))
+    assert torch.allclose(y, (x + out) * 0.75)
+
+
+def test_post_norm_add(ctx):
+    h = torch.randn((3, 1536), device="cuda", generator=g(3))
+    y = torch.randn((3, 1536), device="cuda", generator=g(4)) * 5
+    wp = torch.rand(1536, device="cuda", generator=g(5)) + 0.5
+    wn = torch.rand(1536, device="cuda", generator=g(6)) + 0.5
+    x = torch.empty((3, 1536), dtype=torch.bfloat16, device="cuda")
+    h0 = h.cpu().numpy()
+    L.call("g4_post_norm_add", ctx.handle, P(h), P(y), 1536, P(wp), C.c_float(0.8), P(wn), 3, 1536, C.c_float(1e-6), P(x))
+    hr = (h0 + mo.rms(y.cpu().numpy(), wp.cpu().numpy(), 1e-6)) * np.float32(0.8)
+    assert max_rel(h.cpu().numpy(), hr) < 1e-5
+    assert max_rel(x.float().cpu().numpy(), mo.rms(hr, wn.cpu().numpy(), 1e-6)) < 5e-3
+
+
+@pytest.mark.parametrize("hd,angles,base", [(256, 128, 10000.0), (512, 64, 1000000.0), (64, 32, 10000.0)])
+def test_qkv_post_norm_rope_and_append(ctx, hd, angles, base):
+    H, rows, cap = 8, 3, 40
+    y = torch.randn((rows, (H + 2) * hd), device="cuda", generator=g(hd))
+    qn = torch.rand(hd, device="cuda", generator=g(7)) * 0.5 + 0.2
+    kn = torch.rand(hd, device="cuda", generator=g(8)) * 0.5 + 0.2
+    q = torch.empty((rows, H, hd), dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros((2 * cap, hd), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros((2 * cap, hd), dtype=torch.bfloat16, device="cuda")
+    seq_pos = torch.tensor([0, 21], dtype=torch.int32, device="cuda")
+    rmap = L.G4Rows(seq_pos.data_ptr(), 1, rows, 0)  # sequence 1, positions 21..23
+    L.call("g4_qkv_post", ctx.handle, P(y), (H + 2) * hd, H, hd, 1, P(qn), P(kn), C.c_float(1e-6), angles,
+           C.c_float(base), C.byref(rmap), rows, P(q), P(kc), P(vc), cap)
+    yn = y.cpu().numpy()
+    pos = np.arange(21, 24)
+    qr = mo.norm_rope(yn[:, :H * hd].reshape(rows, H, hd), qn.cpu().numpy(), pos, angles, base, 1e-6)
+    kr = mo.norm_rope(yn[:, H * hd:(H + 1) * hd], kn.cpu().numpy(), pos, angles, base, 1e-6)
+    vr = mo.rms(yn[:, (H + 1) * hd:], None, 1e-6)
+    assert max_rel(q.float().cpu().numpy(), qr) < 5e-3
+    assert max_rel(kc[cap + 21:cap + 24].float().cpu().numpy(), kr) < 5e-3
+    assert max_rel(vc[cap + 21:cap + 24].float().cpu().numpy(), vr) < 5e-3
+    assert float(kc[:cap + 21].abs().sum()) == 0.0  # nothing written outside the three slots
+
+
+def test_gelu_mul_and_gelu_ple(ctx):
+    rows, inter = 4, 6144
+    gu = torch.randn((rows, 2 * inter), device="cuda", generator=g(9)) * 4
+    out = torch.empty((rows, inter), dtype=torch.bfloat16, device="cuda")
+    L.call("g4_gelu_mul", ctx.handle, P(gu), rows, inter, P(out))
+    gn = gu.cpu().numpy()
+    assert max_rel(out.float().cpu().numpy(), mo.gelu(gn[:, :inter]) * gn[:, inter:]) < 5e-3
+    pg = torch.randn((rows, 256), device="cuda", generator=g(10)) * 30  # exercises the +-10 clamp
+    pl = torch.randn((rows, 35, 256), device="cuda", generator=g(11))
+    o2 = torch.empty((rows, 256), dtype=torch.bfloat16, device="cuda")
+    L.call("g4_gelu_ple", ctx.handle, P(pg), P(pl), 7, 35, 256, rows, P(o2))
+    ref = mo.gelu(pg.cpu().numpy()) * pl.cpu().numpy()[:, 7, :]
+    assert max_rel(o2.float().cpu().numpy(), ref) < 5e-3
+
+
+def test_ple_mix(ctx):
+    rows = 3
+    proj = torch.randn((rows, 35 * 256), device="cuda", generator=g(12)) * 10
+    norm = torch.rand(256, device="cuda", generator=g(13)) + 0.5
+    tok = torch.randn((rows, 35 * 256), device="cuda", generator=g(14)) * 0.05
+    out = torch.empty_like(proj)
+    L.call("g4_ple_mix", ctx.handle, P(proj), C.c_float(1 / math.sqrt(1536)), P(norm), P(tok), rows, 35, 256,
+           C.c_float(1e-6), P(out))
+    p = proj.cpu().numpy().reshape(rows, 35, 256) * np.float32(1 / math.sqrt(1536))
+    ref = (mo.rms(p, norm.cpu().numpy(), 1e-6) + tok.cpu().numpy().reshape(rows, 35, 256) * 16) * np.float32(0.7071067811865476)
+    assert max_rel(out.cpu().numpy().reshape(rows, 35, 256), ref) < 1e-5
+
+
+@pytest.mark.parametrize("M", [1, 3, 16, 40])
+def test_dense_head_and_argmax(rt, ctx, M):
+    model = importlib.import_module("gemma4-js_b200.model")
+    V, K = 20000, 1536
+    E = (torch.randn((V, K), device="cuda", generator=g(15)) * 0.05).to(torch.bfloat16)
+    d = model.Dense(ctx, E)
+    x = torch.randn((M, K), device="cuda", generator=g(M)).to(torch.bfloat16)
+    logits = torch.empty((M, V), dtype=torch.float32, device="cuda")
+    L.call("g4_dense_matmul", ctx.handle, d.handle, P(x), M, P(logits))
+    ref = x.float() @ E.float().T
+    assert max_rel(logits.cpu().numpy(), ref.cpu().numpy()) < 1e-4
+    ids = torch.empty(M, dtype=torch.int32, device="cuda")
+    vals = torch.empty(M, dtype=torch.float32, device="cuda")
+    logits[0, 123] = 1e4          # a clear winner, capped to ~30
+    logits[0, 7] = float("nan")  # skipped like the reference's non-finite check
+    L.call("g4_softcap_argmax", ctx.handle, P(logits), M, V, C.c_float(30.0), P(ids), P(vals))
+    capped = torch.tanh(logits / 30) * 30
+    capped = torch.nan_to_num(capped, nan=-float("inf"))
+    assert ids.tolist() == capped.argmax(dim=1).int().tolist()
+    assert abs(float(vals[0]) - 30.0) < 1e-4
+    ctx.check_device()
+
+
+def test_argmax_ties_pick_lowest_index(ctx):
+    logits = torch.zeros((2, 9000), device="cuda")
+    logits[0, [17, 4100, 8999]] = 5.0
+    logits[1, [8999, 300]] = 2.0
+    ids = torch.empty(2, dtype=torch.int32, device="cuda")
+    L.call("g4_softcap_argmax", ctx.handle, P(logits), 2, 9000, C.c_float(30.0), P(ids), None)
+    assert ids.tolist() == [17, 300]
+
+
+def test_embed(ctx):
+    E = (torch.randn((1000, 1536), device="cuda", generator=g(16)) * 0.05).to(torch.bfloat16)
+    ids = torch.tensor([5, 999, 0], dtype=torch.int32, device="cuda")
+    h = torch.empty((3, 1536), device="cuda")
+    x = torch.empty((3, 1536), dtype=torch.bfloat16, device="cuda")
+    L.call("g4_embed", ctx.handle, P(E), 1000, 1536, P(ids), 3, C.c_float(math.sqrt(1536)), P(h), P(x))
+    ref = E[ids.long()].float() * np.float32(math.sqrt(1536))
+    assert torch.equal(h, ref)
+    assert torch.equal(x, ref.to(torch.bfloat16))

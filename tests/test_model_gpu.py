@@ -1,0 +1,140 @@
+"""End-to-end greedy decoding on the GPU (through the C ABI) against the whole-model oracle.
+
+Random-init weights use log-normal embedding row norms (embed_tail) so the greedy
+choice has clear margins; the remaining divergence between two W4A16 implementations
+is bf16-rounding noise of ~1% of the logit range.  `greedy_compare` checks every
+step: a different token is a failure unless the oracle's own top-2 margin at that step
+is inside that noise floor (then both continue from the oracle's token and the step is
+reported as a near tie).
+"""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+model = importlib.import_module("gemma4-js_b200.model")
+mo = importlib.import_module("oracle.model_oracle")
+
+W_KW = dict(embed_sigma=0.03, embed_tail=0.5)
+
+
+def small_cfg(**kw):
+    base = dict(hidden=512, layers=5, vocab=4096, intermediate=1024, intermediate_late=1024, window=16)
+    base.update(kw)
+    return model.ModelConfig().small(**base)
+
+
+def greedy_compare(gpu, orc, prompt, steps, seq=0, noise=0.02):
+    """Prefill + `steps` greedy steps on both; returns (tokens, near_ties, margins)."""
+    g_next = gpu.prefill(seq, prompt)
+    o_next, capped = orc.forward(prompt)
+    toks, ties, margins = [], [], []
+    for step in range(steps + 1):
+        top2 = np.sort(capped)[-2:]
+        margin = float(top2[1] - top2[0])
+        margins.append(margin)
+        if g_next != o_next:
+            assert margin < noise * abs(float(top2[1])), (
+                f"step {step}: GPU picked {g_next}, oracle {o_next} with margin {margin:.4f}")
+            ties.append(step)
+        toks.append(o_next)
+        if step == steps:
+            break
+        ids = torch.tensor([o_next], dtype=torch.int32, device="cuda")
+        g_next = int(gpu.decode_step(ids_dev=ids, batch=1)[0].item()) if seq == 0 else None
+        o_next, capped = orc.forward([o_next])
+    return toks, ties, margins
+
+
+def test_small_model_greedy_32(rt, ctx):
+    cfg = small_cfg()
+    w = model.random_weights(cfg, seed=11, **W_KW)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+    orc = mo.OracleModel(cfg, w, max_seq=64)
+    toks, ties, margins = greedy_compare(gpu, orc, [1, 2, 3, 500, 4000, 7, 9, 11], 32)
+    print("tokens", toks, "near ties", ties, "min margin", min(margins))
+    assert len(toks) == 33 and not ties
+
+
+def test_graph_replay_matches_eager(rt, ctx):
+    cfg = small_cfg()
+    w = model.random_weights(cfg, seed=12, **W_KW)
+    a = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+    b = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+    prompt = [3, 1, 4, 1, 5, 9, 2, 6]
+    ta = [a.prefill(0, prompt)]
+    tb = [b.prefill(0, prompt)]
+    a.buf["next"][0] = ta[0]
+    b.buf["next"][0] = tb[0]
+    for _ in range(20):
+        ta.append(int(a.decode_step(batch=1)[0].item()))
+    b.capture_decode(batch=1)
+    for _ in range(20):
+        tb.append(int(b.replay_decode()[0].item()))
+    torch.cuda.synchronize()
+    assert ta == tb
+    assert int(b.seq_pos[0].item()) == len(prompt) + 20
+
+
+def test_batched_decode_matches_single_sequences(rt, ctx):
+    cfg = small_cfg()
+    w = model.random_weights(cfg, seed=13, **W_KW)
+    prompts = [[1, 2, 3], [400, 401, 402, 403, 404], [7, 7, 7, 7]]
+    B = len(prompts)
+    batch = model.Gemma4Model(ctx, cfg, w, max_batch=B, max_seq=64, max_rows=16)
+    firsts = [batch.prefill(s, p) for s, p in enumerate(prompts)]
+    cur = torch.tensor(firsts, dtype=torch.int32, device="cuda")
+    out_batch = [firsts]
+    for _ in range(12):
+        cur = batch.decode_step(ids_dev=cur, batch=B).clone()
+        out_batch.append(cur.tolist())
+    for s, p in enumerate(prompts):
+        single = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+        t = [single.prefill(0, p)]
+        c = torch.tensor(t, dtype=torch.int32, device="cuda")
+        for _ in range(12):
+            c = single.decode_step(ids_dev=c, batch=1).clone()
+            t.append(int(c[0].item()))
+        assert t == [row[s] for row in out_batch], f"sequence {s}"
+
+
+def test_prefill_through_tcgen05_gemm(rt, ctx):
+    """A 40-token prompt runs every linear through the tcgen05 GEMM (bf16 weight
+    materialisation); the oracle mirrors that for calls of more than 16 rows."""
+    cfg = small_cfg(window=16)
+    w = model.random_weights(cfg, seed=14, **W_KW)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=96, max_rows=64)
+    orc = mo.OracleModel(cfg, w, max_seq=96, gemm_rows=16)
+    prompt = list(np.random.default_rng(5).integers(0, cfg.vocab, 40))
+    toks, ties, margins = greedy_compare(gpu, orc, prompt, 8)
+    print("tokens", toks, "near ties", ties)
+    assert not ties
+
+
+def test_reference_spec_small(rt, ctx):
+    """The checkpoint's own layer spec (KV sharing, hd 512 + rope 1e6/0.25 on global
+    layers, wider MLP late) at small width."""
+    cfg = model.ModelConfig.reference_spec().small(hidden=512, layers=7, vocab=4096, intermediate=1024,
+                                                   intermediate_late=2048, first_shared=5, window=16)
+    w = model.random_weights(cfg, seed=15, **W_KW)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+    orc = mo.OracleModel(cfg, w, max_seq=64)
+    toks, ties, margins = greedy_compare(gpu, orc, [10, 20, 30, 40], 16)
+    print("tokens", toks, "near ties", ties)
+    assert not ties
+
+
+def test_full_size_greedy_32(rt, ctx):
+    """BASELINE config 4's model (35 layers, hidden 1536, MLP 6144, 8q/1kv, hd 256,
+    window 512, PLE 256/layer, vocab 262144 tied), seeded random init: 32 greedy steps
+    must give the oracle's token ids."""
+    cfg = model.ModelConfig()
+    w = model.random_weights(cfg, seed=0, **W_KW)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=128, max_rows=16)
+    orc = mo.OracleModel(cfg, w, max_seq=128)
+    toks, ties, margins = greedy_compare(gpu, orc, [2, 106, 1645, 7, 99, 4242, 262143, 0], 32)
+    print("tokens", toks, "near ties", ties, "min margin", round(min(margins), 4))
+    assert len(toks) == 33 and not ties
