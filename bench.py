@@ -1,10 +1,16 @@
 #!/usr/bin/env python
 """Benchmark of the g4w4 hot path on B200 (one JSON line on rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ple|gemv|attn] [--impl g4|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload serve|decode|ple|gemv|attn|gemm]
+                  [--impl g4|reference]
 
 Workloads (inputs are seeded synthetic data with the configs'
 shapes and value distributions -- the reference publishes no dataset):
+  serve (default) config 5: 256 sequences with 4096-token contexts split over the GPUs
+        as independent replicas, one greedy decode step of all of them per step (one
+        CUDA graph per GPU), token ids all-gathered with NCCL.  Metric: decode tok/s.
+  decode config 4: batch 1, 2048-token prompt (prefill through the tcgen05 GEMM), then
+        greedy decode steps (one CUDA graph per token).
   ple   config 2: PLE W4 gather-dequant of 4096 token ids from the [262144, 8960]
         table into bf16 [4096, 35, 256].  A step is one gather of a fresh id batch.
   gemv  config 1: W4A16 decode GEMV, x [1,1536], W [6144,1536]; a step is one call,
@@ -28,6 +34,8 @@ import sys
 import tempfile
 import time
 from pathlib import Path
+
+import numpy as np
 
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
@@ -394,6 +402,196 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
     }
 
 
+def _decode_model(torch, rt, ctx, batch, max_seq, max_rows, seed=0):
+    model = importlib.import_module("gemma4-js_b200.model")
+    cfg = model.ModelConfig()
+    w = model.random_weights_device(cfg, seed=seed)
+    m = model.Gemma4Model(ctx, cfg, w, max_batch=batch, max_seq=max_seq, max_rows=max_rows)
+    del w
+    torch.cuda.empty_cache()
+    return cfg, m
+
+
+def _attn_roofline(torch, ctx, m, B, peaks, reps=20):
+    """Times the dominant kernel (decode attention over a global layer's cache) alone
+    with CUDA events on its launching stream, using the model's live caches."""
+    lib = importlib.import_module("gemma4-js_b200._lib")
+    Ly = next(L for L in m.layers if L["spec"]["full"] and not L["spec"]["shared"])
+    hd = Ly["spec"]["hd"]
+    rmap = lib.G4Rows(m.seq_pos.data_ptr(), 0, 1, 0)
+    q = (torch.randn((B, 8, hd), device="cuda") * 0.3).to(torch.bfloat16)
+    out = torch.empty_like(q)
+
+    def launch():
+        lib.call("g4_attention_rows", ctx.handle, C.c_void_p(q.data_ptr()), Ly["kv"].handle, B, 8, hd,
+                 C.byref(rmap), m.max_seq, 0, 512, C.c_void_p(out.data_ptr()))
+
+    launch()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        launch()
+    e.record()
+    torch.cuda.synchronize()
+    per = s.elapsed_time(e) / 1e3 / reps
+    keylen = int(m.seq_pos[:B].max().item()) + 1
+    byts = B * keylen * hd * 2 * 2 + 2 * B * 8 * hd * 2
+    gbs = byts / per / 1e9
+    return {"bound": "hbm", "kernel": "attn_decode_kernel (+ combine), global layer", "achieved": round(gbs, 1),
+            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+            "peak_source": peaks["source"], "traffic": TRAFFIC["attn_decode_kernel"], "bytes_per_launch": byts,
+            "us_per_launch": round(per * 1e6, 2)}
+
+
+def run_serve(args, torch, rt, ctx, dist, peaks):
+    """256 sequences with 4096-token contexts, greedy decode; the batch
+    is split across the GPUs as independent replicas; token ids all-gathered with NCCL."""
+    K, W = args.steps, args.warmup
+    B_total, ctx_len = 256, 4096
+    if B_total % dist.world:
+        raise SystemExit(f"256 sequences do not split over {dist.world} GPUs")
+    B = B_total // dist.world
+    max_seq = ctx_len + max(256, W + K + 2)
+    cfg, m = _decode_model(torch, rt, ctx, B, max_seq, B)
+    m.fill_kv_random(ctx_len, seed=dist.rank)
+    g = torch.Generator(device="cuda").manual_seed(1000 + dist.rank)
+    m.buf["next"][:B] = torch.randint(0, cfg.vocab, (B,), device="cuda", generator=g, dtype=torch.int32)
+    m.capture_decode(batch=B)
+    gathered = torch.empty(B_total, dtype=torch.int32, device="cuda")
+
+    def step():
+        nxt = m.replay_decode()
+        if dist.pg:
+            dist.pg.all_gather_into_tensor(gathered, nxt)
+        else:
+            gathered.copy_(nxt)
+
+    n0 = rt.launch_count()
+    for _ in range(W):
+        step()
+    torch.cuda.synchronize()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(K):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = clk.stop()
+    ms = dist.max(s.elapsed_time(e))
+    graph_nodes = rt.launch_count() - n0   # kernels launched eagerly (capture counts once)
+    ctx.check_device()
+    tok_s = B_total * K / (ms / 1e3)
+    # e2e: ids in from pinned host memory, gathered ids out to pinned host memory, every step
+    h_in = torch.randint(0, cfg.vocab, (B,), dtype=torch.int32).pin_memory()
+    h_out = torch.empty(B_total, dtype=torch.int32).pin_memory()
+    e2e_steps = max(3, min(K, 16))
+    dist.barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(e2e_steps):
+        m.buf["next"][:B].copy_(h_in, non_blocking=True)
+        step()
+        h_out.copy_(gathered, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = dist.max(s2.elapsed_time(e2)) / e2e_steps
+    roof = _attn_roofline(torch, ctx, m, B, peaks)
+    line = {
+        "metric": "batched greedy decode throughput (config 5)", "value": round(tok_s, 1), "unit": "tok/s",
+        "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init W4A16 weights, random bf16 K/V for the 4096-token contexts, random ids)",
+        "config": {"workload": "config5_serving", "model": "gemma4-e2b-shaped (35L, hidden 1536, MLP 6144, 8q/1kv, hd 256)",
+                   "global_batch": B_total, "batch_per_gpu": B, "seq_len": ctx_len,
+                   "parallelism": f"replicas x{dist.world}, NCCL all-gather of token ids",
+                   "l2": "per step 1.5 GB of weights + KV of 256 x 4096 tokens (>> 126 MB L2)"},
+        "roofline": roof,
+        "e2e": {"value": round(B_total / (e2e_ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
+                "d2h_bytes_per_step": B_total * 4},
+        "gpu_launches": _graph_kernel_count(m) * K, "clocks": clocks,
+    }
+    if dist.rank == 0 and dist.world == 1:
+        line["cpu_baseline"] = cpu_decode(batch=1, ctx_len=ctx_len)
+    return line
+
+
+def _graph_kernel_count(m):
+    """Kernels of this library per captured decode step (counted while capturing)."""
+    return getattr(m, "graph_kernels", 0)
+
+
+def run_decode(args, torch, rt, ctx, dist, peaks):
+    """batch 1, 2048-token random prompt, then greedy decode."""
+    K, W = args.steps, args.warmup
+    prompt_len = 2048
+    cfg, m = _decode_model(torch, rt, ctx, 1, prompt_len + W + K + 8, prompt_len)
+    ids = np.random.default_rng(dist.rank).integers(0, cfg.vocab, prompt_len)
+    torch.cuda.synchronize()
+    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    first = m.prefill(0, ids)
+    e0.record()
+    torch.cuda.synchronize()
+    prefill_ms = s0.elapsed_time(e0)
+    m.buf["next"][0] = first
+    m.capture_decode(batch=1)
+    for _ in range(W):
+        m.replay_decode()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(K):
+        m.replay_decode()
+    e.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = clk.stop()
+    ms = dist.max(s.elapsed_time(e))
+    ctx.check_device()
+    h_in = torch.tensor([first], dtype=torch.int32).pin_memory()
+    h_out = torch.empty(1, dtype=torch.int32).pin_memory()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    n2 = max(3, min(K, 16))
+    for _ in range(n2):
+        m.buf["next"][:1].copy_(h_in, non_blocking=True)
+        nxt = m.replay_decode()
+        h_out.copy_(nxt, non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = dist.max(s2.elapsed_time(e2)) / n2
+    w4_bytes = sum(L[n].in_dim * L[n].out_dim * 9 // 16 for L in m.layers for n in ("qkv", "o", "gu", "down", "pg", "pp"))
+    per_tok = w4_bytes + m.top.in_dim * m.top.out_dim * 9 // 16 + cfg.vocab * cfg.hidden * 2
+    tok_s = K / (ms / 1e3) * dist.world
+    gbs = per_tok / (ms / 1e3 / K) / 1e9
+    line = {
+        "metric": "greedy decode throughput, batch 1 (config 4)", "value": round(tok_s, 1), "unit": "tok/s",
+        "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompt)",
+        "config": {"workload": "config4_decode_b1", "prompt": prompt_len, "prefill_ms": round(prefill_ms, 2),
+                   "l2": "1.5 GB of weights per token (>> L2)"},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + head bytes per token)",
+                     "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"], "traffic": None,
+                     "bytes_per_launch": per_tok},
+        "e2e": {"value": round(1 / (e2e_ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
+        "gpu_launches": _graph_kernel_count(m) * K, "clocks": clocks,
+    }
+    if dist.rank == 0 and dist.world == 1:
+        line["cpu_baseline"] = cpu_decode(batch=1, ctx_len=prompt_len)
+    return line
+
+
 # ------------------------------------------------------------ CPU baseline --
 def native_oracle():
     """The oracle's C restatement built for this host's CPU (-march=native)."""
@@ -423,6 +621,40 @@ def cpu_ple(sample_s: float, threads: int, vocab_sample: int = 8192):
     return {"value": round(PLE_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{n} x 4096-id gathers (bf16 out) over a {vocab_sample}-row host table, {dt:.1f} s",
             "calls_per_s": round(n / dt, 4)}
+
+
+def cpu_decode(batch: int, ctx_len: int, threads: int = 1, model_layers: int = 35):
+    """Times one greedy decode step of the restated TFJS path on the host: every linear of
+    the 35 layers dequantised on each call and multiplied in f32 (official-quantized-linear.js:82-128),
+    attention over ctx_len keys per layer, the f32 tied head over 262144 rows."""
+    import numpy as np
+    oracle, L = native_oracle()
+    rng = np.random.default_rng(0)
+    shapes = {"qkv": (2560, 1536), "o": (1536, 2048), "gu": (12288, 1536), "down": (1536, 6144), "pg": (256, 1536),
+              "pp": (1536, 256), "top": (8960, 1536)}
+    W = {}
+    for k, (n, kk) in shapes.items():
+        W[k] = (rng.integers(0, 2**32, size=(n, kk // 8), dtype=np.uint64).astype(np.uint32).view(np.int32),
+                oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.02, (n, kk // 32))).astype(np.float32)))
+    head = rng.standard_normal((262144, 1536)).astype(np.float32) * 0.05
+    kc = rng.standard_normal((ctx_len + 1, 256)).astype(np.float32)
+    q = rng.standard_normal((batch, 8, 256)).astype(np.float32)
+    x = {k: rng.standard_normal((batch, kk)).astype(np.float32) for k, (n, kk) in shapes.items()}
+    t0 = time.perf_counter()
+    oracle.linear_w4a16(x["top"], *W["top"], nthreads=threads, L=L)
+    for layer in range(model_layers):
+        for k in ("qkv", "o", "gu", "down", "pg", "pp"):
+            oracle.linear_w4a16(x[k], *W[k], nthreads=threads, L=L)
+        full = (layer + 1) % 5 == 0
+        keys = ctx_len + 1 if full else min(ctx_len + 1, 512)
+        for b in range(batch):
+            oracle.attention(q[b:b + 1], kc[:keys], kc[:keys], keys - 1, not full, 512)
+    logits = x["top"][:, :1536] @ head.T
+    dt = time.perf_counter() - t0
+    del logits
+    return {"value": round(batch / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"one decode step of {batch} sequence(s) at context {ctx_len}: {model_layers} layers x 6 W4A16 linears "
+                      f"(dequantised per call) + attention + f32 tied head, {dt:.1f} s"}
 
 
 def run_reference(args, dist):
@@ -463,7 +695,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="ple", choices=["ple", "gemv", "attn", "gemm"])
+    ap.add_argument("--workload", default="serve", choices=["ple", "gemv", "attn", "gemm", "decode", "serve"])
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--vocab", type=int, default=262144, help="ple: table rows (smaller for ncu captures)")
@@ -482,7 +714,8 @@ def main():
     rt = importlib.import_module("gemma4-js_b200.runtime")
     ctx = rt.Context(dist.local)
     peaks = load_peaks()
-    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn, "gemm": run_gemm}[args.workload]
+    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn, "gemm": run_gemm, "decode": run_decode,
+          "serve": run_serve}[args.workload]
     line = fn(args, torch, rt, ctx, dist, peaks)
     if dist.rank == 0:
         print(json.dumps(line), flush=True)

@@ -18,9 +18,12 @@
 //               lane quarter, convert, store.
 // Every wait is bounded; a timeout raises the context's device error word and the
 // kernel winds down (TMEM is always freed).
+#include <cooperative_groups.h>
 #include <stdio.h>
 
 #include "g4_linear.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
@@ -36,6 +39,7 @@ constexpr int kRawBytes = (BN / 16) * 512;      // 8 KB
 constexpr int kScBytes = (BN / 16) * 64;        // 1 KB
 constexpr int kBBytes = BN * BK * 2;            // 32 KB
 constexpr int kTmemCols = 256;
+constexpr int kRedPitch = BN + 4;  // floats per row of a parked partial tile (bank-skewed)
 
 // Shared-memory plan.  W4 path: [A x4][B x2][raw x4][scales x4][barriers];
 // bf16 path (B loaded by TMA, no dequant): [A x4][B x4][barriers].
@@ -103,6 +107,7 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN 
 struct GemmParams {
     void* y;
     int M, N, K, ldy, y_f32, ktiles;
+    int ksplit;  // CTAs of a cluster that share one output tile, each over 1/ksplit of K
     uint32_t* err;
 };
 
@@ -125,8 +130,12 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mb = blockIdx.x, nb = blockIdx.y;
-    const int KT = p.ktiles;
+    const int S = p.ksplit;
+    const int mb = blockIdx.x / S, kslice = blockIdx.x % S, nb = blockIdx.y;
+    // this CTA's k-tiles: [k0, k0 + KT)
+    const int per = (p.ktiles + S - 1) / S;
+    const int k0 = kslice * per;
+    const int KT = max(0, min(p.ktiles, k0 + per) - k0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -153,9 +162,9 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             prefetch_tensor_map(&wmap);
             if (kW4) prefetch_tensor_map(&smap);
             int issued = 0;
-            for (int kt = 0; kt < KT; ++kt) {
-                const int s = kt % kStages;
-                if (kt >= kStages && !mbar_wait(&load_empty[s], ((kt / kStages) - 1) & 1, p.err)) break;
+            for (int i = 0; i < KT; ++i) {
+                const int s = i % kStages, kt = k0 + i;
+                if (i >= kStages && !mbar_wait(&load_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
                 if constexpr (kW4) {
                     mbar_arrive_expect_tx(&load_full[s], kABytes + kRawBytes + kScBytes);
                     tma_load_2d(smem + kOffA + s * kABytes, &xmap, &load_full[s], kt * BK, mb * BM);
@@ -166,20 +175,20 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                     tma_load_2d(smem + kOffA + s * kABytes, &xmap, &load_full[s], kt * BK, mb * BM);
                     tma_load_2d(smem + kOffB + s * kBBytes, &wmap, &load_full[s], kt * BK, nb * BN);
                 }
-                issued = kt + 1;
+                issued = i + 1;
             }
             // Drain: our copies must land before the CTA can exit.
-            for (int kt = issued > kStages ? issued - kStages : 0; kt < issued; ++kt)
-                mbar_wait(&load_full[kt % kStages], (kt / kStages) & 1, p.err);
+            for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+                mbar_wait(&load_full[i % kStages], (i / kStages) & 1, p.err);
         }
     } else if (warp == 1) {
         // -------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             bool ok = true;
-            for (int kt = 0; kt < KT && ok; ++kt) {
-                const int s = kt % kStages, sb = kW4 ? kt % kBStages : s;
-                ok = mbar_wait(&load_full[s], (kt / kStages) & 1, p.err);
-                if (kW4 && ok) ok = mbar_wait(&b_full[sb], (kt / kBStages) & 1, p.err);
+            for (int i = 0; i < KT && ok; ++i) {
+                const int s = i % kStages, sb = kW4 ? i % kBStages : s;
+                ok = mbar_wait(&load_full[s], (i / kStages) & 1, p.err);
+                if (kW4 && ok) ok = mbar_wait(&b_full[sb], (i / kBStages) & 1, p.err);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t a0 = smem_u32(smem + kOffA + s * kABytes);
@@ -187,7 +196,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
 #pragma unroll
                 for (int ks = 0; ks < BK / 16; ++ks)
                     tc_mma_bf16(tmem, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), kIdesc,
-                                (kt > 0 || ks > 0) ? 1u : 0u);
+                                (i > 0 || ks > 0) ? 1u : 0u);
                 tc_commit(&load_empty[s]);        // X (and bf16 B) stage consumed
                 if (kW4) tc_commit(&b_empty[sb]);  // dequantised B stage consumed
             }
@@ -198,10 +207,10 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         const int wd = warp - 2;  // 0..7: n-tiles 2wd, 2wd+1 of this CTA's 16
         const int g = lane >> 2, t = lane & 3;
         bool ok = true;
-        for (int kt = 0; kW4 && kt < KT && ok; ++kt) {
-            const int s = kt % kStages, sb = kt % kBStages;
-            ok = mbar_wait_warp(&load_full[s], (kt / kStages) & 1, p.err);
-            if (ok && kt >= kBStages) ok = mbar_wait_warp(&b_empty[sb], ((kt / kBStages) - 1) & 1, p.err);
+        for (int i = 0; kW4 && i < KT && ok; ++i) {
+            const int s = i % kStages, sb = i % kBStages;
+            ok = mbar_wait_warp(&load_full[s], (i / kStages) & 1, p.err);
+            if (ok && i >= kBStages) ok = mbar_wait_warp(&b_empty[sb], ((i / kBStages) - 1) & 1, p.err);
             if (!ok) break;
             const uint8_t* raw = smem + kOffRaw + s * kRawBytes;
             const uint8_t* sc = smem + kOffSc + s * kScBytes;
@@ -243,7 +252,28 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             }
         }
         // ------------------------------------------------------------- epilogue
-        if (mbar_wait_warp(acc_full, 0, p.err)) {
+        if (S > 1) {
+            // Split K: park this CTA's FP32 partial tile in its (now idle) shared memory;
+            // the cluster sums the S partials below.
+            if (KT == 0) {  // an empty K slice contributes zeros (its accumulator was never written)
+                const int quarter = warp & 3, col0 = (warp < 6) ? 0 : 128;
+                float* red = reinterpret_cast<float*>(smem) + (quarter * 32 + lane) * kRedPitch + col0;
+                for (int c = 0; c < 128; c += 4) *reinterpret_cast<uint4*>(red + c) = make_uint4(0, 0, 0, 0);
+            } else if (mbar_wait_warp(acc_full, 0, p.err)) {
+                tc_fence_after();
+                const int quarter = warp & 3, col0 = (warp < 6) ? 0 : 128;
+                float* red = reinterpret_cast<float*>(smem) + (quarter * 32 + lane) * kRedPitch + col0;
+#pragma unroll 1
+                for (int c = 0; c < 128; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c), r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<uint4*>(red + c + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+                }
+            }
+        } else if (mbar_wait_warp(acc_full, 0, p.err)) {
             tc_fence_after();
             const int quarter = warp & 3;          // TMEM lanes 32*quarter .. +31
             const int col0 = (warp < 6) ? 0 : 128; // two warps per lane quarter
@@ -290,6 +320,40 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             }
         }
     }
+    if (S > 1) {
+        // Deterministic cluster reduction through distributed shared memory: CTA `kslice`
+        // sums rows kslice, kslice + S, ... of the tile over ranks 0..S-1 in order.
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (warp >= 2) {
+            const int t = threadIdx.x - 64;              // 0..255
+            const int c4 = (t & 63) * 4, rsub = t >> 6;  // 4 columns, one of 4 row phases
+            const int n = nb * BN + c4;
+            for (int rr = kslice + rsub * S; rr < BM; rr += 4 * S) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+                for (int r = 0; r < S; ++r) {
+                    const float4 v = *reinterpret_cast<const float4*>(
+                        cluster.map_shared_rank(reinterpret_cast<float*>(smem), r) + rr * kRedPitch + c4);
+                    acc.x += v.x;
+                    acc.y += v.y;
+                    acc.z += v.z;
+                    acc.w += v.w;
+                }
+                const int row = mb * BM + rr;
+                if (row < p.M && n < p.N) {  // N % 8 == 0: the 4 columns are all in or all out
+                    if (p.y_f32) {
+                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)row * p.ldy + n) = acc;
+                    } else {
+                        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+                        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)row * p.ldy + n) =
+                            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+                    }
+                }
+            }
+        }
+        cluster.sync();  // peers may still be reading this CTA's partial
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
@@ -301,6 +365,41 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
 }  // namespace
 
 namespace g4 {
+
+// Grid: one CTA per 128 x 256 output tile; when that leaves the GPU under-filled, the K
+// range of each tile is split over a cluster of up to 8 CTAs (>= 4 k-tiles each) and
+// the partials are summed through distributed shared memory.
+template <bool kW4>
+g4_status launch_tiles(g4_ctx* ctx, const CUtensorMap& xmap, const CUtensorMap& wmap, const CUtensorMap& smap,
+                       GemmParams p) {
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<kW4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           GemmSmem<kW4>::kBytes));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    const int mt = (p.M + BM - 1) / BM, nt = (p.N + BN - 1) / BN;
+    if (nt > 65535) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: N=%d too large", p.N);
+    int S = 1;
+    while (S < 8 && mt * nt * (S + 1) <= ctx->num_sms && p.ktiles / (S + 1) >= 4) ++S;
+    p.ksplit = S;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(mt * S, nt, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = GemmSmem<kW4>::kBytes;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = S;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<kW4>, xmap, wmap, smap, p);
+    if (e != cudaSuccess) return cuda_error(e, kW4 ? "gemm_tcgen05_kernel<W4>" : "gemm_tcgen05_kernel<bf16>");
+    count_launch();
+    return G4_OK;
+}
 
 bool gemm_supported(const g4_linear* lin, int M) {
     // row pitches of X (K bf16) and Y (N values) must allow 16-byte vector access
@@ -314,12 +413,6 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
                                         (uint64_t)L.K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    static std::atomic<uint64_t> attr_set{0};
-    if (!(attr_set.load() & (1ull << ctx->device))) {
-        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           GemmSmem<true>::kBytes));
-        attr_set.fetch_or(1ull << ctx->device);
-    }
     GemmParams p{};
     p.y = y;
     p.M = M;
@@ -329,11 +422,7 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     p.y_f32 = y_f32;
     p.ktiles = L.Kc;
     p.err = ctx->d_err;
-    const dim3 grid((M + BM - 1) / BM, (L.N + BN - 1) / BN);
-    if (grid.y > 65535) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: N=%d too large", L.N);
-    gemm_tcgen05_kernel<true><<<grid, kThreads, GemmSmem<true>::kBytes, ctx->stream>>>(xmap, lin->wmap, lin->smap, p);
-    G4_CHECK_LAUNCH("gemm_tcgen05_kernel<W4>");
-    return G4_OK;
+    return launch_tiles<true>(ctx, xmap, lin->wmap, lin->smap, p);
 }
 
 g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, const uint16_t* x, int M,
@@ -343,12 +432,6 @@ g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, c
     g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), K, M,
                                         (uint64_t)K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    static std::atomic<uint64_t> attr_set{0};
-    if (!(attr_set.load() & (1ull << ctx->device))) {
-        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_tcgen05_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           GemmSmem<false>::kBytes));
-        attr_set.fetch_or(1ull << ctx->device);
-    }
     GemmParams p{};
     p.y = y;
     p.M = M;
@@ -358,11 +441,7 @@ g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, c
     p.y_f32 = 1;
     p.ktiles = (K + BK - 1) / BK;
     p.err = ctx->d_err;
-    const dim3 grid((M + BM - 1) / BM, (N + BN - 1) / BN);
-    if (grid.y > 65535) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 bf16 GEMM: N=%d too large", N);
-    gemm_tcgen05_kernel<false><<<grid, kThreads, GemmSmem<false>::kBytes, ctx->stream>>>(xmap, bmap, bmap, p);
-    G4_CHECK_LAUNCH("gemm_tcgen05_kernel<bf16>");
-    return G4_OK;
+    return launch_tiles<false>(ctx, xmap, bmap, bmap, p);
 }
 
 g4_status make_linear_maps(g4_linear* lin) {

@@ -78,8 +78,17 @@ class ModelConfig:
 
 
 # ----------------------------------------------------------------- weights ---
-def _w4(rng, n, k, sigma):
-    packed = rng.integers(0, 2**32, size=(n, k // 8), dtype=np.uint64).astype(np.uint32).view(np.int32)
+def _w4(rng, n, k, sigma, symmetric=True):
+    """Packed int32 [n, k/8] + bf16 scales [n, k/32].  symmetric: q uniform in [-7, 7]
+    (nibbles 1..15, zero mean); otherwise uniform over all 16 nibbles ([-8, 7])."""
+    if symmetric:
+        nib = rng.integers(1, 16, size=(n, k), dtype=np.uint8).astype(np.uint32)
+        words = np.zeros((n, k // 8), np.uint32)
+        for j in range(8):
+            words |= nib[:, j::8] << np.uint32(4 * j)
+        packed = words.view(np.int32)
+    else:
+        packed = rng.integers(0, 2**32, size=(n, k // 8), dtype=np.uint64).astype(np.uint32).view(np.int32)
     s = np.abs(rng.standard_normal((n, k // 32), dtype=np.float32)) * np.float32(sigma)
     return packed, _bf16_bits(s)
 
@@ -94,7 +103,8 @@ def _norm(rng, n, center=1.0, spread=0.1):
 
 
 def random_weights(cfg: ModelConfig, seed: int = 0, sigma: float = 0.02, embed_sigma: float = 0.05,
-                   qk_norm: float = 0.3, embed_tail: float = 0.0) -> dict:
+                   qk_norm: float = 0.3, embed_tail: float = 0.0, post_norm: float = 1.0,
+                   ple_post_norm: float | None = None, skip: tuple[float, float] = (0.5, 1.0)) -> dict:
     """Seeded random weights of the architecture on the host (numpy), in the
     checkpoint's formats: W4 linears as compressed-tensors packed int32 + bf16 scales,
     the tied embedding bf16, the PLE table as the W4 shard format, norms f32."""
@@ -112,11 +122,13 @@ def random_weights(cfg: ModelConfig, seed: int = 0, sigma: float = 0.02, embed_s
         lw["down"] = _w4(rng, H, inter, sigma)
         lw["pg"] = _w4(rng, P, H, sigma)
         lw["pp"] = _w4(rng, H, P, sigma)
-        for n in ("n_in", "n_pa", "n_pf", "n_pff", "n_pple"):
+        for n in ("n_in", "n_pf"):
             lw[n] = _norm(rng, H)
+        for n in ("n_pa", "n_pff", "n_pple"):   # scale of each residual update
+            lw[n] = _norm(rng, H, post_norm if n != "n_pple" or ple_post_norm is None else ple_post_norm)
         lw["qn"] = _norm(rng, hd, qk_norm)
         lw["kn"] = _norm(rng, hd, qk_norm)
-        lw["skip"] = float(rng.uniform(0.5, 1.0))
+        lw["skip"] = float(rng.uniform(*skip))
         w["layers"].append(lw)
     w["top"] = _w4(rng, L * P, H, sigma)
     w["ple_norm"] = _norm(rng, P)
@@ -364,17 +376,47 @@ class Gemma4Model:
         stream = torch.cuda.Stream(self.dev)
         g = torch.cuda.CUDAGraph()
         old = self.ctx.stream
+        from .runtime import launch_count
+        n0 = launch_count()
         with torch.cuda.stream(stream):
             self.ctx.set_stream(stream)
             with torch.cuda.graph(g, stream=stream):
                 self.decode_step(batch=B)
         self.ctx.set_stream(old)
+        self.graph_kernels = launch_count() - n0   # libg4w4 kernels per replayed step
         self.graph, self.graph_stream, self.graph_batch = g, stream, B
         return g
 
     def replay_decode(self):
         self.graph.replay()
         return self.buf["next"][: self.graph_batch]
+
+    def fill_kv_random(self, length: int, seed: int = 0, nseq: int | None = None):
+        """Synthetic context for benchmarks: K/V of positions [0, length) of every
+        sequence <- random bf16 (K ~ N(0, 0.3^2), V ~ N(0, 1), the scale of normed
+        keys and values), seq_pos <- length.  Decode cost does not depend on the values."""
+        nseq = nseq or self.max_batch
+        if length > self.max_seq:
+            raise G4Error(-6, f"KV cache capacity {self.max_seq} exceeded")
+        g = torch.Generator(device=self.dev).manual_seed(seed)
+        cudart = C.CDLL("libcudart.so.12")
+        cudart.cudaMemcpy2DAsync.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t,
+                                             C.c_size_t, C.c_int, C.c_void_p]
+        stream = C.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+        for Ly in self.layers:
+            if Ly["spec"]["shared"]:
+                continue
+            hd = Ly["spec"]["hd"]
+            kp, vp = C.c_void_p(), C.c_void_p()
+            call("g4_kv_buffers", Ly["kv"].handle, C.byref(kp), C.byref(vp))
+            for dst, sd in ((kp, 0.3), (vp, 1.0)):
+                src = (torch.randn((nseq, length, hd), device=self.dev, generator=g) * sd).to(torch.bfloat16)
+                rc = cudart.cudaMemcpy2DAsync(dst, self.max_seq * hd * 2, C.c_void_p(src.data_ptr()), length * hd * 2,
+                                              length * hd * 2, nseq, 3, stream)
+                if rc != 0:
+                    raise G4Error(-3, f"cudaMemcpy2DAsync failed ({rc})")
+                torch.cuda.current_stream(self.dev).synchronize()
+        self.seq_pos[:nseq] = length
 
     def close(self):
         self.graph = None
