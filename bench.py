@@ -458,14 +458,12 @@ def run_serve(args, torch, rt, ctx, dist, peaks):
     g = torch.Generator(device="cuda").manual_seed(1000 + dist.rank)
     m.buf["next"][:B] = torch.randint(0, cfg.vocab, (B,), device="cuda", generator=g, dtype=torch.int32)
     m.capture_decode(batch=B)
-    gathered = torch.empty(B_total, dtype=torch.int32, device="cuda")
+    serving = importlib.import_module("gemma4-js_b200.serving")
+    tg = serving.TokenGather(dist.pg, B_total, "cuda")
+    gathered = tg.out
 
     def step():
-        nxt = m.replay_decode()
-        if dist.pg:
-            dist.pg.all_gather_into_tensor(gathered, nxt)
-        else:
-            gathered.copy_(nxt)
+        tg.gather(m.replay_decode())
 
     n0 = rt.launch_count()
     for _ in range(W):

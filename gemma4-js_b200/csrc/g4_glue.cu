@@ -76,31 +76,39 @@ __global__ void add_scale_kernel(const float* __restrict__ a, const float* __res
 
 // RMS_SHADER + ADD_SCALE (+ the next RMS_SHADER) of one residual update:
 //   h = (h + rms(y) * w_post) * skip;  x = bf16(w_next ? rms(h) * w_next : h)
-__global__ void __launch_bounds__(kRowThreads) post_norm_add_kernel(float* __restrict__ h, const float* __restrict__ y,
-                                                                    int ldy, const float* __restrict__ w_post,
-                                                                    float skip, const float* __restrict__ w_next,
-                                                                    int width, float eps, uint16_t* __restrict__ x_out) {
+// One CTA per row, one float4 of the row per thread, kept in registers across the
+// two reductions (width % 4 == 0, width <= 4096).
+__global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__ h, const float* __restrict__ y,
+                                                             int ldy, const float* __restrict__ w_post, float skip,
+                                                             const float* __restrict__ w_next, int width, float eps,
+                                                             uint16_t* __restrict__ x_out) {
     __shared__ float red[32];
-    const int r = blockIdx.x;
-    float* hr = h + (size_t)r * width;
-    const float* yr = y + (size_t)r * ldy;
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < width; i += blockDim.x) ss += yr[i] * yr[i];
-    const float inv = rsqrtf(block_sum(ss, red) / (float)width + eps);
-    float ss2 = 0.f;
-    for (int i = threadIdx.x; i < width; i += blockDim.x) {
-        const float v = (hr[i] + yr[i] * inv * w_post[i]) * skip;
-        hr[i] = v;
-        ss2 += v * v;
+    const int r = blockIdx.x, i = threadIdx.x * 4;
+    const bool on = i < width;
+    float4 yv = make_float4(0.f, 0.f, 0.f, 0.f), hv = yv, wp = yv;
+    if (on) {
+        yv = *reinterpret_cast<const float4*>(y + (size_t)r * ldy + i);
+        hv = *reinterpret_cast<const float4*>(h + (size_t)r * width + i);
+        wp = *reinterpret_cast<const float4*>(w_post + i);
     }
+    const float inv = rsqrtf(block_sum(yv.x * yv.x + yv.y * yv.y + yv.z * yv.z + yv.w * yv.w, red) / (float)width + eps);
+    hv.x = (hv.x + yv.x * inv * wp.x) * skip;
+    hv.y = (hv.y + yv.y * inv * wp.y) * skip;
+    hv.z = (hv.z + yv.z * inv * wp.z) * skip;
+    hv.w = (hv.w + yv.w * inv * wp.w) * skip;
+    if (on) *reinterpret_cast<float4*>(h + (size_t)r * width + i) = hv;
+    if (!x_out) return;
+    float4 o = hv;
     if (w_next) {
-        const float inv2 = rsqrtf(block_sum(ss2, red) / (float)width + eps);
-        for (int i = threadIdx.x; i < width; i += blockDim.x)
-            x_out[(size_t)r * width + i] = (uint16_t)f32_to_bf16_bits(hr[i] * inv2 * w_next[i]);
-    } else if (x_out) {
-        for (int i = threadIdx.x; i < width; i += blockDim.x)
-            x_out[(size_t)r * width + i] = (uint16_t)f32_to_bf16_bits(hr[i]);
+        const float inv2 =
+            rsqrtf(block_sum(hv.x * hv.x + hv.y * hv.y + hv.z * hv.z + hv.w * hv.w, red) / (float)width + eps);
+        if (on) {
+            const float4 wn = *reinterpret_cast<const float4*>(w_next + i);
+            o = make_float4(hv.x * inv2 * wn.x, hv.y * inv2 * wn.y, hv.z * inv2 * wn.z, hv.w * inv2 * wn.w);
+        }
     }
+    if (on)
+        *reinterpret_cast<uint2*>(x_out + (size_t)r * width + i) = make_uint2(pack_bf16x2_bits(o.x, o.y), pack_bf16x2_bits(o.z, o.w));
 }
 
 // Token embedding rows (bf16) times `scale` (SCALE shader with sqrt(hidden)), f32
@@ -159,13 +167,19 @@ __global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int
     dst[i + half] = (uint16_t)f32_to_bf16_bits(o1);
 }
 
-// GELU_MUL over a fused [gate | up] projection: out = bf16(gelu(gate) * up).
-__global__ void gelu_mul_kernel(const float* __restrict__ gu, int inter, long long n, uint16_t* __restrict__ out) {
+// GELU_MUL over a fused [gate | up] projection: out = bf16(gelu(gate) * up), four
+// columns per thread (inter % 4 == 0).
+__global__ void gelu_mul_kernel(const float* __restrict__ gu, int inter, long long n4, uint16_t* __restrict__ out) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= n) return;
-    const long long r = i / inter, c = i - r * inter;
+    if (i >= n4) return;
+    const int q = inter >> 2;
+    const long long r = i / q, c = (i - r * q) * 4;
     const float* row = gu + r * 2 * inter;
-    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(row[c]) * row[inter + c]);
+    const float4 g = *reinterpret_cast<const float4*>(row + c);
+    const float4 u = *reinterpret_cast<const float4*>(row + inter + c);
+    *reinterpret_cast<uint2*>(out + r * inter + c) =
+        make_uint2(pack_bf16x2_bits(gelu_ref(g.x) * u.x, gelu_ref(g.y) * u.y),
+                   pack_bf16x2_bits(gelu_ref(g.z) * u.z, gelu_ref(g.w) * u.w));
 }
 
 // GELU_PLE: out = bf16(gelu(gate) * per_layer[row, layer, :]).
@@ -284,9 +298,12 @@ g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const
     g4_status st = g4::use_device(ctx);
     if (st) return st;
     if (rows < 0 || width <= 0 || !h || !y || !w_post) return g4::set_error(G4_ERR_INVALID, "g4_post_norm_add: bad arguments");
+    if (width % 4 != 0 || width > 4096 || ldy % 4 != 0)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_post_norm_add: width %d / ldy %d (multiples of 4, width <= 4096)", width, ldy);
     if (rows == 0) return G4_OK;
-    post_norm_add_kernel<<<rows, kRowThreads, 0, ctx->stream>>>(h, y, ldy, w_post, skip, w_next, width, eps,
-                                                                static_cast<uint16_t*>(x_out_bf16));
+    const int threads = ((width / 4 + 31) / 32) * 32;
+    post_norm_add_kernel<<<rows, threads, 0, ctx->stream>>>(h, y, ldy, w_post, skip, w_next, width, eps,
+                                                            static_cast<uint16_t*>(x_out_bf16));
     G4_CHECK_LAUNCH("post_norm_add_kernel");
     return G4_OK;
 }
@@ -325,9 +342,10 @@ g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, vo
     g4_status st = g4::use_device(ctx);
     if (st) return st;
     if (rows < 0 || inter <= 0 || !gate_up || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_gelu_mul: bad arguments");
-    const long long n = (long long)rows * inter;
-    if (n == 0) return G4_OK;
-    gelu_mul_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(gate_up, inter, n, static_cast<uint16_t*>(out_bf16));
+    if (inter % 4 != 0) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_gelu_mul: inter %d (multiple of 4)", inter);
+    const long long n4 = (long long)rows * inter / 4;
+    if (n4 == 0) return G4_OK;
+    gelu_mul_kernel<<<blocks_for(n4, 256), 256, 0, ctx->stream>>>(gate_up, inter, n4, static_cast<uint16_t*>(out_bf16));
     G4_CHECK_LAUNCH("gelu_mul_kernel");
     return G4_OK;
 }

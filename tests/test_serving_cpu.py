@@ -1,0 +1,100 @@
+"""CPU tests of the replica serving logic: partitioning, the token-id gather over a
+world-size-2 gloo group, and failure detection when a rank dies (no GPU involved)."""
+import importlib
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+serving = importlib.import_module("gemma4-js_b200.serving")
+
+
+def test_partition_is_contiguous_and_complete():
+    for total in (0, 1, 7, 256):
+        for world in (1, 2, 3, 4, 8):
+            spans = [serving.partition(total, world, r) for r in range(world)]
+            assert sum(c for _, c in spans) == total
+            pos = 0
+            for s, c in spans:
+                assert s == pos
+                pos += c
+            assert max(c for _, c in spans) - min(c for _, c in spans) <= 1
+    assert serving.partition(256, 8, 3) == (96, 32)
+    with pytest.raises(ValueError):
+        serving.partition(4, 2, 2)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, mode, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    try:
+        dist = serving.init_process_group("gloo", timeout_s=5.0)
+        total = 7
+        start, count = serving.partition(total, world, rank)
+        g = serving.TokenGather(dist, total, "cpu")
+        if mode == "ok":
+            for step in range(3):
+                local = torch.arange(start, start + count, dtype=torch.int32) * 10 + step
+                out = g.gather(local)
+                q.put((rank, step, out.tolist()))
+            dist.barrier()
+            dist.destroy_process_group()
+        else:  # rank 1 leaves between steps; rank 0 must get an error, not hang
+            local = torch.arange(start, start + count, dtype=torch.int32)
+            g.gather(local)
+            if rank == 1:
+                q.put((rank, "left", None))
+                os._exit(0)
+            t0 = time.time()
+            try:
+                g.gather(local)
+                q.put((rank, "no-error", time.time() - t0))
+            except Exception as e:  # the process group reports the dead peer
+                q.put((rank, "error", time.time() - t0))
+            os._exit(0)
+    except Exception as e:
+        q.put((rank, "exception", repr(e)))
+
+
+def _run(mode, world=2, wait=60):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(wait)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    return out
+
+
+def test_token_gather_two_ranks():
+    res = _run("ok")
+    got = {(r, s): v for r, s, v in res}
+    for step in range(3):
+        expect = [i * 10 + step for i in range(7)]
+        assert got[(0, step)] == expect
+        assert got[(1, step)] == expect
+
+
+def test_dead_rank_surfaces_as_an_error():
+    res = _run("dead")
+    r0 = [x for x in res if x[0] == 0]
+    assert r0 and r0[0][1] == "error", res
+    assert r0[0][2] < 30.0  # bounded by the process-group timeout, not a hang
