@@ -345,12 +345,19 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
     """M in {16,128,512,2048} x (K,N) in {(1536,6144), (6144,1536), (1536,262144)}."""
     lib = importlib.import_module("gemma4-js_b200._lib").load()
     K_steps, W = args.steps, args.warmup
+    ctx.set_pdl(True)  # back-to-back launches overlap as they do inside a decode step
     gen = torch.Generator(device="cuda").manual_seed(0)
     points, clk = [], ClockSampler(dist.local)
     n0 = rt.launch_count()
     clk.start()
     tot_flop, tot_s = 0.0, 0.0
-    for (Kd, N) in [(1536, 6144), (6144, 1536), (1536, 262144)]:
+    shapes = [(1536, 6144), (6144, 1536), (1536, 262144)]
+    ms_list = (16, 128, 512, 2048)
+    if args.gemm_shapes:  # "M1,M2:KxN,KxN" e.g. "128,256:1536x2560,6144x1536"
+        mpart, spart = args.gemm_shapes.split(":")
+        ms_list = tuple(int(m) for m in mpart.split(","))
+        shapes = [tuple(int(v) for v in sh.split("x")) for sh in spart.split(",")]
+    for (Kd, N) in shapes:
         wbytes = N * Kd // 2 + N * Kd // 16
         copies = max(1, min(32, (256 << 20) // wbytes + 1))   # > 126 MB of weights per rotation
         lins = []
@@ -359,13 +366,13 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
             sc = torch.randn((N, Kd // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
             lins.append(rt.W4Linear(ctx, packed, sc))
             del packed, sc
-        for M in (16, 128, 512, 2048):
+        for M in ms_list:
             x = torch.randn((M, Kd), device="cuda", generator=gen).to(torch.bfloat16)
             y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
 
             def launch(i, M=M, x=x, y=y):
-                st = lib.g4_linear_w4a16(ctx.handle, lins[i % copies].handle, C.c_void_p(x.data_ptr()), M,
-                                         C.c_void_p(y.data_ptr()), 1)
+                st = lib.g4_linear_w4a16_impl(ctx.handle, lins[i % copies].handle, C.c_void_p(x.data_ptr()), M,
+                                              C.c_void_p(y.data_ptr()), 1, args.gemm_impl)
                 if st:
                     raise RuntimeError(lib.g4_last_error_string())
 
@@ -377,7 +384,7 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
             ideal = max(flop / (peaks["bf16_tflops"] * 1e12), byts / (peaks["hbm_gbs"] * 1e9))
             points.append({"M": M, "K": Kd, "N": N, "us": round(per * 1e6, 2), "tflops": round(flop / per / 1e12, 1),
                            "gbs": round(byts / per / 1e9, 1), "frac_of_roofline": round(ideal / per, 3),
-                           "kernel": "gemv" if M <= 16 else "tcgen05"})
+                           "kernel": {1: "gemv", 2: "tcgen05"}.get(args.gemm_impl, "gemv" if M <= 16 else "tcgen05")})
             if M >= 512:
                 tot_flop += flop
                 tot_s += per
@@ -386,9 +393,10 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
         torch.cuda.empty_cache()
     clocks = clk.stop()
     ctx.check_device()
-    tf = tot_flop / tot_s / 1e12
+    tf = tot_flop / tot_s / 1e12 if tot_s > 0 else 0.0
     peak = peaks["bf16_tflops"]
-    best = max((p for p in points if p["M"] >= 512), key=lambda p: p["tflops"])
+    best = max(points, key=lambda p: p["tflops"])
+    tf = tf if tot_s > 0 else best["tflops"]
     return {
         "metric": "W4A16 prefill GEMM TFLOP/s (config 3, M >= 512 aggregate)", "value": round(tf * dist.world, 2),
         "unit": "TFLOP/s", "n_gpus": dist.world, "steps": K_steps, "warmup": W,
@@ -698,9 +706,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--vocab", type=int, default=262144, help="ple: table rows (smaller for ncu captures)")
     ap.add_argument("--copies", type=int, default=0, help="gemv/attn: rotating weight / KV copies")
+    ap.add_argument("--gemm-shapes", default="", help='gemm: "M1,M2:KxN,KxN" instead of the config 3 sweep')
+    ap.add_argument("--gemm-impl", type=int, default=0, help="gemm: 0 auto, 1 GEMV, 2 tcgen05")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
     dist = Dist()
     if args.impl == "reference":
         if dist.rank == 0:

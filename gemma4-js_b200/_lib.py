@@ -49,6 +49,7 @@ SIGNATURES = {
     "g4_ctx_create": (_S, [_I, _P, _PP]),
     "g4_ctx_destroy": (_S, [_P]),
     "g4_ctx_set_stream": (_S, [_P, _P]),
+    "g4_ctx_set_pdl": (_S, [_P, _I]),
     "g4_stream_sync": (_S, [_P]),
     "g4_ctx_check_device": (_S, [_P, C.POINTER(C.c_uint32)]),
     "g4_last_error_string": (C.c_char_p, []),

@@ -69,6 +69,8 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * C::STAGES * C::TILE_BYTES);
     uint64_t* empty = full + C::STAGES;
 
+    pdl_trigger();
+    pdl_wait();  // q, the newest K/V rows and the positions come from the predecessors
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.y, split = blockIdx.x;
     int qp, keylen, kv_row0;
@@ -275,6 +277,8 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
                                                           int heads, uint16_t* __restrict__ out) {
     __shared__ float s_w[kMaxSplits];
     __shared__ float s_red[HD / 32];
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x / heads, h = blockIdx.x - r * heads, d = threadIdx.x;
     const float2* ml = part_ml + (size_t)r * nsplit * 8 + h;
     float mloc = -INFINITY;
@@ -321,6 +325,8 @@ __global__ void __launch_bounds__(HD) attn_combine_kernel(const float* __restric
 // Appends rows to the bf16 cache, rounding f32 input to nearest even.
 __global__ void kv_append_f32_kernel(const float* __restrict__ k, const float* __restrict__ v,
                                      uint16_t* __restrict__ kc, uint16_t* __restrict__ vc, long long n) {
+    pdl_trigger();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     kc[i] = (uint16_t)f32_to_bf16_bits(k[i]);
@@ -395,12 +401,13 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
         G4_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
         attr_set.fetch_or(1ull << ctx->device);
     }
-    attn_decode_kernel<HD><<<dim3(nsplit, rows), C::THREADS, C::SMEM, ctx->stream>>>(km, vm, p);
-    G4_CHECK_LAUNCH("attn_decode_kernel");
-    if (nsplit > 1) {
-        attn_combine_kernel<HD><<<rows * heads, HD, 0, ctx->stream>>>(p.part_o, p.part_ml, nsplit, heads, out);
-        G4_CHECK_LAUNCH("attn_combine_kernel");
-    }
+    g4_status st = g4::launch(ctx, "attn_decode_kernel", attn_decode_kernel<HD>, dim3(nsplit, rows), dim3(C::THREADS),
+                              C::SMEM, 1, km, vm, p);
+    if (st) return st;
+    if (nsplit > 1)
+        return g4::launch(ctx, "attn_combine_kernel", attn_combine_kernel<HD>, dim3(rows * heads), dim3(HD), 0, 1,
+                          static_cast<const float*>(p.part_o), static_cast<const float2*>(p.part_ml), nsplit, heads,
+                          out);
     return G4_OK;
 }
 
@@ -496,9 +503,9 @@ g4_status g4_kv_append(g4_ctx* ctx, g4_kv* kv, const void* k, const void* v, int
         G4_CHECK_CUDA(cudaMemcpyAsync(kd, k, n * 2, cudaMemcpyDeviceToDevice, ctx->stream));
         G4_CHECK_CUDA(cudaMemcpyAsync(vd, v, n * 2, cudaMemcpyDeviceToDevice, ctx->stream));
     } else if (src_dtype == G4_F32) {
-        kv_append_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
-            static_cast<const float*>(k), static_cast<const float*>(v), kd, vd, (long long)n);
-        G4_CHECK_LAUNCH("kv_append_f32_kernel");
+        st = g4::launch(ctx, "kv_append_f32_kernel", kv_append_f32_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256),
+                        0, 1, static_cast<const float*>(k), static_cast<const float*>(v), kd, vd, (long long)n);
+        if (st) return st;
     } else {
         return g4::set_error(G4_ERR_INVALID, "g4_kv_append: dtype %d", (int)src_dtype);
     }

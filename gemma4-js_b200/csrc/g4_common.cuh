@@ -8,6 +8,7 @@
 
 #include <atomic>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/g4w4.h"
@@ -28,6 +29,7 @@ struct g4_ctx {
     std::vector<void*> ws_retired;  // outgrown workspaces: kept until destroy (captured graphs may use them)
     int32_t* d_ids = nullptr;       // staging for host token ids
     size_t d_ids_cap = 0;
+    bool pdl = false;               // launch with programmatic dependent launch (g4_ctx_set_pdl)
 };
 
 // Device error word bits.
@@ -49,6 +51,40 @@ g4_status encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void
                                uint64_t inner, uint64_t outer, uint64_t row_pitch_bytes,
                                uint32_t box_inner, uint32_t box_outer,
                                CUtensorMapSwizzle swizzle);
+
+// Launches `kern` on the context stream with an optional thread-block cluster along x
+// and, when the context enables it, programmatic dependent launch: the kernel may start
+// while its predecessor drains, and waits (griddepcontrol.wait) before it touches any
+// data a predecessor produces.
+template <typename... KArgs, typename... Args>
+g4_status launch(g4_ctx* ctx, const char* name, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                 int cluster_x, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = cluster_x;
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        ++n;
+    }
+    if (ctx->pdl) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_error(e, name);
+    count_launch();
+    return G4_OK;
+}
 
 }  // namespace g4
 
@@ -81,6 +117,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2_bits(float lo, float hi) {
     return f32_to_bf16_bits(lo) | (f32_to_bf16_bits(hi) << 16);
 }
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
+
+// Programmatic dependent launch (no-ops when the kernel was launched without it).
+// Every kernel calls pdl_trigger() first, so its successor can be scheduled early, and
+// pdl_wait() before it reads or writes activations; only immutable weights may be
+// fetched before the wait.  Every kernel waits, which keeps the chain transitive.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 // Bounded spin budget for every wait on a flag or mbarrier (4M polls: well under a
 // few seconds even when every poll suspends; normal waits take microseconds).

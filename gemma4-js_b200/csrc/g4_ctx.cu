@@ -135,6 +135,12 @@ g4_status g4_ctx_set_stream(g4_ctx* ctx, void* stream) {
     return G4_OK;
 }
 
+g4_status g4_ctx_set_pdl(g4_ctx* ctx, int enable) {
+    if (!ctx) return g4::set_error(G4_ERR_INVALID, "null context");
+    ctx->pdl = enable != 0;
+    return G4_OK;
+}
+
 g4_status g4_stream_sync(g4_ctx* ctx) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;

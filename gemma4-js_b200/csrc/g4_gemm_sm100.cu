@@ -154,6 +154,8 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_base_slot;
+    pdl_trigger();
+    if (!(warp == 0 && lane == 0)) pdl_wait();  // the TMA thread waits after prefetching weights
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -161,8 +163,25 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             prefetch_tensor_map(&xmap);
             prefetch_tensor_map(&wmap);
             if (kW4) prefetch_tensor_map(&smap);
-            int issued = 0;
-            for (int i = 0; i < KT; ++i) {
+            // Weights are immutable: start the first stages' weight copies before waiting for
+            // the predecessor kernel that produces X.
+            const int pre = KT < kStages ? KT : kStages;
+            for (int i = 0; i < pre; ++i) {
+                const int kt = k0 + i;
+                if constexpr (kW4) {
+                    mbar_arrive_expect_tx(&load_full[i], kABytes + kRawBytes + kScBytes);
+                    tma_load_2d(smem + kOffRaw + i * kRawBytes, &wmap, &load_full[i], kt * 128, nb * (BN / 16));
+                    tma_load_2d(smem + kOffSc + i * kScBytes, &smap, &load_full[i], kt * 16, nb * (BN / 16));
+                } else {
+                    mbar_arrive_expect_tx(&load_full[i], kABytes + kBBytes);
+                    tma_load_2d(smem + kOffB + i * kBBytes, &wmap, &load_full[i], kt * BK, nb * BN);
+                }
+            }
+            pdl_wait();
+            for (int i = 0; i < pre; ++i)
+                tma_load_2d(smem + kOffA + i * kABytes, &xmap, &load_full[i], (k0 + i) * BK, mb * BM);
+            int issued = pre;
+            for (int i = pre; i < KT; ++i) {
                 const int s = i % kStages, kt = k0 + i;
                 if (i >= kStages && !mbar_wait(&load_empty[s], ((i / kStages) - 1) & 1, p.err)) break;
                 if constexpr (kW4) {
@@ -383,22 +402,8 @@ g4_status launch_tiles(g4_ctx* ctx, const CUtensorMap& xmap, const CUtensorMap& 
     int S = 1;
     while (S < 8 && mt * nt * (S + 1) <= ctx->num_sms && p.ktiles / (S + 1) >= 4) ++S;
     p.ksplit = S;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(mt * S, nt, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = GemmSmem<kW4>::kBytes;
-    cfg.stream = ctx->stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = S;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tcgen05_kernel<kW4>, xmap, wmap, smap, p);
-    if (e != cudaSuccess) return cuda_error(e, kW4 ? "gemm_tcgen05_kernel<W4>" : "gemm_tcgen05_kernel<bf16>");
-    count_launch();
-    return G4_OK;
+    return launch(ctx, kW4 ? "gemm_tcgen05_kernel<W4>" : "gemm_tcgen05_kernel<bf16>", gemm_tcgen05_kernel<kW4>,
+                  dim3(mt * S, nt), dim3(kThreads), GemmSmem<kW4>::kBytes, S, xmap, wmap, smap, p);
 }
 
 bool gemm_supported(const g4_linear* lin, int M) {

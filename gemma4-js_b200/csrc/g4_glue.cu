@@ -52,6 +52,8 @@ __device__ __forceinline__ float gelu_ref(float x) {
 // RMS_SHADER: y = x * rsqrt(mean(x^2) + eps) * scale (scale optional).
 __global__ void __launch_bounds__(kRowThreads) rms_kernel(const float* __restrict__ x, const float* __restrict__ scale,
                                                           int width, float eps, void* __restrict__ out, int out_bf16) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const int r = blockIdx.x;
     const float* xr = x + (size_t)r * width;
@@ -70,6 +72,8 @@ __global__ void __launch_bounds__(kRowThreads) rms_kernel(const float* __restric
 // ADD_SCALE: y = (a + b) * s.
 __global__ void add_scale_kernel(const float* __restrict__ a, const float* __restrict__ b, long long n, float s,
                                  float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) y[i] = (a[i] + b[i]) * s;
 }
@@ -82,6 +86,8 @@ __global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__
                                                              int ldy, const float* __restrict__ w_post, float skip,
                                                              const float* __restrict__ w_next, int width, float eps,
                                                              uint16_t* __restrict__ x_out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const int r = blockIdx.x, i = threadIdx.x * 4;
     const bool on = i < width;
@@ -117,6 +123,8 @@ __global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __re
                                                             const int32_t* __restrict__ ids, float scale,
                                                             float* __restrict__ h, uint16_t* __restrict__ x,
                                                             uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     const int id = ids[r];
     const bool ok = (unsigned)id < (unsigned)vocab;
@@ -138,6 +146,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int
                                 const float* __restrict__ qnorm, const float* __restrict__ knorm, float eps,
                                 int rope_angles, float rope_base, G4Rows R, uint16_t* __restrict__ q_out,
                                 uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cache_cap) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const int slot = blockIdx.x, r = blockIdx.y;
     const int half = hd >> 1;
@@ -170,6 +180,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int
 // GELU_MUL over a fused [gate | up] projection: out = bf16(gelu(gate) * up), four
 // columns per thread (inter % 4 == 0).
 __global__ void gelu_mul_kernel(const float* __restrict__ gu, int inter, long long n4, uint16_t* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const int q = inter >> 2;
@@ -185,6 +197,8 @@ __global__ void gelu_mul_kernel(const float* __restrict__ gu, int inter, long lo
 // GELU_PLE: out = bf16(gelu(gate) * per_layer[row, layer, :]).
 __global__ void gelu_ple_kernel(const float* __restrict__ gate, const float* __restrict__ per_layer, int layer,
                                 int layers, int dim, long long n, uint16_t* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const long long r = i / dim, d = i - r * dim;
@@ -195,6 +209,8 @@ __global__ void gelu_ple_kernel(const float* __restrict__ gate, const float* __r
 // per (row, layer) segment of `dim`.  One CTA per segment, one thread per element.
 __global__ void ple_mix_kernel(const float* __restrict__ proj, float proj_scale, const float* __restrict__ norm,
                                const float* __restrict__ tok_ple, int dim, float eps, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const size_t base = (size_t)blockIdx.x * dim;
     const int d = threadIdx.x;
@@ -214,6 +230,8 @@ __device__ __forceinline__ void arg_better(float& bv, int& bi, float v, int i) {
 }
 __global__ void __launch_bounds__(256) argmax_partial_kernel(const float* __restrict__ logits, int vocab, float cap,
                                                              float2* __restrict__ part) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[256];
     __shared__ int si[256];
     const int r = blockIdx.y, c = blockIdx.x;
@@ -238,6 +256,8 @@ __global__ void __launch_bounds__(256) argmax_partial_kernel(const float* __rest
 // pass 2: reduce the chunk partials of a row; write the id (and optionally the value).
 __global__ void __launch_bounds__(256) argmax_final_kernel(const float2* __restrict__ part, int nparts,
                                                            int32_t* __restrict__ ids, float* __restrict__ vals) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float sv[256];
     __shared__ int si[256];
     const int r = blockIdx.x;
@@ -262,6 +282,8 @@ __global__ void __launch_bounds__(256) argmax_final_kernel(const float2* __restr
 
 // Advances the positions of sequences [seq_base, seq_base + nseq) by `by`.
 __global__ void advance_pos_kernel(int32_t* seq_pos, int seq_base, int nseq, int by) {
+    pdl_trigger();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < nseq) seq_pos[seq_base + i] += by;
 }
@@ -278,9 +300,8 @@ g4_status g4_rms(g4_ctx* ctx, const float* x, const float* scale, int rows, int 
     if (st) return st;
     if (rows < 0 || width <= 0 || !x || !out) return g4::set_error(G4_ERR_INVALID, "g4_rms: bad arguments");
     if (rows == 0) return G4_OK;
-    rms_kernel<<<rows, kRowThreads, 0, ctx->stream>>>(x, scale, width, eps, out, out_dtype == G4_BF16);
-    G4_CHECK_LAUNCH("rms_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "rms_kernel", rms_kernel, dim3(rows), dim3(kRowThreads), 0, 1, x, scale, width, eps, out,
+                      (int)(out_dtype == G4_BF16));
 }
 
 g4_status g4_add_scale(g4_ctx* ctx, const float* a, const float* b, long long n, float scale, float* y) {
@@ -288,9 +309,7 @@ g4_status g4_add_scale(g4_ctx* ctx, const float* a, const float* b, long long n,
     if (st) return st;
     if (n < 0 || !a || !b || !y) return g4::set_error(G4_ERR_INVALID, "g4_add_scale: bad arguments");
     if (n == 0) return G4_OK;
-    add_scale_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(a, b, n, scale, y);
-    G4_CHECK_LAUNCH("add_scale_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "add_scale_kernel", add_scale_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, a, b, n, scale, y);
 }
 
 g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const float* w_post, float skip,
@@ -302,10 +321,8 @@ g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const
         return g4::set_error(G4_ERR_UNSUPPORTED, "g4_post_norm_add: width %d / ldy %d (multiples of 4, width <= 4096)", width, ldy);
     if (rows == 0) return G4_OK;
     const int threads = ((width / 4 + 31) / 32) * 32;
-    post_norm_add_kernel<<<rows, threads, 0, ctx->stream>>>(h, y, ldy, w_post, skip, w_next, width, eps,
-                                                            static_cast<uint16_t*>(x_out_bf16));
-    G4_CHECK_LAUNCH("post_norm_add_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "post_norm_add_kernel", post_norm_add_kernel, dim3(rows), dim3(threads), 0, 1, h, y, ldy,
+                      w_post, skip, w_next, width, eps, static_cast<uint16_t*>(x_out_bf16));
 }
 
 g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, const int32_t* ids_dev, int rows,
@@ -314,11 +331,9 @@ g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, co
     if (st) return st;
     if (rows < 0 || !table_bf16 || !ids_dev || !h_out) return g4::set_error(G4_ERR_INVALID, "g4_embed: bad arguments");
     if (rows == 0) return G4_OK;
-    embed_kernel<<<rows, kRowThreads, 0, ctx->stream>>>(static_cast<const uint16_t*>(table_bf16), vocab, width,
-                                                        ids_dev, scale, h_out, static_cast<uint16_t*>(x_out_bf16),
-                                                        ctx->d_err);
-    G4_CHECK_LAUNCH("embed_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "embed_kernel", embed_kernel, dim3(rows), dim3(kRowThreads), 0, 1,
+                      static_cast<const uint16_t*>(table_bf16), vocab, width, ids_dev, scale, h_out,
+                      static_cast<uint16_t*>(x_out_bf16), ctx->d_err);
 }
 
 g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,
@@ -330,12 +345,10 @@ g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, i
         return g4::set_error(G4_ERR_INVALID, "g4_qkv_post: bad arguments");
     if (hd % 64 != 0 || hd > 1024) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_qkv_post: hd %d", hd);
     if (rows == 0) return G4_OK;
-    qkv_post_kernel<<<dim3(heads + (has_kv ? 2 : 0), rows), hd / 2, 0, ctx->stream>>>(
-        y, ldy, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map,
-        static_cast<uint16_t*>(q_out_bf16), static_cast<uint16_t*>(kcache_bf16), static_cast<uint16_t*>(vcache_bf16),
-        cache_cap);
-    G4_CHECK_LAUNCH("qkv_post_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "qkv_post_kernel", qkv_post_kernel, dim3(heads + (has_kv ? 2 : 0), rows), dim3(hd / 2), 0,
+                      1, y, ldy, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map,
+                      static_cast<uint16_t*>(q_out_bf16), static_cast<uint16_t*>(kcache_bf16),
+                      static_cast<uint16_t*>(vcache_bf16), cache_cap);
 }
 
 g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, void* out_bf16) {
@@ -345,9 +358,8 @@ g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, vo
     if (inter % 4 != 0) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_gelu_mul: inter %d (multiple of 4)", inter);
     const long long n4 = (long long)rows * inter / 4;
     if (n4 == 0) return G4_OK;
-    gelu_mul_kernel<<<blocks_for(n4, 256), 256, 0, ctx->stream>>>(gate_up, inter, n4, static_cast<uint16_t*>(out_bf16));
-    G4_CHECK_LAUNCH("gelu_mul_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "gelu_mul_kernel", gelu_mul_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, 1, gate_up,
+                      inter, n4, static_cast<uint16_t*>(out_bf16));
 }
 
 g4_status g4_gelu_ple(g4_ctx* ctx, const float* gate, const float* per_layer, int layer, int layers, int dim,
@@ -358,10 +370,8 @@ g4_status g4_gelu_ple(g4_ctx* ctx, const float* gate, const float* per_layer, in
         return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple: bad arguments");
     const long long n = (long long)rows * dim;
     if (n == 0) return G4_OK;
-    gelu_ple_kernel<<<blocks_for(n, 256), 256, 0, ctx->stream>>>(gate, per_layer, layer, layers, dim, n,
-                                                                 static_cast<uint16_t*>(out_bf16));
-    G4_CHECK_LAUNCH("gelu_ple_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "gelu_ple_kernel", gelu_ple_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, gate,
+                      per_layer, layer, layers, dim, n, static_cast<uint16_t*>(out_bf16));
 }
 
 g4_status g4_ple_mix(g4_ctx* ctx, const float* proj, float proj_scale, const float* norm, const float* tok_ple,
@@ -371,9 +381,8 @@ g4_status g4_ple_mix(g4_ctx* ctx, const float* proj, float proj_scale, const flo
     if (rows < 0 || !proj || !norm || !tok_ple || !out || dim > 1024 || dim % 32)
         return g4::set_error(G4_ERR_INVALID, "g4_ple_mix: bad arguments");
     if (rows == 0) return G4_OK;
-    ple_mix_kernel<<<rows * layers, dim, 0, ctx->stream>>>(proj, proj_scale, norm, tok_ple, dim, eps, out);
-    G4_CHECK_LAUNCH("ple_mix_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "ple_mix_kernel", ple_mix_kernel, dim3(rows * layers), dim3(dim), 0, 1, proj, proj_scale,
+                      norm, tok_ple, dim, eps, out);
 }
 
 g4_status g4_softcap_argmax(g4_ctx* ctx, const float* logits, int rows, int vocab, float cap, int32_t* ids_out,
@@ -386,11 +395,11 @@ g4_status g4_softcap_argmax(g4_ctx* ctx, const float* logits, int rows, int voca
     st = g4::ensure_workspace(ctx, (size_t)rows * nparts * sizeof(float2));
     if (st) return st;
     float2* part = static_cast<float2*>(ctx->ws);
-    argmax_partial_kernel<<<dim3(nparts, rows), 256, 0, ctx->stream>>>(logits, vocab, cap, part);
-    G4_CHECK_LAUNCH("argmax_partial_kernel");
-    argmax_final_kernel<<<rows, 256, 0, ctx->stream>>>(part, nparts, ids_out, vals_out);
-    G4_CHECK_LAUNCH("argmax_final_kernel");
-    return G4_OK;
+    st = g4::launch(ctx, "argmax_partial_kernel", argmax_partial_kernel, dim3(nparts, rows), dim3(256), 0, 1, logits,
+                    vocab, cap, part);
+    if (st) return st;
+    return g4::launch(ctx, "argmax_final_kernel", argmax_final_kernel, dim3(rows), dim3(256), 0, 1,
+                      static_cast<const float2*>(part), nparts, ids_out, vals_out);
 }
 
 g4_status g4_advance_positions(g4_ctx* ctx, int32_t* seq_pos, int seq_base, int nseq, int by) {
@@ -398,9 +407,8 @@ g4_status g4_advance_positions(g4_ctx* ctx, int32_t* seq_pos, int seq_base, int 
     if (st) return st;
     if (!seq_pos || nseq < 0) return g4::set_error(G4_ERR_INVALID, "g4_advance_positions: bad arguments");
     if (nseq == 0) return G4_OK;
-    advance_pos_kernel<<<blocks_for(nseq, 256), 256, 0, ctx->stream>>>(seq_pos, seq_base, nseq, by);
-    G4_CHECK_LAUNCH("advance_pos_kernel");
-    return G4_OK;
+    return g4::launch(ctx, "advance_pos_kernel", advance_pos_kernel, dim3(blocks_for(nseq, 256)), dim3(256), 0, 1,
+                      seq_pos, seq_base, nseq, by);
 }
 
 }  // extern "C"

@@ -44,11 +44,14 @@ __global__ void __launch_bounds__(kHeadWarps * 32) head_gemv_kernel(const uint16
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_trigger();
     if (threadIdx.x == 0) {
         mbar_arrive_expect_tx(bar, (uint32_t)(rows + M) * K * 2);
         for (int r = 0; r < rows; ++r) bulk_load(wsm + r * pitch, w + (size_t)(n0 + r) * K, K * 2, bar);
-        for (int b = 0; b < M; ++b) bulk_load(xsm + b * pitch, x + (size_t)b * K, K * 2, bar);
     }
+    pdl_wait();  // the head rows are immutable; x comes from the predecessor
+    if (threadIdx.x == 0)
+        for (int b = 0; b < M; ++b) bulk_load(xsm + b * pitch, x + (size_t)b * K, K * 2, bar);
     // rows past N read as zero
     for (int i = threadIdx.x; i < (16 - rows) * (K / 8); i += blockDim.x) {
         const int r = rows + i / (K / 8), c = i % (K / 8);
@@ -166,12 +169,12 @@ g4_status g4_dense_matmul(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, in
         attr_set.fetch_or(1ull << ctx->device);
     }
     const unsigned grid = (unsigned)((d->N + 15) / 16);
+    const uint16_t* w = d->w;
     if (nb == 1)
-        head_gemv_kernel<1><<<grid, kHeadWarps * 32, smem, ctx->stream>>>(d->w, d->N, d->K, x, M, y, ctx->d_err);
-    else
-        head_gemv_kernel<2><<<grid, kHeadWarps * 32, smem, ctx->stream>>>(d->w, d->N, d->K, x, M, y, ctx->d_err);
-    G4_CHECK_LAUNCH("head_gemv_kernel");
-    return G4_OK;
+        return g4::launch(ctx, "head_gemv_kernel", head_gemv_kernel<1>, dim3(grid), dim3(kHeadWarps * 32), smem, 1, w,
+                          d->N, d->K, x, M, y, ctx->d_err);
+    return g4::launch(ctx, "head_gemv_kernel", head_gemv_kernel<2>, dim3(grid), dim3(kHeadWarps * 32), smem, 1, w, d->N,
+                      d->K, x, M, y, ctx->d_err);
 }
 
 }  // extern "C"

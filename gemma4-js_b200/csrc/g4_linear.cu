@@ -146,7 +146,7 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int nt = blockIdx.x, split = blockIdx.y;
+    const int split = blockIdx.x, nt = blockIdx.y;
     const int c_begin = split * chunks_per_split;
     const int c_end = min(L.Kc, c_begin + chunks_per_split);
 
@@ -155,6 +155,8 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_trigger();
+    if (threadIdx.x != 0) pdl_wait();  // thread 0 waits after it has started the weight copies
 
     float acc[kNB][4];
 #pragma unroll
@@ -172,6 +174,7 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
             const size_t blk = (size_t)nt * L.Kc + p0;
             bulk_load(wsm, L.wfrag + blk * 32, nch * 512, bar);
             bulk_load(ssm, L.sfrag + blk * 8, nch * 64, bar);
+            if (p0 == c_begin) pdl_wait();  // weights are immutable; activations come from the predecessor
             for (int b = 0; b < M; ++b)
                 bulk_load(xsm + b * xstride, x + (size_t)b * ldx + k0, klen * 2, bar);
         }
@@ -234,7 +237,7 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         }
     }
     // ---- reduce the S CTAs of the cluster through distributed shared memory ----
-    const int S = gridDim.y;
+    const int S = gridDim.x;
     if (S > 1) {
         cg::cluster_group cluster = cg::this_cluster();
         cluster.sync();
@@ -290,28 +293,16 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     const int cps = (L.Kc + S - 1) / S;
     for (int m0 = 0; m0 < M; m0 += 16) {
         const int mm = (M - m0) < 16 ? (M - m0) : 16;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(L.NT, S, 1);
-        cfg.blockDim = dim3(kGemvWarps * 32, 1, 1);
-        cfg.dynamicSmemBytes = gemv_smem_bytes(cps < kGemvPass ? cps : kGemvPass, mm);
-        cfg.stream = ctx->stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = 1;
-        attr[0].val.clusterDim.y = S;
-        attr[0].val.clusterDim.z = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        const size_t smem = gemv_smem_bytes(cps < kGemvPass ? cps : kGemvPass, mm);
         const uint16_t* xs = x + (size_t)m0 * L.K;
         void* ys = y_f32 ? (void*)(reinterpret_cast<float*>(y) + (size_t)m0 * L.N)
                          : (void*)(reinterpret_cast<uint16_t*>(y) + (size_t)m0 * L.N);
-        cudaError_t e;
-        if (mm <= 8)
-            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<1>, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
-        else
-            e = cudaLaunchKernelEx(&cfg, gemv_w4a16_kernel<2>, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
-        if (e != cudaSuccess) return cuda_error(e, "gemv_w4a16_kernel");
-        count_launch();
+        // the split-K cluster runs along x: grid (S, NT), CTA (split, tile)
+        g4_status st = mm <= 8 ? launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<1>, dim3(S, L.NT), dim3(kGemvWarps * 32),
+                                        smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err)
+                               : launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<2>, dim3(S, L.NT), dim3(kGemvWarps * 32),
+                                        smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
+        if (st) return st;
     }
     return G4_OK;
 }

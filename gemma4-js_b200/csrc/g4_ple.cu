@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(256) ple_gather_kernel(const uint4* __restrict
                                                          const int32_t* __restrict__ ids, int T,
                                                          int vocab, int groups_per_row,
                                                          void* __restrict__ out, uint32_t* err) {
+    pdl_trigger();
+    pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long total = (long long)T * groups_per_row;
     if (i >= total) return;
@@ -216,13 +218,10 @@ g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids
     if (blocks > 0x7fffffffLL) return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: T too large");
     const uint4* p = reinterpret_cast<const uint4*>(tab->packed);
     if (out_dtype == G4_BF16)
-        ple_gather_kernel<false><<<(unsigned)blocks, threads, 0, ctx->stream>>>(
-            p, tab->scales, d_ids, T, tab->vocab, gpr, out, ctx->d_err);
-    else
-        ple_gather_kernel<true><<<(unsigned)blocks, threads, 0, ctx->stream>>>(
-            p, tab->scales, d_ids, T, tab->vocab, gpr, out, ctx->d_err);
-    G4_CHECK_LAUNCH("ple_gather_kernel");
-    return G4_OK;
+        return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false>, dim3((unsigned)blocks), dim3(threads), 0, 1,
+                          p, static_cast<const uint16_t*>(tab->scales), d_ids, T, tab->vocab, gpr, out, ctx->d_err);
+    return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true>, dim3((unsigned)blocks), dim3(threads), 0, 1, p,
+                      static_cast<const uint16_t*>(tab->scales), d_ids, T, tab->vocab, gpr, out, ctx->d_err);
 }
 
 }  // extern "C"

@@ -225,8 +225,10 @@ class Gemma4Model:
     """Mirror of Gemma4WebGPU over libg4w4 (see the module docstring)."""
 
     def __init__(self, ctx: Context, cfg: ModelConfig, w: dict, max_batch: int = 1, max_seq: int = 512,
-                 max_rows: int | None = None):
+                 max_rows: int | None = None, pdl: bool = True):
         self.ctx, self.cfg = ctx, cfg
+        if pdl:  # the decode step is a long chain of this library's kernels on one stream
+            ctx.set_pdl(True)
         self.max_batch, self.max_seq = max_batch, max_seq
         self.max_rows = max(max_rows or 0, max_batch, 1)
         dev = ctx.torch_device

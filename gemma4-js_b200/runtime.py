@@ -51,6 +51,10 @@ class Context:
         self._stream = stream
         call("g4_ctx_set_stream", self.handle, C.c_void_p(stream.cuda_stream))
 
+    def set_pdl(self, enable: bool) -> None:
+        """Programmatic dependent launch for this context's kernels (g4_ctx_set_pdl)."""
+        call("g4_ctx_set_pdl", self.handle, int(bool(enable)))
+
     @property
     def stream(self) -> torch.cuda.Stream:
         return self._stream

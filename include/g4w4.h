@@ -68,6 +68,11 @@ typedef struct {
 g4_status g4_ctx_create(int device, void* stream, g4_ctx** out);
 g4_status g4_ctx_destroy(g4_ctx* ctx);
 g4_status g4_ctx_set_stream(g4_ctx* ctx, void* stream);
+/* Programmatic dependent launch for this context's kernels (default off): each kernel
+ * may be scheduled while its predecessor on the stream drains and prefetches its
+ * weights before waiting for the predecessor's results.  Use it for long chains of
+ * this library's kernels on one stream (a captured decode step). */
+g4_status g4_ctx_set_pdl(g4_ctx* ctx, int enable);
 /* Waits for all work issued on the context stream (reference: queue.onSubmittedWorkDone). */
 g4_status g4_stream_sync(g4_ctx* ctx);
 /* Reads and clears the device-side error word that kernels set when a bounded wait
