@@ -27,8 +27,10 @@ def small_cfg(**kw):
     return model.ModelConfig().small(**base)
 
 
-def greedy_compare(gpu, orc, prompt, steps, seq=0, noise=0.02):
-    """Prefill + `steps` greedy steps on both; returns (tokens, near_ties, margins)."""
+def greedy_compare(gpu, orc, prompt, steps, seq=0, noise=0.02, forced=None):
+    """Prefill + `steps` decode steps on both; returns (tokens, near_ties, margins).
+    Each step feeds both sides the oracle's greedy pick, or forced[step] when given
+    (teacher forcing: every step is then a different decision point)."""
     g_next = gpu.prefill(seq, prompt)
     o_next, capped = orc.forward(prompt)
     toks, ties, margins = [], [], []
@@ -43,9 +45,10 @@ def greedy_compare(gpu, orc, prompt, steps, seq=0, noise=0.02):
         toks.append(o_next)
         if step == steps:
             break
-        ids = torch.tensor([o_next], dtype=torch.int32, device="cuda")
-        g_next = int(gpu.decode_step(ids_dev=ids, batch=1)[0].item()) if seq == 0 else None
-        o_next, capped = orc.forward([o_next])
+        feed = o_next if forced is None else int(forced[step])
+        ids = torch.tensor([feed], dtype=torch.int32, device="cuda")
+        g_next = int(gpu.decode_step(ids_dev=ids, batch=1)[0].item())
+        o_next, capped = orc.forward([feed])
     return toks, ties, margins
 
 
@@ -127,14 +130,42 @@ def test_reference_spec_small(rt, ctx):
     assert not ties
 
 
-def test_full_size_greedy_32(rt, ctx):
+# A random-init network this deep is chaotic at most initialisations: two correct
+# implementations (or the oracle evaluated in two orders) drift apart by O(1) in the
+# logits.  This initialisation keeps the residual updates small (post norms 0.1) and
+# feeds the PLE strongly (2.0), which the CPU oracle shows to be self-consistent
+# (noise floor ~0.05 on top logits ~6, greedy margins >= 0.1).
+FULL_KW = dict(embed_sigma=0.035, post_norm=0.1, ple_post_norm=2.0, skip=(0.98, 1.0))
+
+
+@pytest.fixture(scope="module")
+def full_size(rt, ctx):
+    cfg = model.ModelConfig()
+    w = model.random_weights(cfg, seed=0, **FULL_KW)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=128, max_rows=16)
+    orc = mo.OracleModel(cfg, w, max_seq=128)
+    return cfg, gpu, orc
+
+
+def test_full_size_greedy_32(full_size):
     """BASELINE config 4's model (35 layers, hidden 1536, MLP 6144, 8q/1kv, hd 256,
     window 512, PLE 256/layer, vocab 262144 tied), seeded random init: 32 greedy steps
     must give the oracle's token ids."""
-    cfg = model.ModelConfig()
-    w = model.random_weights(cfg, seed=0, **W_KW)
-    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=128, max_rows=16)
-    orc = mo.OracleModel(cfg, w, max_seq=128)
+    cfg, gpu, orc = full_size
+    gpu.reset()
+    orc.reset()
     toks, ties, margins = greedy_compare(gpu, orc, [2, 106, 1645, 7, 99, 4242, 262143, 0], 32)
     print("tokens", toks, "near ties", ties, "min margin", round(min(margins), 4))
     assert len(toks) == 33 and not ties
+
+
+def test_full_size_teacher_forced_32(full_size):
+    """Same model, 32 random input tokens: the greedy pick after every one of them must
+    match the oracle's (32 different decision points)."""
+    cfg, gpu, orc = full_size
+    gpu.reset()
+    orc.reset()
+    forced = np.random.default_rng(7).integers(0, cfg.vocab, 32)
+    toks, ties, margins = greedy_compare(gpu, orc, [5, 6, 7, 8], 32, forced=forced)
+    print("picks", toks, "distinct", len(set(toks)), "near ties", ties, "min margin", round(min(margins), 4))
+    assert len(toks) == 33 and len(ties) <= 1
