@@ -63,7 +63,9 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                    AttnParams p) {
     using C = AttnCfg<HD>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // Offset the __shared__ array itself (not an integer round trip) so the compiler keeps
+    // shared-memory addressing for every access through `smem`.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* kst = smem;                                   // [STAGES][TILE]
     uint8_t* vst = smem + C::STAGES * C::TILE_BYTES;       // [STAGES][TILE]
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + 2 * C::STAGES * C::TILE_BYTES);

@@ -111,6 +111,58 @@ struct GemmParams {
     uint32_t* err;
 };
 
+// Split-K reduction of one cluster rank: rows kslice, kslice + S, ... of the tile are
+// summed over the S parked partials in rank order (deterministic) and stored.  Thread t
+// owns 4 columns of every 4th of those rows; all S x RB loads of a batch of RB rows are
+// issued before any is used, so a batch costs one distributed-shared-memory round trip.
+template <int S>
+__device__ __forceinline__ void split_reduce(uint8_t* smem, cg::cluster_group& cluster, int kslice, int mb, int nb,
+                                             int t, const GemmParams& p) {
+    constexpr int J = (BM + 4 * S - 1) / (4 * S);  // rows per thread
+    constexpr int RB = (16 / S) > 0 ? (16 / S) : 1; // rows per batch
+    const int c4 = (t & 63) * 4, rsub = t >> 6;
+    const int n = nb * BN + c4;
+    const float* peer[S];
+#pragma unroll
+    for (int r = 0; r < S; ++r) peer[r] = cluster.map_shared_rank(reinterpret_cast<float*>(smem), r);
+#pragma unroll
+    for (int j0 = 0; j0 < J; j0 += RB) {
+        float4 v[RB][S];
+#pragma unroll
+        for (int jb = 0; jb < RB; ++jb) {
+            const int rr = kslice + S * (rsub + 4 * (j0 + jb));
+            const bool live = j0 + jb < J && rr < BM && mb * BM + rr < p.M;  // rows past M are not moved
+#pragma unroll
+            for (int r = 0; r < S; ++r)
+                v[jb][r] = live ? *reinterpret_cast<const float4*>(peer[r] + rr * kRedPitch + c4)
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int jb = 0; jb < RB; ++jb) {
+            const int rr = kslice + S * (rsub + 4 * (j0 + jb));
+            if (j0 + jb >= J || rr >= BM) continue;
+            float4 acc = v[jb][0];
+#pragma unroll
+            for (int r = 1; r < S; ++r) {
+                acc.x += v[jb][r].x;
+                acc.y += v[jb][r].y;
+                acc.z += v[jb][r].z;
+                acc.w += v[jb][r].w;
+            }
+            const int row = mb * BM + rr;
+            if (row < p.M && n < p.N) {  // N % 8 == 0: the 4 columns are all in or all out
+                if (p.y_f32) {
+                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)row * p.ldy + n) = acc;
+                } else {
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+                    *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)row * p.ldy + n) =
+                        make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+                }
+            }
+        }
+    }
+}
+
 // kW4 = true: B = dequant(int4 blocks) by the producer warps (wmap / smap = weight
 // blocks / scales).  kW4 = false: B is a bf16 [N, K] matrix loaded by TMA (wmap,
 // 128B swizzle), e.g. the tied bf16 LM head; smap is unused.
@@ -121,7 +173,9 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     using L = GemmSmem<kW4>;
     constexpr int kOffA = L::kOffA, kOffB = L::kOffB, kOffRaw = L::kOffRaw, kOffSc = L::kOffSc, kOffBar = L::kOffBar;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // Offset the __shared__ array itself (not an integer round trip) so the compiler keeps
+    // shared-memory addressing for every access through `smem`.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t* load_full = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint64_t* load_empty = load_full + kStages;
     uint64_t* b_full = load_empty + kStages;
@@ -274,10 +328,12 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         if (S > 1) {
             // Split K: park this CTA's FP32 partial tile in its (now idle) shared memory;
             // the cluster sums the S partials below.
+            const bool row_live = mb * BM + (warp & 3) * 32 + lane < p.M;  // rows past M are never read
             if (KT == 0) {  // an empty K slice contributes zeros (its accumulator was never written)
                 const int quarter = warp & 3, col0 = (warp < 6) ? 0 : 128;
                 float* red = reinterpret_cast<float*>(smem) + (quarter * 32 + lane) * kRedPitch + col0;
-                for (int c = 0; c < 128; c += 4) *reinterpret_cast<uint4*>(red + c) = make_uint4(0, 0, 0, 0);
+                if (row_live)
+                    for (int c = 0; c < 128; c += 4) *reinterpret_cast<uint4*>(red + c) = make_uint4(0, 0, 0, 0);
             } else if (mbar_wait_warp(acc_full, 0, p.err)) {
                 tc_fence_after();
                 const int quarter = warp & 3, col0 = (warp < 6) ? 0 : 128;
@@ -287,9 +343,11 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c), r);
                     tmem_ld_wait();
+                    if (row_live) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4)
-                        *reinterpret_cast<uint4*>(red + c + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<uint4*>(red + c + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+                    }
                 }
             }
         } else if (mbar_wait_warp(acc_full, 0, p.err)) {
@@ -345,30 +403,14 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         cg::cluster_group cluster = cg::this_cluster();
         cluster.sync();
         if (warp >= 2) {
-            const int t = threadIdx.x - 64;              // 0..255
-            const int c4 = (t & 63) * 4, rsub = t >> 6;  // 4 columns, one of 4 row phases
-            const int n = nb * BN + c4;
-            for (int rr = kslice + rsub * S; rr < BM; rr += 4 * S) {
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-                for (int r = 0; r < S; ++r) {
-                    const float4 v = *reinterpret_cast<const float4*>(
-                        cluster.map_shared_rank(reinterpret_cast<float*>(smem), r) + rr * kRedPitch + c4);
-                    acc.x += v.x;
-                    acc.y += v.y;
-                    acc.z += v.z;
-                    acc.w += v.w;
-                }
-                const int row = mb * BM + rr;
-                if (row < p.M && n < p.N) {  // N % 8 == 0: the 4 columns are all in or all out
-                    if (p.y_f32) {
-                        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)row * p.ldy + n) = acc;
-                    } else {
-                        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-                        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)row * p.ldy + n) =
-                            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-                    }
-                }
+            switch (S) {
+                case 2: split_reduce<2>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
+                case 3: split_reduce<3>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
+                case 4: split_reduce<4>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
+                case 5: split_reduce<5>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
+                case 6: split_reduce<6>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
+                case 7: split_reduce<7>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
+                default: split_reduce<8>(smem, cluster, kslice, mb, nb, threadIdx.x - 64, p); break;
             }
         }
         cluster.sync();  // peers may still be reading this CTA's partial
