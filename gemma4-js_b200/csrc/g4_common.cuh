@@ -23,7 +23,7 @@ struct g4_ctx {
     int device = 0;
     cudaStream_t stream = nullptr;
     int num_sms = 148;
-    uint32_t* d_err = nullptr;      // device error word (bit set, see G4_DEVERR_*)
+    uint32_t* d_err = nullptr;      // device error words: [0] G4_DEVERR_* bits, [1] site of a timed-out wait
     void* ws = nullptr;             // grow-only scratch for split-K / split-KV partials
     size_t ws_bytes = 0;
     std::vector<void*> ws_retired;  // outgrown workspaces: kept until destroy (captured graphs may use them)
@@ -125,12 +125,21 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-// Bounded spin budget for every wait on a flag or mbarrier (4M polls: well under a
-// few seconds even when every poll suspends; normal waits take microseconds).
-constexpr uint32_t kSpinLimit = 1u << 22;
+// Every wait on a flag or mbarrier gives up after kWaitLimitNs of wall time (normal waits
+// take microseconds); the kernel then raises G4_DEVERR_TIMEOUT and winds down.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
-__device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bit) {
-    if (err) atomicOr(err, bit);
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// err[0]: G4_DEVERR_* bits; err[1]: the site code of the first wait that gave up.
+__device__ __forceinline__ void raise_error(uint32_t* err, uint32_t bit, uint32_t site = 0) {
+    if (!err) return;
+    atomicOr(err, bit);
+    if (site) atomicCAS(err + 1, 0u, site);
 }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -165,18 +174,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Waits for the phase with `parity` to complete.  Gives up after kSpinLimit polls,
-// raises G4_DEVERR_TIMEOUT and returns false; the caller then winds down.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    raise_error(err, G4_DEVERR_TIMEOUT);
+// Waits for the phase with `parity` to complete.  Gives up after kWaitLimitNs, raises
+// G4_DEVERR_TIMEOUT (recording `site`) and returns false; the caller then winds down.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t site = 0) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+    }
+    raise_error(err, G4_DEVERR_TIMEOUT, site);
     return false;
 }
 
 // Warp-uniform variant: every lane of the warp gets the same answer.
-__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* err) {
-    const bool ok = mbar_wait(bar, parity, err);
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t site = 0) {
+    const bool ok = mbar_wait(bar, parity, err, site);
     return __all_sync(0xffffffffu, ok);
 }
 

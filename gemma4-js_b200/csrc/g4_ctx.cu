@@ -107,8 +107,8 @@ g4_status g4_ctx_create(int device, void* stream, g4_ctx** out) {
     c->device = device;
     c->stream = static_cast<cudaStream_t>(stream);
     c->num_sms = prop.multiProcessorCount;
-    cudaError_t e = cudaMalloc(&c->d_err, sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, sizeof(uint32_t));
+    cudaError_t e = cudaMalloc(&c->d_err, 2 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMemset(c->d_err, 0, 2 * sizeof(uint32_t));
     if (e != cudaSuccess) {
         delete c;
         return g4::cuda_error(e, "g4_ctx_create");
@@ -151,15 +151,17 @@ g4_status g4_stream_sync(g4_ctx* ctx) {
 g4_status g4_ctx_check_device(g4_ctx* ctx, uint32_t* flags) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;
-    uint32_t h = 0;
-    G4_CHECK_CUDA(cudaMemcpyAsync(&h, ctx->d_err, sizeof(h), cudaMemcpyDeviceToHost, ctx->stream));
+    uint32_t hw[2] = {0, 0};
+    G4_CHECK_CUDA(cudaMemcpyAsync(hw, ctx->d_err, sizeof(hw), cudaMemcpyDeviceToHost, ctx->stream));
     G4_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
+    const uint32_t h = hw[0];
     if (flags) *flags = h;
     if (h) {
-        G4_CHECK_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(uint32_t), ctx->stream));
+        G4_CHECK_CUDA(cudaMemsetAsync(ctx->d_err, 0, sizeof(hw), ctx->stream));
         G4_CHECK_CUDA(cudaStreamSynchronize(ctx->stream));
         if (h & G4_DEVERR_TIMEOUT)
-            return g4::set_error(G4_ERR_TIMEOUT, "a device-side bounded wait timed out (flags 0x%x)", h);
+            return g4::set_error(G4_ERR_TIMEOUT, "a device-side bounded wait timed out (flags 0x%x, wait site %u)", h,
+                                 hw[1]);
         return g4::set_error(G4_ERR_DEVICE, "a kernel saw an out-of-range index (flags 0x%x)", h);
     }
     return G4_OK;

@@ -22,6 +22,7 @@
 #include <stdio.h>
 
 #include "g4_linear.cuh"
+#include "g4_tcgen05.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -54,55 +55,8 @@ struct GemmSmem {
     static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
 };
 
-// ---- tcgen05 wrappers ----
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-                 "r"(ncols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-__device__ __forceinline__ void tc_mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-// 32 lanes x 32 consecutive columns of 32-bit data.
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);       // start address
-    d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;               // stride byte offset: 8 rows x 128 B
-    d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
-    d |= (uint64_t)2 << 61;                         // SWIZZLE_128B
-    return d;
-}
 // Instruction descriptor: D f32, A = B = bf16, both K-major, M = 128, N = 256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+constexpr uint32_t kIdesc = mma_idesc_bf16(BM, BN);
 
 struct GemmParams {
     void* y;
@@ -268,7 +222,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 const uint32_t b0 = smem_u32(smem + kOffB + sb * kBBytes);
 #pragma unroll
                 for (int ks = 0; ks < BK / 16; ++ks)
-                    tc_mma_bf16(tmem, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), kIdesc,
+                    tc_mma_ss(tmem, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), kIdesc,
                                 (i > 0 || ks > 0) ? 1u : 0u);
                 tc_commit(&load_empty[s]);        // X (and bf16 B) stage consumed
                 if (kW4) tc_commit(&b_empty[sb]);  // dequantised B stage consumed
@@ -342,7 +296,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 for (int c = 0; c < 128; c += 32) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c), r);
-                    tmem_ld_wait();
+                    tmem_ld_wait(r);
                     if (row_live) {
 #pragma unroll
                         for (int i = 0; i < 32; i += 4)
@@ -359,7 +313,7 @@ gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             for (int c = 0; c < 128; c += 32) {
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(col0 + c), r);
-                tmem_ld_wait();
+                tmem_ld_wait(r);
                 const int n0 = nb * BN + col0 + c;
                 if (row < p.M && n0 < p.N) {
                     if (p.y_f32) {
@@ -453,25 +407,6 @@ bool gemm_supported(const g4_linear* lin, int M) {
     return M >= 1 && lin->dev.K % 32 == 0 && lin->dev.N % 8 == 0;
 }
 
-g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32) {
-    const g4_linear_dev& L = lin->dev;
-    if (!gemm_supported(lin, M)) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: shape K=%d N=%d", L.K, L.N);
-    CUtensorMap xmap;
-    g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
-                                        (uint64_t)L.K * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    GemmParams p{};
-    p.y = y;
-    p.M = M;
-    p.N = L.N;
-    p.K = L.K;
-    p.ldy = L.N;
-    p.y_f32 = y_f32;
-    p.ktiles = L.Kc;
-    p.err = ctx->d_err;
-    return launch_tiles<true>(ctx, xmap, lin->wmap, lin->smap, p);
-}
-
 g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, const uint16_t* x, int M,
                            float* y) {
     if (K % 8 != 0 || N % 8 != 0) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 bf16 GEMM: K=%d N=%d", K, N);
@@ -489,16 +424,6 @@ g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, c
     p.ktiles = (K + BK - 1) / BK;
     p.err = ctx->d_err;
     return launch_tiles<false>(ctx, xmap, bmap, bmap, p);
-}
-
-g4_status make_linear_maps(g4_linear* lin) {
-    g4_linear_dev& L = lin->dev;
-    // weight blocks as uint32 [NT rows][Kc * 128]; one box = 16 n-tiles x one 512-byte block
-    g4_status st = encode_tensor_map_2d(&lin->wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, L.wfrag, (uint64_t)L.Kc * 128,
-                                        L.NT, (uint64_t)L.Kc * 512, 128, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st) return st;
-    return encode_tensor_map_2d(&lin->smap, CU_TENSOR_MAP_DATA_TYPE_UINT32, L.sfrag, (uint64_t)L.Kc * 16, L.NT,
-                                (uint64_t)L.Kc * 64, 16, 16, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace g4

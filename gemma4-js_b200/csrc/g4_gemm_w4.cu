@@ -1,0 +1,419 @@
+// g4_gemm_w4.cu -- W4A16 GEMM on the tcgen05 tensor cores with the dequantised weights
+// held in tensor memory.
+//
+// Y[M, N] = X[M, K] . dequant(W)[N, K]^T, X bf16, FP32 accumulation in TMEM, Y bf16/f32.
+// Replaces GPUOps.w4 for many rows (custom-webgpu/gpu-runtime.js:1316-1324; the
+// reference runs one WGSL thread per output over all of K, W4_SHADER :1068-1102).
+//
+// The tensor core computes tiles of Y^T: D[128 weight rows, T tokens] += Wq[128, 16] .
+// X[T, 16]^T, with Wq the A operand read from TMEM and X the B operand read from shared
+// memory (128-byte swizzled, K-major, loaded by TMA).  The dequantised weights go from
+// registers straight into TMEM (tcgen05.st), so shared memory carries only X and the
+// packed int4 blocks: ~73 KB per 128 x 256 x 64 step instead of ~114 KB when the bf16
+// weights are staged in shared memory, which is what bounds a one-CTA tile at 128 B per
+// clock of shared-memory bandwidth.
+//
+// Roles (576 threads, one CTA per SM, persistent over tiles when there are enough of them):
+//   warp 0       TMA producer: per 128-column stage, X [T x 128] (two 64-column boxes)
+//                and the stage's two packed weight blocks (128 rows x 64 int4 + 256 bf16
+//                scales each, 9216 B contiguous, one bulk copy) into a 3-stage ring.
+//                Weight blocks of the first stages are requested before waiting on the
+//                predecessor kernel (programmatic dependent launch): they are immutable.
+//   warp 1       TMEM allocator (512 columns: accumulator 0..255, weight ring 256..383)
+//                and MMA issuer: one thread, tcgen05.mma M = 128, N = T, K = 16, eight
+//                per stage.  tcgen05.mma issue is nearly synchronous with its execution,
+//                so each synchronisation point (two barrier waits) covers 8 MMAs.
+//   warps 2..9   dequantisers: warp w owns TMEM lane quarter w % 4 (32 weight rows) and
+//                one 64-column half of the stage; q = nibble - 8 exactly in bf16, times
+//                the bf16 scale with one rounding (the compressed-tensors bf16
+//                materialisation, roundFloat32ToBF16 of q*s, official-w4a16.js:34-48,
+//                :95), then tcgen05.st into a 2-stage TMEM ring.
+//   warps 10..17 epilogue: warp w drains lane quarter w % 4, tokens 128 * ((w - 10) / 4)
+//                + 0..127: tcgen05.ld (double-buffered), release the accumulator after the
+//                last load, then neighbouring lanes swap values so that every store
+//                writes two adjacent columns of Y.
+#include <cooperative_groups.h>
+
+#include "g4_linear.cuh"
+#include "g4_tcgen05.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace {
+
+using namespace g4dev;
+
+constexpr int TW = 128;     // weight rows per tile (MMA M)
+constexpr int TTmax = 256;  // tokens per tile (MMA N), at most
+constexpr int TK = 64;      // K per weight block / X box (one 128-byte swizzle row)
+constexpr int kSub = 2;     // weight blocks per pipeline stage (K = 128 per stage)
+constexpr int kStages = 3;  // X + weight-block ring (shared memory)
+constexpr int kAStages = 2; // dequantised weight ring (TMEM, 64 columns each)
+constexpr int kDq = 8;
+constexpr int kEpi = 8;
+constexpr int kThreads = (2 + kDq + kEpi) * 32;
+constexpr int kXSub = TTmax * TK * 2;         // 32 KB: one [T x 64] box
+constexpr int kXBytes = kSub * kXSub;         // 64 KB per stage
+constexpr int kBlkBytes = g4::kTblkBytes;     // 4096 B of nibbles + 512 B of scales
+constexpr int kTmemCols = 512;
+constexpr int kAccCol = 0, kACol = 256;
+constexpr int kPartPitch = TW + 4;            // floats per token row of a parked partial
+
+struct Smem {
+    static constexpr int kOffX = 0;
+    static constexpr int kOffBlk = kOffX + kStages * kXBytes;
+    static constexpr int kOffBar = kOffBlk + kStages * kSub * kBlkBytes;
+    static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
+};
+static_assert(TTmax * kPartPitch * 4 <= Smem::kOffBlk, "a parked partial must fit in the X ring");
+static_assert(Smem::kBytes <= 232448, "shared memory plan exceeds 227 KB");
+
+struct W4Params {
+    const uint8_t* tblk;  // [NS][Kc] weight blocks
+    void* y;
+    int M, N, ldy, y_f32;
+    int Kc;          // 64-column weight blocks along K
+    int NS, MT, TT;  // weight slabs of 128 rows, token tiles, tokens per tile (multiple of 32)
+    int ksplit;      // CTAs of a cluster sharing one tile, each over 1/ksplit of K
+    uint32_t* err;
+};
+
+// Split-K: this rank sums tokens kslice, kslice + S, ... of the tile over the S parked
+// partials ([TT][kPartPitch] f32 in each rank's shared memory) in rank order and stores
+// them; 32 threads per token row, 4 weight rows each.
+__device__ __forceinline__ void split_reduce(uint8_t* smem, cg::cluster_group& cluster, int S, int kslice, int ws,
+                                             int ms, const W4Params& p) {
+    const float* peer[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+        peer[r] = cluster.map_shared_rank(reinterpret_cast<float*>(smem), r < S ? r : 0);
+    const int ntok = (p.TT - kslice + S - 1) / S;
+    for (int idx = threadIdx.x; idx < ntok * 32; idx += kThreads) {
+        const int tl = kslice + (idx >> 5) * S;
+        const int c4 = (idx & 31) * 4;
+        const int m = ms * p.TT + tl, n = ws * TW + c4;
+        if (m >= p.M || n >= p.N) continue;  // N % 8 == 0: the 4 rows are all in or all out
+        float4 v[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+            if (r < S) v[r] = *reinterpret_cast<const float4*>(peer[r] + tl * kPartPitch + c4);
+        float4 acc = v[0];
+#pragma unroll
+        for (int r = 1; r < 8; ++r)
+            if (r < S) {
+                acc.x += v[r].x;
+                acc.y += v[r].y;
+                acc.z += v[r].z;
+                acc.w += v[r].w;
+            }
+        if (p.y_f32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + n) = acc;
+        } else {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * p.ldy + n) =
+                make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const W4Params p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // Offset the __shared__ array itself (not an integer round trip) so the compiler keeps
+    // shared-memory addressing for every access through `smem`.
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* load_full = reinterpret_cast<uint64_t*>(smem + Smem::kOffBar);
+    uint64_t* load_empty = load_full + kStages;
+    uint64_t* a_full = load_empty + kStages;
+    uint64_t* a_empty = a_full + kAStages;
+    uint64_t* acc_full = a_empty + kAStages;
+    uint64_t* acc_empty = acc_full + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = p.ksplit;
+    const int ntiles = p.NS * p.MT;
+    // S == 1: persistent, tiles blockIdx.x, + gridDim.x, ...; S > 1: cluster c owns tile c.
+    const int tile0 = S > 1 ? (int)blockIdx.x / S : (int)blockIdx.x;
+    const int tstep = S > 1 ? ntiles : (int)gridDim.x;
+    const int kslice = S > 1 ? (int)blockIdx.x % S : 0;
+    const int per = (p.Kc + S - 1) / S;
+    const int k0 = kslice * per;                       // first weight block of this CTA's K range
+    const int KT = max(0, min(p.Kc, k0 + per) - k0);   // weight blocks per tile
+    const int NST = (KT + kSub - 1) / kSub;            // pipeline stages per tile
+    const uint32_t xsub = (uint32_t)p.TT * TK * 2;     // bytes of one X box
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&load_full[s], 1);
+            mbar_init(&load_empty[s], 1 + kDq);  // the MMA (X read) and every dequant warp (blocks read)
+        }
+        for (int s = 0; s < kAStages; ++s) {
+            mbar_init(&a_full[s], kDq);
+            mbar_init(&a_empty[s], 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kEpi);
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_trigger();
+    // Only the TMA thread (after its weight prefetch) and the epilogue touch memory that a
+    // predecessor kernel may still be producing (X) or reading (Y).
+    if (warp >= 2 + kDq) pdl_wait();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tensor_map(&xmap);
+            int pre = 0;
+            for (int t = tile0; t < ntiles && pre < kStages; t += tstep)
+                for (int j = 0; j < NST && pre < kStages; ++j, ++pre) {
+                    const int ws = t / p.MT, nsub = min(kSub, KT - j * kSub);
+                    mbar_arrive_expect_tx(&load_full[pre], (uint32_t)nsub * (xsub + kBlkBytes));
+                    bulk_load(smem + Smem::kOffBlk + pre * kSub * kBlkBytes,
+                              p.tblk + ((size_t)ws * p.Kc + k0 + j * kSub) * kBlkBytes, nsub * kBlkBytes,
+                              &load_full[pre]);
+                }
+            pdl_wait();
+            bool ok = true;
+            int g = 0;
+            for (int t = tile0; t < ntiles && ok; t += tstep) {
+                const int ws = t / p.MT, ms = t % p.MT;
+                for (int j = 0; j < NST; ++j, ++g) {
+                    const int s = g % kStages, nsub = min(kSub, KT - j * kSub);
+                    if (g >= kStages) {
+                        if (!mbar_wait(&load_empty[s], ((g / kStages) - 1) & 1, p.err, 0x101)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&load_full[s], (uint32_t)nsub * (xsub + kBlkBytes));
+                        bulk_load(smem + Smem::kOffBlk + s * kSub * kBlkBytes,
+                                  p.tblk + ((size_t)ws * p.Kc + k0 + j * kSub) * kBlkBytes, nsub * kBlkBytes,
+                                  &load_full[s]);
+                    }
+                    for (int u = 0; u < nsub; ++u)
+                        tma_load_2d(smem + Smem::kOffX + s * kXBytes + u * kXSub, &xmap, &load_full[s],
+                                    (k0 + j * kSub + u) * TK, ms * p.TT);
+                }
+            }
+            // Drain: our copies must land before the CTA can exit.
+            for (int j = g > kStages ? g - kStages : 0; j < g; ++j)
+                mbar_wait(&load_full[j % kStages], (j / kStages) & 1, p.err, 0x102);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // -------------------------------------------------------------- MMA issuer
+        if (lane == 0 && KT > 0) {
+            const uint32_t idesc = mma_idesc_bf16(TW, p.TT);
+            bool ok = true;
+            int g = 0, tj = 0;
+            for (int t = tile0; t < ntiles && ok; t += tstep, ++tj) {
+                if (tj > 0 && !mbar_wait(acc_empty, (tj - 1) & 1, p.err, 0x103)) break;  // epilogue drained the accumulator
+                tc_fence_after();
+                for (int j = 0; j < NST; ++j, ++g) {
+                    const int s = g % kStages, sa = g % kAStages, nsub = min(kSub, KT - j * kSub);
+                    if (!mbar_wait(&load_full[s], (g / kStages) & 1, p.err, 0x104) ||
+                        !mbar_wait(&a_full[sa], (g / kAStages) & 1, p.err, 0x105)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t xa = smem_u32(smem + Smem::kOffX + s * kXBytes);
+                    const uint32_t aa = tmem + kACol + sa * (kSub * 32);
+#pragma unroll
+                    for (int u = 0; u < kSub; ++u)
+                        if (u < nsub)
+#pragma unroll
+                            for (int ks = 0; ks < TK / 16; ++ks)
+                                tc_mma_ts(tmem + kAccCol, aa + u * 32 + ks * 8, sw128_desc(xa + u * kXSub + ks * 32),
+                                          idesc, (j > 0 || u > 0 || ks > 0) ? 1u : 0u);
+                    tc_commit(&a_empty[sa]);    // weight stage consumed
+                    tc_commit(&load_empty[s]);  // X stage consumed
+                }
+                tc_commit(acc_full);  // tile complete (or abandoned after a timeout)
+            }
+        }
+        __syncwarp();
+    } else if (warp < 2 + kDq) {
+        // ---------------------------------------------------------- dequantisers
+        const int q = warp & 3, h = (warp - 2) >> 2;  // lane quarter, weight block of the stage
+        const int r = 32 * q + lane;                   // weight row of the tile = TMEM lane
+        const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + kACol + h * 32;
+        bool ok = true;
+        int g = 0;
+        for (int t = tile0; t < ntiles && ok; t += tstep) {
+            for (int j = 0; j < NST; ++j, ++g) {
+                const int s = g % kStages, sa = g % kAStages;
+                const bool live = h < min(kSub, KT - j * kSub);
+                ok = mbar_wait_warp(&load_full[s], (g / kStages) & 1, p.err, 0x106);
+                if (ok && g >= kAStages) ok = mbar_wait_warp(&a_empty[sa], ((g / kAStages) - 1) & 1, p.err, 0x107);
+                if (!ok) break;
+                if (live) {
+                    const uint8_t* blk = smem + Smem::kOffBlk + (s * kSub + h) * kBlkBytes;
+                    uint32_t o[32];
+#pragma unroll
+                    for (int half = 0; half < 2; ++half) {
+                        const uint4 wv = *reinterpret_cast<const uint4*>(blk + half * 2048 + r * 16);
+                        const uint32_t sb = *reinterpret_cast<const uint16_t*>(blk + 4096 + half * 256 + r * 2);
+                        const uint32_t s2 = sb | (sb << 16);
+                        const uint32_t w[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                        for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+                            for (int pp = 0; pp < 4; ++pp) {
+                                // nibble pair pp of word wi = columns 32 half + 8 wi + 2 pp, +1
+                                const uint32_t qv = int4pair_to_bf16x2(w[wi] >> (4 * pp));
+                                asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(o[half * 16 + wi * 4 + pp]) : "r"(qv), "r"(s2));
+                            }
+                    }
+                    tmem_st_32x32b_x32(ta + sa * (kSub * 32), o);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&load_empty[s]);  // the blocks' registers are consumed above
+                if (live) tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[sa]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------- epilogue
+        const int q = warp & 3, e = (warp - 2 - kDq) >> 2;
+        const int rt = 32 * q + lane;  // weight row of the tile = TMEM lane
+        const uint32_t tq = tmem + ((uint32_t)(32 * q) << 16) + kAccCol;
+        const int cbeg = 128 * e, cend = min(p.TT, cbeg + 128);  // this warp's token columns
+        const bool odd = lane & 1;
+        int tj = 0;
+        for (int t = tile0; t < ntiles; t += tstep, ++tj) {
+            const int ws = t / p.MT, ms = t % p.MT;
+            if (S > 1) {
+                // park the FP32 partial as [token][weight row] in the (idle) X ring
+                float* part = reinterpret_cast<float*>(smem);
+                if (KT == 0) {  // an empty K slice contributes zeros
+                    for (int c = cbeg; c < cend; ++c) part[c * kPartPitch + rt] = 0.f;
+                } else if (mbar_wait_warp(acc_full, 0, p.err, 0x108)) {
+                    tc_fence_after();
+                    for (int c = cbeg; c < cend; c += 32) {
+                        uint32_t v[32];
+                        tmem_ld_32x32b_x32(tq + c, v);
+                        tmem_ld_wait(v);
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) part[(c + jj) * kPartPitch + rt] = __uint_as_float(v[jj]);
+                    }
+                }
+                break;  // one tile per CTA
+            }
+            if (!mbar_wait_warp(acc_full, tj & 1, p.err, 0x109)) break;
+            tc_fence_after();
+            // Lane pairs (2i, 2i+1) hold weight rows n, n+1: for tokens (jj, jj+1) the even
+            // lane stores (n, n+1) of token jj and the odd lane (n, n+1) of token jj + 1.
+            const int n = ws * TW + 32 * q + (lane & ~1);
+            uint32_t va[32], vb[32];
+            if (cbeg < cend) {
+                tmem_ld_32x32b_x32(tq + cbeg, va);
+                tmem_ld_wait(va);
+            }
+#pragma unroll
+            for (int ci = 0; ci < 4; ++ci) {
+                const int c = cbeg + 32 * ci;
+                uint32_t(&cur)[32] = (ci & 1) ? vb : va;
+                uint32_t(&nxt)[32] = (ci & 1) ? va : vb;
+                const bool have = c < cend, more = c + 32 < cend;
+                if (more) tmem_ld_32x32b_x32(tq + c + 32, nxt);
+                if (!more && (have || ci == 0)) {  // everything this warp needs is in registers
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(acc_empty);
+                }
+                if (have) {  // warp-uniform: every lane takes part in the shuffles
+                    const int m0 = ms * p.TT + c;
+                    const bool col_ok = n < p.N;  // N % 8 == 0: n and n + 1 are both in or both out
+#pragma unroll
+                    for (int jj = 0; jj < 32; jj += 2) {
+                        const uint32_t send = odd ? cur[jj] : cur[jj + 1];
+                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const float lo = __uint_as_float(odd ? recv : cur[jj]);
+                        const float hi = __uint_as_float(odd ? cur[jj + 1] : recv);
+                        const int m = m0 + jj + (odd ? 1 : 0);
+                        if (col_ok && m < p.M) {
+                            if (p.y_f32) {
+                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + n) =
+                                    make_float2(lo, hi);
+                            } else {
+                                __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+                                *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * p.ldy +
+                                                                   n) = b2;
+                            }
+                        }
+                    }
+                }
+                if (more) tmem_ld_wait(nxt);
+            }
+        }
+        __syncwarp();
+    }
+
+    if (S > 1) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        split_reduce(smem, cluster, S, kslice, tile0 / p.MT, tile0 % p.MT, p);
+        cluster.sync();  // peers may still be reading this CTA's partial
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+namespace g4 {
+
+// Tiles: 128 weight rows x T tokens (T = M rounded up to 32, at most 256).  With at least
+// one tile per SM the grid is persistent (one CTA per SM walking the tiles, token tile
+// fastest so concurrent CTAs share the weight slabs in L2); otherwise K is split over a
+// cluster of up to 8 CTAs (>= 4 steps each).
+g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32) {
+    const g4_linear_dev& L = lin->dev;
+    if (!gemm_supported(lin, M)) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: shape K=%d N=%d", L.K, L.N);
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_w4_tmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Smem::kBytes));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    W4Params p{};
+    p.tblk = L.tblk;
+    p.y = y;
+    p.M = M;
+    p.N = L.N;
+    p.ldy = L.N;
+    p.y_f32 = y_f32;
+    p.Kc = L.Kc;
+    p.NS = L.NS;
+    p.TT = M >= TTmax ? TTmax : (M + 31) / 32 * 32;
+    p.MT = (M + p.TT - 1) / p.TT;
+    p.err = ctx->d_err;
+    CUtensorMap xmap;
+    g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
+                                        (uint64_t)L.K * 2, TK, p.TT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    const long long ntiles = (long long)p.NS * p.MT;
+    if (ntiles > 0x7fffffffLL) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: M=%d N=%d too large", M, L.N);
+    int S = 1;
+    while (S < 8 && ntiles * (S + 1) <= ctx->num_sms && p.Kc / (S + 1) >= 4) ++S;
+    p.ksplit = S;
+    const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
+    return launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel, dim3(grid), dim3(kThreads), Smem::kBytes, S, xmap,
+                  p);
+}
+
+}  // namespace g4

@@ -74,6 +74,26 @@ __global__ void repack_kernel(const uint32_t* __restrict__ raw, const uint16_t* 
                                         (uint32_t)sc[2] | ((uint32_t)sc[3] << 16));
 }
 
+// GEMM layout (g4_linear_dev::tblk): thread i fills row r = i % 128, half h = (i / 128) % 2
+// of block b = i / 256 (slab b / Kc, step b % Kc): 16 bytes of nibbles and one scale.
+__global__ void repack_tblk_kernel(const uint32_t* __restrict__ raw, const uint16_t* __restrict__ raw_s, int K,
+                                   int N, int Kc, int NS, uint8_t* __restrict__ tblk) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)NS * Kc * 256) return;
+    const int r = (int)(i & 127), h = (int)((i >> 7) & 1);
+    const long long b = i >> 8;
+    const int kc = (int)(b % Kc), ws = (int)(b / Kc);
+    const int row = ws * 128 + r, G = kc * 2 + h;  // G: group of 32 columns
+    const int groups = K / 32, words = K / 8;
+    const bool ok = row < N && G < groups;
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = ok ? permute_nibbles(raw[(size_t)row * words + G * 4 + j]) : 0x88888888u;
+    uint8_t* blk = tblk + b * g4::kTblkBytes;
+    *reinterpret_cast<uint4*>(blk + h * 2048 + r * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint16_t*>(blk + 4096 + h * 256 + r * 2) = ok ? raw_s[(size_t)row * groups + G] : (uint16_t)0;
+}
+
 // Reads one original word back out of the fragment layout.
 __device__ __forceinline__ void locate(const g4_linear_dev& L, int row, int word, uint32_t& w,
                                        uint32_t& sbits) {
@@ -331,11 +351,13 @@ g4_status g4_linear_create(g4_ctx* ctx, const void* packed_i32, const void* scal
     L.N = N;
     L.Kc = (K + 63) / 64;
     L.NT = (N + 15) / 16;
+    L.NS = (N + 127) / 128;
     const size_t raw_w = (size_t)N * (K / 8) * 4, raw_s = (size_t)N * (K / 32) * 2;
     const size_t nblk = (size_t)L.NT * L.Kc;
     void *dw = nullptr, *ds = nullptr;
     cudaError_t e = cudaMalloc(&L.wfrag, nblk * 32 * sizeof(uint4));
     if (e == cudaSuccess) e = cudaMalloc(&L.sfrag, nblk * 8 * sizeof(uint2));
+    if (e == cudaSuccess) e = cudaMalloc(&L.tblk, (size_t)L.NS * L.Kc * g4::kTblkBytes);
     if (e == cudaSuccess && !src_on_device) {
         e = cudaMalloc(&dw, raw_w);
         if (e == cudaSuccess) e = cudaMalloc(&ds, raw_s);
@@ -350,6 +372,13 @@ g4_status g4_linear_create(g4_ctx* ctx, const void* packed_i32, const void* scal
                                                                                   L.wfrag, L.sfrag);
         e = cudaGetLastError();
         g4::count_launch();
+        const long long tthreads = (long long)L.NS * L.Kc * 256;
+        if (e == cudaSuccess) {
+            repack_tblk_kernel<<<(unsigned)((tthreads + 255) / 256), 256, 0, ctx->stream>>>(rw, rs, K, N, L.Kc, L.NS,
+                                                                                           L.tblk);
+            e = cudaGetLastError();
+            g4::count_launch();
+        }
     }
     if (e == cudaSuccess && !src_on_device) e = cudaStreamSynchronize(ctx->stream);
     cudaFree(dw);
@@ -357,11 +386,6 @@ g4_status g4_linear_create(g4_ctx* ctx, const void* packed_i32, const void* scal
     if (e != cudaSuccess) {
         g4_linear_destroy(lin);
         return g4::cuda_error(e, "g4_linear_create");
-    }
-    st = g4::make_linear_maps(lin);
-    if (st) {
-        g4_linear_destroy(lin);
-        return st;
     }
     *out = lin;
     return G4_OK;
@@ -372,6 +396,7 @@ g4_status g4_linear_destroy(g4_linear* lin) {
     if (lin->ctx) cudaSetDevice(lin->ctx->device);
     cudaFree(lin->dev.wfrag);
     cudaFree(lin->dev.sfrag);
+    cudaFree(lin->dev.tblk);
     delete lin;
     return G4_OK;
 }

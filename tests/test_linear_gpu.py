@@ -104,6 +104,17 @@ def test_tcgen05_gemm_matches_oracle(rt, ctx, ops, oracle, K, N, M):
     assert max_rel(y, ref) < TOL
 
 
+@pytest.mark.parametrize("M,K,N", [
+    (600, 256, 8960),   # 210 tiles of 128 rows x 256 tokens: persistent CTAs walk 1-2 tiles each
+    (2048, 96, 2560),   # 160 tiles, a half-empty last K step
+    (40, 2112, 264),    # split K over 8 CTAs with 33 steps: the last CTA's K slice is empty
+    (300, 6144, 1536),  # two token tiles (256 + 44), split K
+])
+def test_tcgen05_gemm_tiling_edges(rt, ctx, ops, oracle, M, K, N):
+    y, ref = _run(rt, ctx, ops, oracle, K, N, M, impl=2, seed=M + K + N)
+    assert max_rel(y, ref) < TOL
+
+
 @pytest.mark.parametrize("M,K,N", [(256, 1536, 6144), (130, 6144, 1536), (64, 96, 40)])
 def test_tcgen05_gemm_vs_torch_fp32_on_bf16_weights(rt, ctx, ops, oracle, M, K, N):
     """The GEMM multiplies bf16 activations by the bf16 materialisation of the weights
