@@ -191,6 +191,8 @@ def ple_setup(torch, rt, ctx, n_batches, T=4096, vocab=262144, width=8960, seed=
 
 
 PLE_BYTES = 4096 * (4480 + 560) + 4096 * 4 + 4096 * 8960 * 2   # 94,060,544 B per call
+GEMV_BYTES = 6144 * 1536 // 2 + 6144 * 1536 // 32 * 2 + 1536 * 2 + 6144 * 2   # 5,323,776 B per call
+ATTN_BYTES = 4096 * 256 * 2 * 2 + 2 * 8 * 256 * 2   # K and V at keylen 4096, q and out: 4,202,496 B
 
 
 def run_ple(args, torch, rt, ctx, dist, peaks):
@@ -283,7 +285,7 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
     ms = time_graph(torch, ctx, launch, K, W, dist)
     clocks = clk.stop()
     launches = rt.launch_count() - n0 - W
-    byts = N * Kd // 2 + N * Kd // 32 * 2 + Kd * 2 + N * 2   # 5,323,776
+    byts = GEMV_BYTES
     per = ms / 1e3 / K
     gbs = byts / per / 1e9
     peak = peaks["hbm_gbs"]
@@ -324,7 +326,7 @@ def run_attn(args, torch, rt, ctx, dist, peaks):
     ms = time_graph(torch, ctx, launch, K, W, dist)
     clocks = clk.stop()
     launches = rt.launch_count() - n0 - W
-    byts = keylen * hd * 2 * 2 + 2 * 8 * hd * 2
+    byts = ATTN_BYTES
     per = ms / 1e3 / K
     gbs = byts / per / 1e9
     peak = peaks["hbm_gbs"]
@@ -629,49 +631,129 @@ def cpu_ple(sample_s: float, threads: int, vocab_sample: int = 8192):
             "calls_per_s": round(n / dt, 4)}
 
 
-def cpu_decode(batch: int, ctx_len: int, threads: int = 1, model_layers: int = 35):
-    """Times one greedy decode step of the restated TFJS path on the host: every linear of
-    the 35 layers dequantised on each call and multiplied in f32 (official-quantized-linear.js:82-128),
-    attention over ctx_len keys per layer, the f32 tied head over 262144 rows."""
-    import numpy as np
-    oracle, L = native_oracle()
-    rng = np.random.default_rng(0)
-    shapes = {"qkv": (2560, 1536), "o": (1536, 2048), "gu": (12288, 1536), "down": (1536, 6144), "pg": (256, 1536),
+class CpuDecode:
+    """One greedy decode step of the restated TFJS path on the host: every linear of the 35
+    layers dequantised on each call and multiplied in f32 (official-quantized-linear.js:82-128),
+    attention over the context per layer (window 512 on 4 of 5 layers), the f32 tied head
+    over 262144 rows (a BLAS matmul)."""
+
+    SHAPES = {"qkv": (2560, 1536), "o": (1536, 2048), "gu": (12288, 1536), "down": (1536, 6144), "pg": (256, 1536),
               "pp": (1536, 256), "top": (8960, 1536)}
-    W = {}
-    for k, (n, kk) in shapes.items():
-        W[k] = (rng.integers(0, 2**32, size=(n, kk // 8), dtype=np.uint64).astype(np.uint32).view(np.int32),
-                oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.02, (n, kk // 32))).astype(np.float32)))
-    head = rng.standard_normal((262144, 1536)).astype(np.float32) * 0.05
-    kc = rng.standard_normal((ctx_len + 1, 256)).astype(np.float32)
-    q = rng.standard_normal((batch, 8, 256)).astype(np.float32)
-    x = {k: rng.standard_normal((batch, kk)).astype(np.float32) for k, (n, kk) in shapes.items()}
-    t0 = time.perf_counter()
-    oracle.linear_w4a16(x["top"], *W["top"], nthreads=threads, L=L)
-    for layer in range(model_layers):
-        for k in ("qkv", "o", "gu", "down", "pg", "pp"):
-            oracle.linear_w4a16(x[k], *W[k], nthreads=threads, L=L)
-        full = (layer + 1) % 5 == 0
-        keys = ctx_len + 1 if full else min(ctx_len + 1, 512)
-        for b in range(batch):
-            oracle.attention(q[b:b + 1], kc[:keys], kc[:keys], keys - 1, not full, 512)
-    logits = x["top"][:, :1536] @ head.T
-    dt = time.perf_counter() - t0
-    del logits
+
+    def __init__(self, ctx_len: int, threads: int, layers: int = 35):
+        import numpy as np
+        self.np = np
+        self.oracle, self.L = native_oracle()
+        self.ctx_len, self.threads, self.layers = ctx_len, threads, layers
+        rng = np.random.default_rng(0)
+        self.W = {}
+        for k, (n, kk) in self.SHAPES.items():
+            self.W[k] = (rng.integers(0, 2**32, size=(n, kk // 8), dtype=np.uint64).astype(np.uint32).view(np.int32),
+                         self.oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.02, (n, kk // 32))).astype(np.float32)))
+        self.head = rng.standard_normal((262144, 1536)).astype(np.float32) * 0.05
+        self.kc = rng.standard_normal((ctx_len + 1, 256)).astype(np.float32)
+        self.rng = rng
+
+    def step(self, batch: int) -> float:
+        """Runs one decode step for `batch` sequences; returns its wall time in seconds."""
+        np, o, L = self.np, self.oracle, self.L
+        q = self.rng.standard_normal((batch, 8, 256)).astype(np.float32)
+        x = {k: self.rng.standard_normal((batch, kk)).astype(np.float32) for k, (n, kk) in self.SHAPES.items()}
+        t0 = time.perf_counter()
+        o.linear_w4a16(x["top"], *self.W["top"], nthreads=self.threads, L=L)
+        for layer in range(self.layers):
+            for k in ("qkv", "o", "gu", "down", "pg", "pp"):
+                o.linear_w4a16(x[k], *self.W[k], nthreads=self.threads, L=L)
+            full = (layer + 1) % 5 == 0
+            keys = self.ctx_len + 1 if full else min(self.ctx_len + 1, 512)
+            for b in range(batch):
+                o.attention(q[b:b + 1], self.kc[:keys], self.kc[:keys], keys - 1, not full, 512)
+        logits = x["top"][:, :1536] @ self.head.T
+        dt = time.perf_counter() - t0
+        del logits
+        return dt
+
+
+def cpu_decode(batch: int, ctx_len: int, threads: int = 1, model_layers: int = 35):
+    """The cpu_baseline object: one decode step of CpuDecode on `threads` host threads."""
+    dt = CpuDecode(ctx_len, threads, model_layers).step(batch)
     return {"value": round(batch / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port",
             "sample": f"one decode step of {batch} sequence(s) at context {ctx_len}: {model_layers} layers x 6 W4A16 linears "
                       f"(dequantised per call) + attention + f32 tied head, {dt:.1f} s"}
 
 
+def _reference_line(args, dist, metric, value, unit, ms, config, dtype, sample, threads, hib=True):
+    return {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": dist.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": hib,
+            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)", "config": config,
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def run_reference(args, dist):
-    """Reference arm: the CPU restatement of the TFJS path, all host threads, rank 0 only."""
+    """Reference arm: the CPU restatement of the TFJS path (the oracle port; the JS
+    reference itself has no runtime in this image), all host threads, rank 0 only, on
+    a bounded sample of the same workload per step."""
     threads = os.cpu_count() or 1
-    if args.workload != "ple":
-        return {"impl": "reference", "unavailable": f"reference arm implemented for workload ple only"}
     K, W = args.steps, args.warmup
     import numpy as np
+    if args.workload in ("serve", "decode"):
+        # a step: one greedy decode step of one sequence of the batch (all 35 layers, the
+        # full head); serve at context 4096, decode (config 4) at the 2048-token prompt
+        ctx_len = 4096 if args.workload == "serve" else 2048
+        m = CpuDecode(ctx_len, threads)
+        for _ in range(W):
+            m.step(1)
+        dt = sum(m.step(1) for _ in range(K))
+        v = round(K / dt, 5)
+        if args.workload == "serve":
+            metric, config = "batched greedy decode throughput (config 5)", {
+                "workload": "config5_serve", "global_batch": 256, "seq_len": 4096, "parallelism": f"replicas{dist.world}"}
+        else:
+            metric, config = "greedy decode throughput, batch 1 (config 4)", {
+                "workload": "config4_decode", "global_batch": 1, "seq_len": 2048, "parallelism": "replica"}
+        return _reference_line(args, dist, metric, v, "tok/s", dt / K * 1e3, config, "f32",
+                               f"{K} decode steps of 1 sequence at context {ctx_len} (35 layers x 6 W4A16 linears "
+                               f"dequantised per call, attention, f32 tied head)", threads)
     oracle, L = native_oracle()
     rng = np.random.default_rng(0)
+    if args.workload in ("gemv", "gemm"):
+        Kd, N, M = (1536, 6144, 1) if args.workload == "gemv" else (1536, 6144, 512)
+        packed = rng.integers(0, 2**32, size=(N, Kd // 8), dtype=np.uint64).astype(np.uint32).view(np.int32)
+        scales = oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.02, (N, Kd // 32))).astype(np.float32))
+        x = rng.standard_normal((M, Kd)).astype(np.float32)
+        for _ in range(W):
+            oracle.linear_w4a16(x, packed, scales, nthreads=threads, L=L)
+        t0 = time.perf_counter()
+        for _ in range(K):
+            oracle.linear_w4a16(x, packed, scales, nthreads=threads, L=L)
+        dt = time.perf_counter() - t0
+        if args.workload == "gemv":
+            v = round(GEMV_BYTES * K / dt / 1e9, 4)
+            return _reference_line(args, dist, "W4A16 decode GEMV throughput (algorithmic bytes)", v, "GB/s",
+                                   dt / K * 1e3, {"workload": "config1_gemv", "M": 1, "K": Kd, "N": N}, "f32",
+                                   f"{K} calls of the dequantise-then-matmul linear (official-quantized-linear.js:82-128)",
+                                   threads)
+        v = round(2.0 * M * N * Kd * K / dt / 1e12, 5)
+        return _reference_line(args, dist, "W4A16 prefill GEMM throughput (config 3 sweep)", v, "TFLOP/s",
+                               dt / K * 1e3, {"workload": "config3_gemm", "sample": f"M={M} K={Kd} N={N}"}, "f32",
+                               f"{K} calls at M={M}, (K, N) = ({Kd}, {N}), one point of the config 3 sweep", threads)
+    if args.workload == "attn":
+        keylen, hd = 4096, 256
+        kc = rng.standard_normal((keylen, hd)).astype(np.float32)
+        vc = rng.standard_normal((keylen, hd)).astype(np.float32)
+        q = rng.standard_normal((1, 8, hd)).astype(np.float32)
+        for _ in range(W):
+            oracle.attention(q, kc, vc, keylen - 1, False, 512)
+        t0 = time.perf_counter()
+        for _ in range(K):
+            oracle.attention(q, kc, vc, keylen - 1, False, 512)
+        dt = time.perf_counter() - t0
+        v = round(ATTN_BYTES * K / dt / 1e9, 4)
+        return _reference_line(args, dist, "GQA decode attention throughput (algorithmic bytes)", v, "GB/s",
+                               dt / K * 1e3, {"workload": "decode_attention_global", "keylen": keylen, "hd": hd,
+                                              "heads": 8}, "f32", f"{K} global-attention decode calls, one thread",
+                               1)
     vs = 8192
     q = rng.integers(-7, 8, size=(vs, 8960), dtype=np.int8)
     nib = (q.astype(np.int16) & 0xF).astype(np.uint8)
