@@ -682,10 +682,10 @@ def cpu_decode(batch: int, ctx_len: int, threads: int = 1, model_layers: int = 3
                       f"(dequantised per call) + attention + f32 tied head, {dt:.1f} s"}
 
 
-def _reference_line(args, dist, metric, value, unit, ms, config, dtype, sample, threads, hib=True):
+def _reference_line(args, dist, metric, value, unit, ms, config, dtype, sample, threads, hib=True, scaling="weak"):
     return {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": hib,
-            "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)", "config": config,
+            "scaling": scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)", "config": config,
             "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
@@ -714,7 +714,8 @@ def run_reference(args, dist):
                 "workload": "config4_decode", "global_batch": 1, "seq_len": 2048, "parallelism": "replica"}
         return _reference_line(args, dist, metric, v, "tok/s", dt / K * 1e3, config, "f32",
                                f"{K} decode steps of 1 sequence at context {ctx_len} (35 layers x 6 W4A16 linears "
-                               f"dequantised per call, attention, f32 tied head)", threads)
+                               f"dequantised per call, attention, f32 tied head)", threads,
+                               scaling="strong" if args.workload == "serve" else "weak")
     oracle, L = native_oracle()
     rng = np.random.default_rng(0)
     if args.workload in ("gemv", "gemm"):

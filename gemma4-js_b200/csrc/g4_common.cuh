@@ -163,14 +163,17 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+// One poll.  A thread whose phase is not complete is suspended (it does not take issue
+// slots from the warps doing work) until the phase completes or kPollSuspendNs passes.
+constexpr uint32_t kPollSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kPollSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -180,7 +183,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer_ns();
     for (;;) {
-        for (int i = 0; i < 32; ++i)
+        for (int i = 0; i < 4; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         if (globaltimer_ns() - t0 > kWaitLimitNs) break;
     }
@@ -217,6 +220,18 @@ __device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// TMA tile store shared -> global (elements outside the tensor are not written), tracked as
+// a bulk async-group of the issuing thread.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the shared-memory sources of this thread's bulk groups have been read.
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until this thread's bulk groups have completed (global writes performed).
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---- warp MMA (legacy HMMA path; used where the op is HBM-bound) ----
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4],

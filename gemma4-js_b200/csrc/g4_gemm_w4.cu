@@ -80,7 +80,18 @@ struct W4Params {
 
 // Split-K: this rank sums tokens kslice, kslice + S, ... of the tile over the S parked
 // partials ([TT][kPartPitch] f32 in each rank's shared memory) in rank order and stores
-// them; 32 threads per token row, 4 weight rows each.
+// them; 32 threads per token row, 4 weight rows each.  Each thread takes two items at a
+// time and issues all 2 x S distributed-shared-memory loads before summing (the loads are
+// latency-bound, not bandwidth-bound).
+__device__ __forceinline__ void store4(const W4Params& p, int m, int n, float4 acc) {
+    if (p.y_f32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + n) = acc;
+    } else {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * p.ldy + n) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+    }
+}
 __device__ __forceinline__ void split_reduce(uint8_t* smem, cg::cluster_group& cluster, int S, int kslice, int ws,
                                              int ms, const W4Params& p) {
     const float* peer[8];
@@ -88,36 +99,45 @@ __device__ __forceinline__ void split_reduce(uint8_t* smem, cg::cluster_group& c
     for (int r = 0; r < 8; ++r)
         peer[r] = cluster.map_shared_rank(reinterpret_cast<float*>(smem), r < S ? r : 0);
     const int ntok = (p.TT - kslice + S - 1) / S;
-    for (int idx = threadIdx.x; idx < ntok * 32; idx += kThreads) {
-        const int tl = kslice + (idx >> 5) * S;
-        const int c4 = (idx & 31) * 4;
-        const int m = ms * p.TT + tl, n = ws * TW + c4;
-        if (m >= p.M || n >= p.N) continue;  // N % 8 == 0: the 4 rows are all in or all out
-        float4 v[8];
+    const int items = ntok * 32;
+    constexpr int kT = 512;  // threads taking part (16 warps)
+    if (threadIdx.x >= kT) return;
+    for (int i0 = threadIdx.x; i0 < items; i0 += 2 * kT) {
+        float4 v[2][8];
+        int m[2], n[2];
+        bool live[2];
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
-            if (r < S) v[r] = *reinterpret_cast<const float4*>(peer[r] + tl * kPartPitch + c4);
-        float4 acc = v[0];
+        for (int u = 0; u < 2; ++u) {
+            const int idx = i0 + u * kT;
+            const int tl = kslice + (idx >> 5) * S;
+            const int c4 = (idx & 31) * 4;
+            m[u] = ms * p.TT + tl;
+            n[u] = ws * TW + c4;
+            live[u] = idx < items && m[u] < p.M && n[u] < p.N;  // N % 8 == 0: 4 rows all in or all out
 #pragma unroll
-        for (int r = 1; r < 8; ++r)
-            if (r < S) {
-                acc.x += v[r].x;
-                acc.y += v[r].y;
-                acc.z += v[r].z;
-                acc.w += v[r].w;
-            }
-        if (p.y_f32) {
-            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + n) = acc;
-        } else {
-            __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-            *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * p.ldy + n) =
-                make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+            for (int r = 0; r < 8; ++r)
+                if (live[u] && r < S) v[u][r] = *reinterpret_cast<const float4*>(peer[r] + tl * kPartPitch + c4);
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            if (!live[u]) continue;
+            float4 acc = v[u][0];
+#pragma unroll
+            for (int r = 1; r < 8; ++r)
+                if (r < S) {
+                    acc.x += v[u][r].x;
+                    acc.y += v[u][r].y;
+                    acc.z += v[u][r].z;
+                    acc.w += v[u][r].w;
+                }
+            store4(p, m[u], n[u], acc);
         }
     }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const W4Params p) {
+gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
+                    const W4Params p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // Offset the __shared__ array itself (not an integer round trip) so the compiler keeps
     // shared-memory addressing for every access through `smem`.
@@ -142,6 +162,10 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const W4Params p) 
     const int KT = max(0, min(p.Kc, k0 + per) - k0);   // weight blocks per tile
     const int NST = (KT + kSub - 1) / kSub;            // pipeline stages per tile
     const uint32_t xsub = (uint32_t)p.TT * TK * 2;     // bytes of one X box
+    // bf16 output of an unsplit tile leaves through a TMA store staged in the X stage that
+    // the tile's last MMAs read: that stage is handed back to the producer by the epilogue
+    // (after the store has read it) instead of by the MMA commit.
+    const bool staged = S == 1 && !p.y_f32;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -232,8 +256,8 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const W4Params p) 
                             for (int ks = 0; ks < TK / 16; ++ks)
                                 tc_mma_ts(tmem + kAccCol, aa + u * 32 + ks * 8, sw128_desc(xa + u * kXSub + ks * 32),
                                           idesc, (j > 0 || u > 0 || ks > 0) ? 1u : 0u);
-                    tc_commit(&a_empty[sa]);    // weight stage consumed
-                    tc_commit(&load_empty[s]);  // X stage consumed
+                    tc_commit(&a_empty[sa]);                                  // weight stage consumed
+                    if (!(staged && j == NST - 1)) tc_commit(&load_empty[s]);  // X stage consumed
                 }
                 tc_commit(acc_full);  // tile complete (or abandoned after a timeout)
             }
@@ -311,51 +335,68 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const W4Params p) 
             }
             if (!mbar_wait_warp(acc_full, tj & 1, p.err, 0x109)) break;
             tc_fence_after();
-            // Lane pairs (2i, 2i+1) hold weight rows n, n+1: for tokens (jj, jj+1) the even
-            // lane stores (n, n+1) of token jj and the odd lane (n, n+1) of token jj + 1.
-            const int n = ws * TW + 32 * q + (lane & ~1);
-            uint32_t va[32], vb[32];
-            if (cbeg < cend) {
-                tmem_ld_32x32b_x32(tq + cbeg, va);
-                tmem_ld_wait(va);
-            }
+            if (staged) {
+                // Drain the accumulator into the X stage as bf16 [T][128] (row = token), release
+                // it after the last TMEM load, then one thread stores the tile with TMA.
+                const int slast = ((tj + 1) * NST - 1) % kStages;
+                uint16_t* stg = reinterpret_cast<uint16_t*>(smem + Smem::kOffX + slast * kXBytes);
+                for (int c = cbeg; c < cend || (c == cbeg && cbeg >= cend); c += 32) {
+                    uint32_t v[32];
+                    const bool have = c < cend;
+                    if (have) {
+                        tmem_ld_32x32b_x32(tq + c, v);
+                        tmem_ld_wait(v);
+                    }
+                    if (c + 32 >= cend) {  // everything this warp needs is in registers
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(acc_empty);
+                    }
+                    if (!have) break;
+                    uint16_t* col = stg + (size_t)c * TW + rt;  // token c, weight row rt
 #pragma unroll
-            for (int ci = 0; ci < 4; ++ci) {
-                const int c = cbeg + 32 * ci;
-                uint32_t(&cur)[32] = (ci & 1) ? vb : va;
-                uint32_t(&nxt)[32] = (ci & 1) ? va : vb;
-                const bool have = c < cend, more = c + 32 < cend;
-                if (more) tmem_ld_32x32b_x32(tq + c + 32, nxt);
-                if (!more && (have || ci == 0)) {  // everything this warp needs is in registers
+                    for (int jj = 0; jj < 32; jj += 2) {
+                        __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]));
+                        const uint32_t bits = *reinterpret_cast<uint32_t*>(&b2);
+                        col[jj * TW] = (uint16_t)(bits & 0xFFFFu);
+                        col[(jj + 1) * TW] = (uint16_t)(bits >> 16);
+                    }
+                }
+                fence_proxy_async_smem();  // the generic stores, before the async-proxy read
+                asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
+                if (warp == 2 + kDq && lane == 0) {
+                    tma_store_2d(&ymap, stg, ws * TW, ms * p.TT);
+                    bulk_commit_group();
+                    bulk_wait_read_all();
+                    mbar_arrive(&load_empty[slast]);  // the producer may refill the stage
+                }
+                continue;
+            }
+            // FP32 output: one chunk at a time, each lane stores its weight row's 32 tokens.
+            const int n = ws * TW + rt;
+            for (int c = cbeg; c < cend || (c == cbeg && cbeg >= cend); c += 32) {
+                uint32_t v[32];
+                const bool have = c < cend;
+                if (have) {
+                    tmem_ld_32x32b_x32(tq + c, v);
+                    tmem_ld_wait(v);
+                }
+                if (c + 32 >= cend) {  // everything this warp needs is in registers
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(acc_empty);
                 }
-                if (have) {  // warp-uniform: every lane takes part in the shuffles
-                    const int m0 = ms * p.TT + c;
-                    const bool col_ok = n < p.N;  // N % 8 == 0: n and n + 1 are both in or both out
+                if (!have) break;
+                const int m0 = ms * p.TT + c;
+                if (n < p.N) {
+                    float* yp = reinterpret_cast<float*>(p.y) + (size_t)m0 * p.ldy + n;
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj += 2) {
-                        const uint32_t send = odd ? cur[jj] : cur[jj + 1];
-                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
-                        const float lo = __uint_as_float(odd ? recv : cur[jj]);
-                        const float hi = __uint_as_float(odd ? cur[jj + 1] : recv);
-                        const int m = m0 + jj + (odd ? 1 : 0);
-                        if (col_ok && m < p.M) {
-                            if (p.y_f32) {
-                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + n) =
-                                    make_float2(lo, hi);
-                            } else {
-                                __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
-                                *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * p.ldy +
-                                                                   n) = b2;
-                            }
-                        }
-                    }
+                    for (int jj = 0; jj < 32; ++jj)
+                        if (m0 + jj < p.M) yp[(size_t)jj * p.ldy] = __uint_as_float(v[jj]);
                 }
-                if (more) tmem_ld_wait(nxt);
             }
         }
+        if (staged && warp == 2 + kDq && lane == 0) bulk_wait_all();  // the tile stores have landed
         __syncwarp();
     }
 
@@ -406,6 +447,14 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
                                         (uint64_t)L.K * 2, TK, p.TT, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
+    CUtensorMap ymap = xmap;  // unused for f32 output
+    if (!y_f32) {
+        if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
+            return set_error(G4_ERR_INVALID, "tcgen05 GEMM: y must be 16-byte aligned");
+        st = encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW, p.TT,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (st) return st;
+    }
     const long long ntiles = (long long)p.NS * p.MT;
     if (ntiles > 0x7fffffffLL) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: M=%d N=%d too large", M, L.N);
     int S = 1;
@@ -413,7 +462,7 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     p.ksplit = S;
     const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
     return launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel, dim3(grid), dim3(kThreads), Smem::kBytes, S, xmap,
-                  p);
+                  ymap, p);
 }
 
 }  // namespace g4
