@@ -42,9 +42,20 @@ sys.path.insert(0, str(REPO))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu
-# captures (profiles/); None until a capture of that kernel exists.
-TRAFFIC = {"ple_gather_kernel": None, "gemv_w4a16_kernel": None, "attn_decode_kernel": None}
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu captures
+# (profiles/).  Writes that are still in L2 when a kernel ends are not counted by ncu.
+TRAFFIC = {
+    "ple_gather_kernel": 20_571_136 + 19_982_080,  # T = 4096 (profiles/ple_gather_kernel__config2_*)
+    "gemv_w4a16_kernel": 5_336_576,                # config 1 (profiles/gemv_w4a16_kernel__config1_*)
+    "attn_decode_kernel": 4_221_696,               # one sequence at keylen 4096 (profiles/attn_decode_kernel__dram_bytes_*)
+}
+
+
+def gemm_traffic(M: int, K: int, N: int) -> int:
+    """DRAM bytes of one W4A16 GEMM launch: packed weights + scales + X once each.  Checked
+    against the capture at M=2048, K=1536, N=6144 (11,650,560 B measured, 11,599,872 B by this
+    formula; profiles/gemm_w4_tmem_kernel__config3_*); scaled by formula to other shapes."""
+    return N * K // 2 + N * (K // 32) * 2 + M * K * 2
 
 
 def load_peaks():
@@ -407,7 +418,9 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
         "config": {"workload": "config3_gemm_sweep", "l2": "rotating weight copies (> 256 MB per rotation)"},
         "roofline": {"bound": "tensor", "kernel": "gemm_w4a16_tcgen05_kernel", "achieved": round(best["tflops"], 1),
                      "peak": peak, "unit": "TFLOP/s", "frac": round(best["tflops"] / peak, 4),
-                     "peak_source": peaks["source"], "traffic": None, "point": best},
+                     "peak_source": peaks["source"], "traffic": gemm_traffic(best["M"], best["K"], best["N"]),
+                     "traffic_basis": "ncu DRAM bytes at M=2048 K=1536 N=6144 scaled by the weight + X bytes",
+                     "point": best},
         "sweep": points, "gpu_launches": rt.launch_count() - n0, "clocks": clocks,
     }
 
@@ -448,10 +461,12 @@ def _attn_roofline(torch, ctx, m, B, peaks, reps=20):
     keylen = int(m.seq_pos[:B].max().item()) + 1
     byts = B * keylen * hd * 2 * 2 + 2 * B * 8 * hd * 2
     gbs = byts / per / 1e9
-    return {"bound": "hbm", "kernel": "attn_decode_kernel (+ combine), global layer", "achieved": round(gbs, 1),
+    return {"bound": "hbm", "kernel": "attn_decode_kernel (+ combine when keys are split), global layer", "achieved": round(gbs, 1),
             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
-            "peak_source": peaks["source"], "traffic": TRAFFIC["attn_decode_kernel"], "bytes_per_launch": byts,
-            "us_per_launch": round(per * 1e6, 2)}
+            "peak_source": peaks["source"],
+            "traffic": int(TRAFFIC["attn_decode_kernel"] * B * keylen / 4096),
+            "traffic_basis": "ncu DRAM bytes of one sequence at keylen 4096, times the sequences and keys of this launch",
+            "bytes_per_launch": byts, "us_per_launch": round(per * 1e6, 2)}
 
 
 def run_serve(args, torch, rt, ctx, dist, peaks):
