@@ -274,6 +274,7 @@ def run_ple(args, torch, rt, ctx, dist, peaks):
 def run_gemv(args, torch, rt, ctx, dist, peaks):
     lib = importlib.import_module("gemma4-js_b200._lib").load()
     K, W = args.steps, args.warmup
+    ctx.set_pdl(not args.no_pdl)  # back-to-back linears overlap as they do inside a decode step
     Kd, N, copies = 1536, 6144, args.copies or 64
     gen = torch.Generator(device="cuda").manual_seed(0)
     lins = []
@@ -305,7 +306,8 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
         "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded)", "config": {"workload": "config1_gemv", "M": 1, "K": Kd, "N": N,
-                                                  "l2": "64 rotating weight copies (340 MB > 126 MB L2)"},
+                                                  "l2": "64 rotating weight copies (340 MB > 126 MB L2)",
+                                                  "pdl": not args.no_pdl},
         "roofline": {"bound": "hbm", "kernel": "gemv_w4a16_kernel", "achieved": round(gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
                      "traffic": TRAFFIC["gemv_w4a16_kernel"], "bytes_per_launch": byts},
@@ -806,6 +808,7 @@ def main():
     ap.add_argument("--copies", type=int, default=0, help="gemv/attn: rotating weight / KV copies")
     ap.add_argument("--gemm-shapes", default="", help='gemm: "M1,M2:KxN,KxN" instead of the config 3 sweep')
     ap.add_argument("--gemm-impl", type=int, default=0, help="gemm: 0 auto, 1 GEMV, 2 tcgen05")
+    ap.add_argument("--no-pdl", action="store_true", help="gemv: launch without programmatic dependent launch")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

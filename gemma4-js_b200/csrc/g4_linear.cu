@@ -175,7 +175,6 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         fence_mbar_init();
     }
     __syncthreads();
-    pdl_trigger();
     if (threadIdx.x != 0) pdl_wait();  // thread 0 waits after it has started the weight copies
 
     float acc[kNB][4];
@@ -241,6 +240,9 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         __syncthreads();  // the buffers are refilled by the next pass
     }
 
+    // Dependents are released only now: launched at entry, the next kernel's CTAs would take
+    // SM slots that this grid's later CTAs still need (measured: 6.4 vs 3.8 us per GEMV).
+    pdl_trigger();
     // ---- reduce the warps of the CTA ----
 #pragma unroll
     for (int j = 0; j < kNB; ++j)
