@@ -162,10 +162,12 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     const int KT = max(0, min(p.Kc, k0 + per) - k0);   // weight blocks per tile
     const int NST = (KT + kSub - 1) / kSub;            // pipeline stages per tile
     const uint32_t xsub = (uint32_t)p.TT * TK * 2;     // bytes of one X box
-    // bf16 output of an unsplit tile leaves through a TMA store staged in the X stage that
-    // the tile's last MMAs read: that stage is handed back to the producer by the epilogue
-    // (after the store has read it) instead of by the MMA commit.
-    const bool staged = S == 1 && !p.y_f32;
+    // The output of an unsplit tile leaves through TMA stores staged in the X stages that
+    // the tile's last MMAs read (bf16: one stage holds [T][128]; f32: one stage per 128
+    // tokens); those stages are handed back to the producer by the epilogue (after the
+    // stores have read them) instead of by the MMA commit.
+    const int out_stages = (p.y_f32 && p.TT > 128) ? 2 : 1;
+    const bool staged = S == 1 && NST >= out_stages;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -257,7 +259,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                                 tc_mma_ts(tmem + kAccCol, aa + u * 32 + ks * 8, sw128_desc(xa + u * kXSub + ks * 32),
                                           idesc, (j > 0 || u > 0 || ks > 0) ? 1u : 0u);
                     tc_commit(&a_empty[sa]);                                  // weight stage consumed
-                    if (!(staged && j == NST - 1)) tc_commit(&load_empty[s]);  // X stage consumed
+                    if (!(staged && j >= NST - out_stages)) tc_commit(&load_empty[s]);  // X stage consumed
                 }
                 tc_commit(acc_full);  // tile complete (or abandoned after a timeout)
             }
@@ -336,10 +338,11 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             if (!mbar_wait_warp(acc_full, tj & 1, p.err, 0x109)) break;
             tc_fence_after();
             if (staged) {
-                // Drain the accumulator into the X stage as bf16 [T][128] (row = token), release
-                // it after the last TMEM load, then one thread stores the tile with TMA.
-                const int slast = ((tj + 1) * NST - 1) % kStages;
-                uint16_t* stg = reinterpret_cast<uint16_t*>(smem + Smem::kOffX + slast * kXBytes);
+                // Drain the accumulator into the X stage(s) as [token][128 weight rows] (bf16:
+                // all T tokens in the last stage; f32: tokens 128e.. in stage g_last - e),
+                // release it after the last TMEM load, then one thread stores with TMA.
+                const int glast = (tj + 1) * NST - 1;
+                uint8_t* stg = smem + Smem::kOffX + ((glast - (p.y_f32 ? e : 0)) % kStages) * kXBytes;
                 for (int c = cbeg; c < cend || (c == cbeg && cbeg >= cend); c += 32) {
                     uint32_t v[32];
                     const bool have = c < cend;
@@ -353,22 +356,31 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                         if (lane == 0) mbar_arrive(acc_empty);
                     }
                     if (!have) break;
-                    uint16_t* col = stg + (size_t)c * TW + rt;  // token c, weight row rt
+                    if (p.y_f32) {
+                        float* col = reinterpret_cast<float*>(stg) + (size_t)(c - cbeg) * TW + rt;
 #pragma unroll
-                    for (int jj = 0; jj < 32; jj += 2) {
-                        __nv_bfloat162 b2 = __floats2bfloat162_rn(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]));
-                        const uint32_t bits = *reinterpret_cast<uint32_t*>(&b2);
-                        col[jj * TW] = (uint16_t)(bits & 0xFFFFu);
-                        col[(jj + 1) * TW] = (uint16_t)(bits >> 16);
+                        for (int jj = 0; jj < 32; ++jj) col[jj * TW] = __uint_as_float(v[jj]);
+                    } else {
+                        uint16_t* col = reinterpret_cast<uint16_t*>(stg) + (size_t)c * TW + rt;  // token c, row rt
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj += 2) {
+                            __nv_bfloat162 b2 =
+                                __floats2bfloat162_rn(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]));
+                            const uint32_t bits = *reinterpret_cast<uint32_t*>(&b2);
+                            col[jj * TW] = (uint16_t)(bits & 0xFFFFu);
+                            col[(jj + 1) * TW] = (uint16_t)(bits >> 16);
+                        }
                     }
                 }
                 fence_proxy_async_smem();  // the generic stores, before the async-proxy read
                 asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
                 if (warp == 2 + kDq && lane == 0) {
-                    tma_store_2d(&ymap, stg, ws * TW, ms * p.TT);
+                    for (int h = 0; h < out_stages; ++h)
+                        tma_store_2d(&ymap, smem + Smem::kOffX + ((glast - h) % kStages) * kXBytes, ws * TW,
+                                     ms * p.TT + 128 * h);
                     bulk_commit_group();
                     bulk_wait_read_all();
-                    mbar_arrive(&load_empty[slast]);  // the producer may refill the stage
+                    for (int h = 0; h < out_stages; ++h) mbar_arrive(&load_empty[(glast - h) % kStages]);
                 }
                 continue;
             }
@@ -447,14 +459,15 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
                                         (uint64_t)L.K * 2, TK, p.TT, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    CUtensorMap ymap = xmap;  // unused for f32 output
-    if (!y_f32) {
-        if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
-            return set_error(G4_ERR_INVALID, "tcgen05 GEMM: y must be 16-byte aligned");
-        st = encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW, p.TT,
-                                  CU_TENSOR_MAP_SWIZZLE_NONE);
-        if (st) return st;
-    }
+    // Y tiles leave through TMA stores: bf16 boxes of [T][128], f32 boxes of [min(T, 128)][128].
+    if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
+        return set_error(G4_ERR_INVALID, "tcgen05 GEMM: y must be 16-byte aligned");
+    CUtensorMap ymap;
+    st = y_f32 ? encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, L.N, M, (uint64_t)L.N * 4, TW,
+                                      std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE)
+               : encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW, p.TT,
+                                      CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st) return st;
     const long long ntiles = (long long)p.NS * p.MT;
     if (ntiles > 0x7fffffffLL) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: M=%d N=%d too large", M, L.N);
     int S = 1;

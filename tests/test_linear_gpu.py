@@ -58,7 +58,7 @@ def _run(rt, ctx, ops, oracle, K, N, M, impl, seed, out_dtype=torch.bfloat16):
 
 
 @pytest.mark.parametrize("M", [1, 2, 3, 7, 8, 9, 16])
-@pytest.mark.parametrize("K,N", [(1536, 6144), (6144, 1536), (96, 40), (256, 1536), (1536, 8960)])
+@pytest.mark.parametrize("K,N", [(1536, 6144), (6144, 1536), (96, 40), (256, 1536), (1536, 8960), (96, 4744)])
 def test_gemv_matches_oracle(rt, ctx, ops, oracle, K, N, M):
     y, ref = _run(rt, ctx, ops, oracle, K, N, M, impl=1, seed=K * 7 + N + M)
     assert max_rel(y, ref) < TOL
@@ -115,7 +115,8 @@ def test_tcgen05_gemm_tiling_edges(rt, ctx, ops, oracle, M, K, N):
     assert max_rel(y, ref) < TOL
 
 
-@pytest.mark.parametrize("M,K,N", [(256, 1536, 6144), (130, 6144, 1536), (64, 96, 40)])
+@pytest.mark.parametrize("M,K,N", [(256, 1536, 6144), (130, 6144, 1536), (64, 96, 40), (200, 1536, 2560),
+                                   (256, 128, 1536), (600, 256, 8960)])
 def test_tcgen05_gemm_vs_torch_fp32_on_bf16_weights(rt, ctx, ops, oracle, M, K, N):
     """The GEMM multiplies bf16 activations by the bf16 materialisation of the weights
     (RNE of q*s) with FP32 accumulation: a torch fp32 matmul of the same operands must
