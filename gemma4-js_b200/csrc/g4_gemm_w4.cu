@@ -29,15 +29,16 @@
 //                materialisation, roundFloat32ToBF16 of q*s, official-w4a16.js:34-48,
 //                :95), then tcgen05.st into a 2-stage TMEM ring.
 //   warps 10..17 epilogue: warp w drains lane quarter w % 4, tokens 128 * ((w - 10) / 4)
-//                + 0..127: tcgen05.ld (double-buffered), release the accumulator after the
-//                last load, then neighbouring lanes swap values so that every store
-//                writes two adjacent columns of Y.
-#include <cooperative_groups.h>
-
+//                + 0..127, with tcgen05.ld into registers, into the X stage(s) the tile's
+//                last MMAs consumed ([token][128 rows], bf16 or f32), releases the
+//                accumulator after its last load, and one thread stores the tile with TMA.
+// When the tiles do not fill the GPU, K is split over S CTAs per tile; each stores its
+// FP32 partial tile (through the same staged TMA store) into plane `slice` of an
+// L2-resident workspace [S][Mp][N], and splitk_sum_kernel adds the planes in slice order
+// (deterministic).  Every wait is bounded; a timeout raises the context's device error
+// word and the kernel winds down (TMEM is always freed).
 #include "g4_linear.cuh"
 #include "g4_tcgen05.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace {
 
@@ -57,7 +58,6 @@ constexpr int kXBytes = kSub * kXSub;         // 64 KB per stage
 constexpr int kBlkBytes = g4::kTblkBytes;     // 4096 B of nibbles + 512 B of scales
 constexpr int kTmemCols = 512;
 constexpr int kAccCol = 0, kACol = 256;
-constexpr int kPartPitch = TW + 4;            // floats per token row of a parked partial
 
 struct Smem {
     static constexpr int kOffX = 0;
@@ -65,7 +65,7 @@ struct Smem {
     static constexpr int kOffBar = kOffBlk + kStages * kSub * kBlkBytes;
     static constexpr int kBytes = kOffBar + 256 + 1024;  // + alignment slack
 };
-static_assert(TTmax * kPartPitch * 4 <= Smem::kOffBlk, "a parked partial must fit in the X ring");
+static_assert(TTmax * TW * 2 <= kXBytes && 128 * TW * 4 <= kXBytes, "an output stage must fit in an X stage");
 static_assert(Smem::kBytes <= 232448, "shared memory plan exceeds 227 KB");
 
 struct W4Params {
@@ -74,66 +74,11 @@ struct W4Params {
     int M, N, ldy, y_f32;
     int Kc;          // 64-column weight blocks along K
     int NS, MT, TT;  // weight slabs of 128 rows, token tiles, tokens per tile (multiple of 32)
-    int ksplit;      // CTAs of a cluster sharing one tile, each over 1/ksplit of K
+    int ksplit;      // CTAs sharing one tile, each over a slice of K (1: no split)
+    int kper;        // weight blocks per K slice
+    float* part;     // ksplit > 1: partial planes [ksplit][Mp][N] f32, Mp = MT * (TT > 128 ? 256 : TT)
     uint32_t* err;
 };
-
-// Split-K: this rank sums tokens kslice, kslice + S, ... of the tile over the S parked
-// partials ([TT][kPartPitch] f32 in each rank's shared memory) in rank order and stores
-// them; 32 threads per token row, 4 weight rows each.  Each thread takes two items at a
-// time and issues all 2 x S distributed-shared-memory loads before summing (the loads are
-// latency-bound, not bandwidth-bound).
-__device__ __forceinline__ void store4(const W4Params& p, int m, int n, float4 acc) {
-    if (p.y_f32) {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + (size_t)m * p.ldy + n) = acc;
-    } else {
-        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * p.ldy + n) =
-            make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
-    }
-}
-__device__ __forceinline__ void split_reduce(uint8_t* smem, cg::cluster_group& cluster, int S, int kslice, int ws,
-                                             int ms, const W4Params& p) {
-    const float* peer[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r)
-        peer[r] = cluster.map_shared_rank(reinterpret_cast<float*>(smem), r < S ? r : 0);
-    const int ntok = (p.TT - kslice + S - 1) / S;
-    const int items = ntok * 32;
-    constexpr int kT = 512;  // threads taking part (16 warps)
-    if (threadIdx.x >= kT) return;
-    for (int i0 = threadIdx.x; i0 < items; i0 += 2 * kT) {
-        float4 v[2][8];
-        int m[2], n[2];
-        bool live[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int idx = i0 + u * kT;
-            const int tl = kslice + (idx >> 5) * S;
-            const int c4 = (idx & 31) * 4;
-            m[u] = ms * p.TT + tl;
-            n[u] = ws * TW + c4;
-            live[u] = idx < items && m[u] < p.M && n[u] < p.N;  // N % 8 == 0: 4 rows all in or all out
-#pragma unroll
-            for (int r = 0; r < 8; ++r)
-                if (live[u] && r < S) v[u][r] = *reinterpret_cast<const float4*>(peer[r] + tl * kPartPitch + c4);
-        }
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            if (!live[u]) continue;
-            float4 acc = v[u][0];
-#pragma unroll
-            for (int r = 1; r < 8; ++r)
-                if (r < S) {
-                    acc.x += v[u][r].x;
-                    acc.y += v[u][r].y;
-                    acc.z += v[u][r].z;
-                    acc.w += v[u][r].w;
-                }
-            store4(p, m[u], n[u], acc);
-        }
-    }
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
@@ -153,21 +98,23 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.ksplit;
     const int ntiles = p.NS * p.MT;
-    // S == 1: persistent, tiles blockIdx.x, + gridDim.x, ...; S > 1: cluster c owns tile c.
+    // S == 1: persistent, tiles blockIdx.x, + gridDim.x, ...; S > 1: CTAs t*S .. t*S+S-1 own
+    // tile t, each one K slice.
     const int tile0 = S > 1 ? (int)blockIdx.x / S : (int)blockIdx.x;
     const int tstep = S > 1 ? ntiles : (int)gridDim.x;
     const int kslice = S > 1 ? (int)blockIdx.x % S : 0;
-    const int per = (p.Kc + S - 1) / S;
-    const int k0 = kslice * per;                       // first weight block of this CTA's K range
-    const int KT = max(0, min(p.Kc, k0 + per) - k0);   // weight blocks per tile
+    const int k0 = kslice * p.kper;                       // first weight block of this CTA's K range
+    const int KT = max(0, min(p.Kc, k0 + p.kper) - k0);   // weight blocks per tile (the host leaves no slice empty)
     const int NST = (KT + kSub - 1) / kSub;            // pipeline stages per tile
     const uint32_t xsub = (uint32_t)p.TT * TK * 2;     // bytes of one X box
     // The output of an unsplit tile leaves through TMA stores staged in the X stages that
     // the tile's last MMAs read (bf16: one stage holds [T][128]; f32: one stage per 128
     // tokens); those stages are handed back to the producer by the epilogue (after the
     // stores have read them) instead of by the MMA commit.
-    const int out_stages = (p.y_f32 && p.TT > 128) ? 2 : 1;
-    const bool staged = S == 1 && NST >= out_stages;
+    const bool out_f32 = p.y_f32 || S > 1;  // partial planes are f32
+    const int out_stages = (out_f32 && p.TT > 128) ? 2 : 1;
+    const bool staged = NST >= out_stages;
+    const int plane_row0 = kslice * p.MT * (p.TT > 128 ? 256 : p.TT);  // first row of this CTA's output plane
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -318,23 +265,6 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         int tj = 0;
         for (int t = tile0; t < ntiles; t += tstep, ++tj) {
             const int ws = t / p.MT, ms = t % p.MT;
-            if (S > 1) {
-                // park the FP32 partial as [token][weight row] in the (idle) X ring
-                float* part = reinterpret_cast<float*>(smem);
-                if (KT == 0) {  // an empty K slice contributes zeros
-                    for (int c = cbeg; c < cend; ++c) part[c * kPartPitch + rt] = 0.f;
-                } else if (mbar_wait_warp(acc_full, 0, p.err, 0x108)) {
-                    tc_fence_after();
-                    for (int c = cbeg; c < cend; c += 32) {
-                        uint32_t v[32];
-                        tmem_ld_32x32b_x32(tq + c, v);
-                        tmem_ld_wait(v);
-#pragma unroll
-                        for (int jj = 0; jj < 32; ++jj) part[(c + jj) * kPartPitch + rt] = __uint_as_float(v[jj]);
-                    }
-                }
-                break;  // one tile per CTA
-            }
             if (!mbar_wait_warp(acc_full, tj & 1, p.err, 0x109)) break;
             tc_fence_after();
             if (staged) {
@@ -342,7 +272,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 // all T tokens in the last stage; f32: tokens 128e.. in stage g_last - e),
                 // release it after the last TMEM load, then one thread stores with TMA.
                 const int glast = (tj + 1) * NST - 1;
-                uint8_t* stg = smem + Smem::kOffX + ((glast - (p.y_f32 ? e : 0)) % kStages) * kXBytes;
+                uint8_t* stg = smem + Smem::kOffX + ((glast - (out_f32 ? e : 0)) % kStages) * kXBytes;
                 for (int c = cbeg; c < cend || (c == cbeg && cbeg >= cend); c += 32) {
                     uint32_t v[32];
                     const bool have = c < cend;
@@ -356,7 +286,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                         if (lane == 0) mbar_arrive(acc_empty);
                     }
                     if (!have) break;
-                    if (p.y_f32) {
+                    if (out_f32) {
                         float* col = reinterpret_cast<float*>(stg) + (size_t)(c - cbeg) * TW + rt;
 #pragma unroll
                         for (int jj = 0; jj < 32; ++jj) col[jj * TW] = __uint_as_float(v[jj]);
@@ -377,15 +307,17 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (warp == 2 + kDq && lane == 0) {
                     for (int h = 0; h < out_stages; ++h)
                         tma_store_2d(&ymap, smem + Smem::kOffX + ((glast - h) % kStages) * kXBytes, ws * TW,
-                                     ms * p.TT + 128 * h);
+                                     plane_row0 + ms * p.TT + 128 * h);
                     bulk_commit_group();
                     bulk_wait_read_all();
                     for (int h = 0; h < out_stages; ++h) mbar_arrive(&load_empty[(glast - h) % kStages]);
                 }
                 continue;
             }
-            // FP32 output: one chunk at a time, each lane stores its weight row's 32 tokens.
+            // Fallback (f32 output, or a partial, with fewer stages than output stages): one
+            // chunk at a time, each lane stores its weight row's 32 tokens.
             const int n = ws * TW + rt;
+            float* ybase = S > 1 ? p.part + (size_t)plane_row0 * p.ldy : reinterpret_cast<float*>(p.y);
             for (int c = cbeg; c < cend || (c == cbeg && cbeg >= cend); c += 32) {
                 uint32_t v[32];
                 const bool have = c < cend;
@@ -401,7 +333,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 if (!have) break;
                 const int m0 = ms * p.TT + c;
                 if (n < p.N) {
-                    float* yp = reinterpret_cast<float*>(p.y) + (size_t)m0 * p.ldy + n;
+                    float* yp = ybase + (size_t)m0 * p.ldy + n;
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj)
                         if (m0 + jj < p.M) yp[(size_t)jj * p.ldy] = __uint_as_float(v[jj]);
@@ -412,17 +344,42 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
         __syncwarp();
     }
 
-    if (S > 1) {
-        cg::cluster_group cluster = cg::this_cluster();
-        cluster.sync();
-        split_reduce(smem, cluster, S, kslice, tile0 / p.MT, tile0 % p.MT, p);
-        cluster.sync();  // peers may still be reading this CTA's partial
-    }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// Split-K epilogue: y[m, n] = sum over slices s (in order) of part[s][m][n], f32 or bf16
+// out; one thread per 4 columns.  Reads the planes from L2 (they were just written).
+__global__ void __launch_bounds__(256) splitk_sum_kernel(const float4* __restrict__ part, int S,
+                                                         long long plane4, int M, int N4, void* __restrict__ y,
+                                                         int y_f32) {
+    pdl_trigger();
+    pdl_wait();  // the partial planes come from the GEMM
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)M * N4) return;
+    float4 acc = __ldcg(part + i);
+    int s = 1;
+    for (; s + 4 <= S; s += 4) {  // four planes in flight, summed in slice order
+        const float4 a = __ldcg(part + s * plane4 + i), b = __ldcg(part + (s + 1) * plane4 + i);
+        const float4 c = __ldcg(part + (s + 2) * plane4 + i), d = __ldcg(part + (s + 3) * plane4 + i);
+        acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+        acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
+        acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
+        acc.x += d.x; acc.y += d.y; acc.z += d.z; acc.w += d.w;
+    }
+    for (; s < S; ++s) {
+        const float4 a = __ldcg(part + s * plane4 + i);
+        acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
+    }
+    if (y_f32) {
+        reinterpret_cast<float4*>(y)[i] = acc;
+    } else {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+        reinterpret_cast<uint2*>(y)[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
     }
 }
 
@@ -432,8 +389,9 @@ namespace g4 {
 
 // Tiles: 128 weight rows x T tokens (T = M rounded up to 32, at most 256).  With at least
 // one tile per SM the grid is persistent (one CTA per SM walking the tiles, token tile
-// fastest so concurrent CTAs share the weight slabs in L2); otherwise K is split over a
-// cluster of up to 8 CTAs (>= 4 steps each).
+// fastest so concurrent CTAs share the weight slabs in L2); otherwise K is split over S
+// CTAs per tile (at most one CTA per SM in total, >= 3 weight blocks per slice) whose
+// partial planes splitk_sum_kernel adds.
 g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32) {
     const g4_linear_dev& L = lin->dev;
     if (!gemm_supported(lin, M)) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: shape K=%d N=%d", L.K, L.N);
@@ -443,6 +401,8 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
                                            Smem::kBytes));
         attr_set.fetch_or(1ull << ctx->device);
     }
+    if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
+        return set_error(G4_ERR_INVALID, "tcgen05 GEMM: y must be 16-byte aligned");
     W4Params p{};
     p.tblk = L.tblk;
     p.y = y;
@@ -455,27 +415,43 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     p.TT = M >= TTmax ? TTmax : (M + 31) / 32 * 32;
     p.MT = (M + p.TT - 1) / p.TT;
     p.err = ctx->d_err;
-    CUtensorMap xmap;
-    g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
-                                        (uint64_t)L.K * 2, TK, p.TT, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    // Y tiles leave through TMA stores: bf16 boxes of [T][128], f32 boxes of [min(T, 128)][128].
-    if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
-        return set_error(G4_ERR_INVALID, "tcgen05 GEMM: y must be 16-byte aligned");
-    CUtensorMap ymap;
-    st = y_f32 ? encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, L.N, M, (uint64_t)L.N * 4, TW,
-                                      std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE)
-               : encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW, p.TT,
-                                      CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (st) return st;
     const long long ntiles = (long long)p.NS * p.MT;
     if (ntiles > 0x7fffffffLL) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: M=%d N=%d too large", M, L.N);
     int S = 1;
-    while (S < 8 && ntiles * (S + 1) <= ctx->num_sms && p.Kc / (S + 1) >= 4) ++S;
+    while (ntiles * (S + 1) <= ctx->num_sms && p.Kc / (S + 1) >= 3) ++S;
+    p.kper = (p.Kc + S - 1) / S;
+    S = (p.Kc + p.kper - 1) / p.kper;  // no empty slice
     p.ksplit = S;
+    CUtensorMap xmap, ymap;
+    g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
+                                        (uint64_t)L.K * 2, TK, p.TT, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    // Rows of one partial plane: whole token tiles, and whole 128-row store boxes (a box that
+    // ran past the plane would write into the next slice's plane).
+    const long long Mp = (long long)p.MT * (p.TT > 128 ? 256 : p.TT);
+    if (S > 1) {
+        // partial planes [S][Mp][N] f32 in the context workspace; f32 boxes of [min(T, 128)][128]
+        const size_t bytes = (size_t)S * Mp * L.N * 4;
+        st = ensure_workspace(ctx, bytes);
+        if (st) return st;
+        p.part = static_cast<float*>(ctx->ws);
+        st = encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.part, L.N, (uint64_t)(S * Mp),
+                                  (uint64_t)L.N * 4, TW, std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+        // Y tiles leave through TMA stores: bf16 boxes of [T][128], f32 boxes of [min(T, 128)][128]
+        st = y_f32 ? encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, L.N, M, (uint64_t)L.N * 4, TW,
+                                          std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE)
+                   : encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW,
+                                          p.TT, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    if (st) return st;
     const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
-    return launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel, dim3(grid), dim3(kThreads), Smem::kBytes, S, xmap,
-                  ymap, p);
+    st = launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel, dim3(grid), dim3(kThreads), Smem::kBytes, 1, xmap,
+                ymap, p);
+    if (st || S == 1) return st;
+    const long long n4 = (long long)M * (L.N / 4);
+    return launch(ctx, "splitk_sum_kernel", splitk_sum_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, 1,
+                  reinterpret_cast<const float4*>(p.part), S, Mp * (L.N / 4), M, L.N / 4, y, y_f32);
 }
 
 }  // namespace g4
