@@ -175,7 +175,15 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         fence_mbar_init();
     }
     __syncthreads();
-    if (threadIdx.x != 0) pdl_wait();  // thread 0 waits after it has started the weight copies
+    // Dependents are released once this grid's predecessor has completed (every thread has
+    // passed its wait): the next kernel's CTAs then prefetch their weights while this one
+    // computes, and at most two kernels' CTAs share the SMs.  Released at entry, a chain of
+    // dependents ran ahead and took the slots this grid still needed (6.4 vs 3.5 us per
+    // GEMV); released after the main loop, the next kernel's weight fetch did not overlap.
+    if (threadIdx.x != 0) {
+        pdl_wait();
+        pdl_trigger();
+    }
 
     float acc[kNB][4];
 #pragma unroll
@@ -193,7 +201,10 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
             const size_t blk = (size_t)nt * L.Kc + p0;
             bulk_load(wsm, L.wfrag + blk * 32, nch * 512, bar);
             bulk_load(ssm, L.sfrag + blk * 8, nch * 64, bar);
-            if (p0 == c_begin) pdl_wait();  // weights are immutable; activations come from the predecessor
+            if (p0 == c_begin) {  // weights are immutable; activations come from the predecessor
+                pdl_wait();
+                pdl_trigger();
+            }
             for (int b = 0; b < M; ++b)
                 bulk_load(xsm + b * xstride, x + (size_t)b * ldx + k0, klen * 2, bar);
         }
@@ -239,10 +250,11 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         }
         __syncthreads();  // the buffers are refilled by the next pass
     }
+    if (threadIdx.x == 0 && c_begin >= c_end) {  // an empty K slice: thread 0 never reached its wait
+        pdl_wait();
+        pdl_trigger();
+    }
 
-    // Dependents are released only now: launched at entry, the next kernel's CTAs would take
-    // SM slots that this grid's later CTAs still need (measured: 6.4 vs 3.8 us per GEMV).
-    pdl_trigger();
     // ---- reduce the warps of the CTA ----
 #pragma unroll
     for (int j = 0; j < kNB; ++j)
