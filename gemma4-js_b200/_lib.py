@@ -23,6 +23,11 @@ class G4Rows(C.Structure):
     """g4_rows: where the rows of a batch sit in their sequences (include/g4w4.h)."""
     _fields_ = [("seq_pos", C.c_void_p), ("seq_base", C.c_int), ("rows_per_seq", C.c_int), ("pos0", C.c_int)]
 
+
+class G4Planes(C.Structure):
+    """g4_planes: a linear's f32 output as partial planes summed in slice order (include/g4w4.h)."""
+    _fields_ = [("base", C.c_void_p), ("count", C.c_int), ("stride", C.c_longlong), ("ld", C.c_int)]
+
 STATUS_NAMES = {
     0: "G4_OK", -1: "G4_ERR_INVALID", -2: "G4_ERR_OOM", -3: "G4_ERR_CUDA", -4: "G4_ERR_TIMEOUT",
     -5: "G4_ERR_UNSUPPORTED", -6: "G4_ERR_RANGE", -7: "G4_ERR_DEVICE",
@@ -81,6 +86,11 @@ SIGNATURES = {
     "g4_qkv_post": (_S, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P, _P, _I]),
     "g4_gelu_mul": (_S, [_P, _P, _I, _I, _P]),
     "g4_gelu_ple": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "g4_linear_w4a16_planes": (_S, [_P, _P, _P, _I, _P]),
+    "g4_post_norm_add_planes": (_S, [_P, _P, _P, _P, _F, _P, _I, _I, _F, _P]),
+    "g4_qkv_post_planes": (_S, [_P, _P, _I, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P, _P, _I]),
+    "g4_gelu_mul_planes": (_S, [_P, _P, _I, _I, _P]),
+    "g4_gelu_ple_planes": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "g4_ple_mix": (_S, [_P, _P, _F, _P, _P, _I, _I, _I, _F, _P]),
     "g4_softcap_argmax": (_S, [_P, _P, _I, _I, _F, _P, _P]),
     "g4_advance_positions": (_S, [_P, _P, _I, _I, _I]),

@@ -392,7 +392,10 @@ namespace g4 {
 // fastest so concurrent CTAs share the weight slabs in L2); otherwise K is split over S
 // CTAs per tile (at most one CTA per SM in total, >= 3 weight blocks per slice) whose
 // partial planes splitk_sum_kernel adds.
-g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32) {
+// planes != nullptr: leave the f32 output as partial planes in the context workspace (no
+// summing pass; y is ignored) and describe them in *planes.
+static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32,
+                           g4_planes* planes) {
     const g4_linear_dev& L = lin->dev;
     if (!gemm_supported(lin, M)) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: shape K=%d N=%d", L.K, L.N);
     static std::atomic<uint64_t> attr_set{0};
@@ -401,7 +404,7 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
                                            Smem::kBytes));
         attr_set.fetch_or(1ull << ctx->device);
     }
-    if (reinterpret_cast<uintptr_t>(y) % 16 != 0)
+    if (!planes && reinterpret_cast<uintptr_t>(y) % 16 != 0)
         return set_error(G4_ERR_INVALID, "tcgen05 GEMM: y must be 16-byte aligned");
     W4Params p{};
     p.tblk = L.tblk;
@@ -429,12 +432,21 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     // Rows of one partial plane: whole token tiles, and whole 128-row store boxes (a box that
     // ran past the plane would write into the next slice's plane).
     const long long Mp = (long long)p.MT * (p.TT > 128 ? 256 : p.TT);
+    if (planes && S == 1) {  // the whole f32 output is the one plane, in the workspace
+        st = ensure_workspace(ctx, (size_t)M * L.N * 4);
+        if (st) return st;
+        y = ctx->ws;
+        p.y = y;
+        y_f32 = p.y_f32 = 1;
+        *planes = g4_planes{static_cast<const float*>(ctx->ws), 1, 0, L.N};
+    }
     if (S > 1) {
         // partial planes [S][Mp][N] f32 in the context workspace; f32 boxes of [min(T, 128)][128]
         const size_t bytes = (size_t)S * Mp * L.N * 4;
         st = ensure_workspace(ctx, bytes);
         if (st) return st;
         p.part = static_cast<float*>(ctx->ws);
+        if (planes) *planes = g4_planes{p.part, S, Mp * L.N, L.N};
         st = encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.part, L.N, (uint64_t)(S * Mp),
                                   (uint64_t)L.N * 4, TW, std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
@@ -448,10 +460,18 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
     st = launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel, dim3(grid), dim3(kThreads), Smem::kBytes, 1, xmap,
                 ymap, p);
-    if (st || S == 1) return st;
+    if (st || S == 1 || planes) return st;
     const long long n4 = (long long)M * (L.N / 4);
     return launch(ctx, "splitk_sum_kernel", splitk_sum_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, 1,
                   reinterpret_cast<const float4*>(p.part), S, Mp * (L.N / 4), M, L.N / 4, y, y_f32);
+}
+
+g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32) {
+    return gemm_core(ctx, lin, x, M, y, y_f32, nullptr);
+}
+
+g4_status launch_gemm_planes(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, g4_planes* planes) {
+    return gemm_core(ctx, lin, x, M, nullptr, 1, planes);
 }
 
 }  // namespace g4

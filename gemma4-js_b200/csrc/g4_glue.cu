@@ -41,6 +41,30 @@ __device__ __forceinline__ int row_position(const G4Rows& R, int r) {
 }
 __device__ __forceinline__ int row_seq(const G4Rows& R, int r) { return R.seq_base + r / R.rows_per_seq; }
 
+// A linear's output as partial planes (g4_planes): the slices are added in order, the
+// same bits the linear's own last pass (splitk_sum_kernel) produces.
+struct Planes {
+    const float* base;
+    long long stride;
+    int count, ld;
+};
+__device__ __forceinline__ float ld_planes(const Planes& P, size_t off) {
+    float a = P.base[off];
+    for (int s = 1; s < P.count; ++s) a += P.base[(size_t)s * P.stride + off];
+    return a;
+}
+__device__ __forceinline__ float4 ld4_planes(const Planes& P, size_t off) {
+    float4 a = *reinterpret_cast<const float4*>(P.base + off);
+    for (int s = 1; s < P.count; ++s) {
+        const float4 b = *reinterpret_cast<const float4*>(P.base + (size_t)s * P.stride + off);
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+    }
+    return a;
+}
+
 // gelu_tanh with the reference's clamp of the tanh argument to [-10, 10] (:1154).
 __device__ __forceinline__ float gelu_ref(float x) {
     const float c = 0.7978845608028654f;
@@ -82,8 +106,8 @@ __global__ void add_scale_kernel(const float* __restrict__ a, const float* __res
 //   h = (h + rms(y) * w_post) * skip;  x = bf16(w_next ? rms(h) * w_next : h)
 // One CTA per row, one float4 of the row per thread, kept in registers across the
 // two reductions (width % 4 == 0, width <= 4096).
-__global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__ h, const float* __restrict__ y,
-                                                             int ldy, const float* __restrict__ w_post, float skip,
+__global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__ h, Planes y,
+                                                             const float* __restrict__ w_post, float skip,
                                                              const float* __restrict__ w_next, int width, float eps,
                                                              uint16_t* __restrict__ x_out) {
     pdl_trigger();
@@ -93,7 +117,7 @@ __global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__
     const bool on = i < width;
     float4 yv = make_float4(0.f, 0.f, 0.f, 0.f), hv = yv, wp = yv;
     if (on) {
-        yv = *reinterpret_cast<const float4*>(y + (size_t)r * ldy + i);
+        yv = ld4_planes(y, (size_t)r * y.ld + i);
         hv = *reinterpret_cast<const float4*>(h + (size_t)r * width + i);
         wp = *reinterpret_cast<const float4*>(w_post + i);
     }
@@ -142,7 +166,7 @@ __global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __re
 // bf16 caches at the row's absolute position (KVCache.append, gemma4-webgpu.js:128-135).
 // One CTA per (row, head slot); slot < H: q head, H: k, H + 1: v.  Thread i owns
 // elements i and i + hd/2 (a rotation pair).
-__global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int hd, int has_kv,
+__global__ void qkv_post_kernel(Planes y, int H, int hd, int has_kv,
                                 const float* __restrict__ qnorm, const float* __restrict__ knorm, float eps,
                                 int rope_angles, float rope_base, G4Rows R, uint16_t* __restrict__ q_out,
                                 uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cache_cap) {
@@ -152,8 +176,8 @@ __global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int
     const int slot = blockIdx.x, r = blockIdx.y;
     const int half = hd >> 1;
     const int i = threadIdx.x;  // 0 .. half-1
-    const float* src = y + (size_t)r * ldy + (size_t)slot * hd;
-    const float a0 = src[i], a1 = src[i + half];
+    const size_t src = (size_t)r * y.ld + (size_t)slot * hd;
+    const float a0 = ld_planes(y, src + i), a1 = ld_planes(y, src + i + half);
     const float inv = rsqrtf(block_sum(a0 * a0 + a1 * a1, red) / (float)hd + eps);
     const int pos = row_position(R, r);
     if (slot == H + 1) {  // v: RMS without scale (official-w4a16-layer0.js:176-182)
@@ -179,30 +203,31 @@ __global__ void qkv_post_kernel(const float* __restrict__ y, int ldy, int H, int
 
 // GELU_MUL over a fused [gate | up] projection: out = bf16(gelu(gate) * up), four
 // columns per thread (inter % 4 == 0).
-__global__ void gelu_mul_kernel(const float* __restrict__ gu, int inter, long long n4, uint16_t* __restrict__ out) {
+__global__ void gelu_mul_kernel(Planes gu, int inter, long long n4, uint16_t* __restrict__ out) {
     pdl_trigger();
     pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n4) return;
     const int q = inter >> 2;
     const long long r = i / q, c = (i - r * q) * 4;
-    const float* row = gu + r * 2 * inter;
-    const float4 g = *reinterpret_cast<const float4*>(row + c);
-    const float4 u = *reinterpret_cast<const float4*>(row + inter + c);
+    const size_t row = (size_t)r * gu.ld;
+    const float4 g = ld4_planes(gu, row + c);
+    const float4 u = ld4_planes(gu, row + inter + c);
     *reinterpret_cast<uint2*>(out + r * inter + c) =
         make_uint2(pack_bf16x2_bits(gelu_ref(g.x) * u.x, gelu_ref(g.y) * u.y),
                    pack_bf16x2_bits(gelu_ref(g.z) * u.z, gelu_ref(g.w) * u.w));
 }
 
 // GELU_PLE: out = bf16(gelu(gate) * per_layer[row, layer, :]).
-__global__ void gelu_ple_kernel(const float* __restrict__ gate, const float* __restrict__ per_layer, int layer,
-                                int layers, int dim, long long n, uint16_t* __restrict__ out) {
+__global__ void gelu_ple_kernel(Planes gate, const float* __restrict__ per_layer, int layer, int layers, int dim,
+                                long long n, uint16_t* __restrict__ out) {
     pdl_trigger();
     pdl_wait();
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const long long r = i / dim, d = i - r * dim;
-    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(gate[i]) * per_layer[(r * layers + layer) * dim + d]);
+    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(ld_planes(gate, (size_t)r * gate.ld + d)) *
+                                        per_layer[(r * layers + layer) * dim + d]);
 }
 
 // SCALE + PLE_MIX: p = proj * proj_scale; y = (rms(p) * norm + tok_ple * sqrt(dim)) / sqrt(2)
@@ -312,17 +337,28 @@ g4_status g4_add_scale(g4_ctx* ctx, const float* a, const float* b, long long n,
     return g4::launch(ctx, "add_scale_kernel", add_scale_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, a, b, n, scale, y);
 }
 
-g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const float* w_post, float skip,
-                           const float* w_next, int rows, int width, float eps, void* x_out_bf16) {
+static Planes planes_of(const g4_planes* y) { return Planes{y->base, y->stride, y->count, y->ld}; }
+static bool planes_ok(const g4_planes* y) { return y && y->base && y->count >= 1 && y->ld > 0; }
+
+g4_status g4_post_norm_add_planes(g4_ctx* ctx, float* h, const g4_planes* y, const float* w_post, float skip,
+                                  const float* w_next, int rows, int width, float eps, void* x_out_bf16) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;
-    if (rows < 0 || width <= 0 || !h || !y || !w_post) return g4::set_error(G4_ERR_INVALID, "g4_post_norm_add: bad arguments");
-    if (width % 4 != 0 || width > 4096 || ldy % 4 != 0)
-        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_post_norm_add: width %d / ldy %d (multiples of 4, width <= 4096)", width, ldy);
+    if (rows < 0 || width <= 0 || !h || !planes_ok(y) || !w_post)
+        return g4::set_error(G4_ERR_INVALID, "g4_post_norm_add: bad arguments");
+    if (width % 4 != 0 || width > 4096 || y->ld % 4 != 0 || (y->count > 1 && y->stride % 4 != 0))
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_post_norm_add: width %d / ldy %d (multiples of 4, width <= 4096)",
+                             width, y->ld);
     if (rows == 0) return G4_OK;
     const int threads = ((width / 4 + 31) / 32) * 32;
-    return g4::launch(ctx, "post_norm_add_kernel", post_norm_add_kernel, dim3(rows), dim3(threads), 0, 1, h, y, ldy,
-                      w_post, skip, w_next, width, eps, static_cast<uint16_t*>(x_out_bf16));
+    return g4::launch(ctx, "post_norm_add_kernel", post_norm_add_kernel, dim3(rows), dim3(threads), 0, 1, h,
+                      planes_of(y), w_post, skip, w_next, width, eps, static_cast<uint16_t*>(x_out_bf16));
+}
+
+g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const float* w_post, float skip,
+                           const float* w_next, int rows, int width, float eps, void* x_out_bf16) {
+    const g4_planes one{y, 1, 0, ldy};
+    return g4_post_norm_add_planes(ctx, h, &one, w_post, skip, w_next, rows, width, eps, x_out_bf16);
 }
 
 g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, const int32_t* ids_dev, int rows,
@@ -336,42 +372,64 @@ g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, co
                       static_cast<uint16_t*>(x_out_bf16), ctx->d_err);
 }
 
-g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,
-                      const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
-                      int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap) {
+g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd, int has_kv, const float* qnorm,
+                             const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
+                             int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;
-    if (rows < 0 || !y || !qnorm || !rows_map || !q_out_bf16 || (has_kv && (!knorm || !kcache_bf16 || !vcache_bf16)))
+    if (rows < 0 || !planes_ok(y) || !qnorm || !rows_map || !q_out_bf16 ||
+        (has_kv && (!knorm || !kcache_bf16 || !vcache_bf16)))
         return g4::set_error(G4_ERR_INVALID, "g4_qkv_post: bad arguments");
     if (hd % 64 != 0 || hd > 1024) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_qkv_post: hd %d", hd);
     if (rows == 0) return G4_OK;
     return g4::launch(ctx, "qkv_post_kernel", qkv_post_kernel, dim3(heads + (has_kv ? 2 : 0), rows), dim3(hd / 2), 0,
-                      1, y, ldy, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map,
+                      1, planes_of(y), heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map,
                       static_cast<uint16_t*>(q_out_bf16), static_cast<uint16_t*>(kcache_bf16),
                       static_cast<uint16_t*>(vcache_bf16), cache_cap);
 }
 
-g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, void* out_bf16) {
+g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,
+                      const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
+                      int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap) {
+    const g4_planes one{y, 1, 0, ldy};
+    return g4_qkv_post_planes(ctx, &one, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, rows_map, rows,
+                              q_out_bf16, kcache_bf16, vcache_bf16, cache_cap);
+}
+
+g4_status g4_gelu_mul_planes(g4_ctx* ctx, const g4_planes* gate_up, int rows, int inter, void* out_bf16) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;
-    if (rows < 0 || inter <= 0 || !gate_up || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_gelu_mul: bad arguments");
-    if (inter % 4 != 0) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_gelu_mul: inter %d (multiple of 4)", inter);
+    if (rows < 0 || inter <= 0 || !planes_ok(gate_up) || !out_bf16)
+        return g4::set_error(G4_ERR_INVALID, "g4_gelu_mul: bad arguments");
+    if (inter % 4 != 0 || gate_up->ld % 4 != 0 || (gate_up->count > 1 && gate_up->stride % 4 != 0))
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_gelu_mul: inter %d (multiple of 4)", inter);
     const long long n4 = (long long)rows * inter / 4;
     if (n4 == 0) return G4_OK;
-    return g4::launch(ctx, "gelu_mul_kernel", gelu_mul_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, 1, gate_up,
-                      inter, n4, static_cast<uint16_t*>(out_bf16));
+    return g4::launch(ctx, "gelu_mul_kernel", gelu_mul_kernel, dim3(blocks_for(n4, 256)), dim3(256), 0, 1,
+                      planes_of(gate_up), inter, n4, static_cast<uint16_t*>(out_bf16));
+}
+
+g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, void* out_bf16) {
+    const g4_planes one{gate_up, 1, 0, 2 * inter};
+    return g4_gelu_mul_planes(ctx, &one, rows, inter, out_bf16);
+}
+
+g4_status g4_gelu_ple_planes(g4_ctx* ctx, const g4_planes* gate, const float* per_layer, int layer, int layers,
+                             int dim, int rows, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || !planes_ok(gate) || !per_layer || !out_bf16 || layer < 0 || layer >= layers)
+        return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple: bad arguments");
+    const long long n = (long long)rows * dim;
+    if (n == 0) return G4_OK;
+    return g4::launch(ctx, "gelu_ple_kernel", gelu_ple_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1,
+                      planes_of(gate), per_layer, layer, layers, dim, n, static_cast<uint16_t*>(out_bf16));
 }
 
 g4_status g4_gelu_ple(g4_ctx* ctx, const float* gate, const float* per_layer, int layer, int layers, int dim,
                       int rows, void* out_bf16) {
-    g4_status st = g4::use_device(ctx);
-    if (st) return st;
-    if (rows < 0 || !gate || !per_layer || !out_bf16 || layer < 0 || layer >= layers)
-        return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple: bad arguments");
-    const long long n = (long long)rows * dim;
-    if (n == 0) return G4_OK;
-    return g4::launch(ctx, "gelu_ple_kernel", gelu_ple_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, gate,
-                      per_layer, layer, layers, dim, n, static_cast<uint16_t*>(out_bf16));
+    const g4_planes one{gate, 1, 0, dim};
+    return g4_gelu_ple_planes(ctx, &one, per_layer, layer, layers, dim, rows, out_bf16);
 }
 
 g4_status g4_ple_mix(g4_ctx* ctx, const float* proj, float proj_scale, const float* norm, const float* tok_ple,

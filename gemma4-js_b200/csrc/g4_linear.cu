@@ -468,4 +468,19 @@ g4_status g4_linear_w4a16(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16,
     return g4_linear_w4a16_impl(ctx, lin, x_bf16, M, y, y_dtype, 0);
 }
 
+g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, g4_planes* out) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!lin || !out || !x_bf16 || M <= 0) return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_planes: bad arguments");
+    if (reinterpret_cast<uintptr_t>(x_bf16) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_planes: x must be 16-byte aligned");
+    const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
+    if (M > 16 && g4::gemm_supported(lin, M)) return g4::launch_gemm_planes(ctx, lin, x, M, out);
+    // the GEMV's f32 output is the one plane
+    st = g4::ensure_workspace(ctx, (size_t)M * lin->dev.N * 4);
+    if (st) return st;
+    *out = g4_planes{static_cast<const float*>(ctx->ws), 1, 0, lin->dev.N};
+    return g4::launch_gemv(ctx, lin, x, M, ctx->ws, 1);
+}
+
 }  // extern "C"

@@ -27,6 +27,8 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
 // tcgen05 W4A16 GEMM, weights dequantised into tensor memory (g4_gemm_w4.cu)
 bool gemm_supported(const g4_linear* lin, int M);
 g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32);
+// The f32 output left as partial planes in the context workspace (see g4_planes).
+g4_status launch_gemm_planes(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, g4_planes* planes);
 // tcgen05 GEMM with a bf16 B operand loaded by TMA (bmap: [N, K] bf16, boxes of 64 x 256,
 // 128B swizzle); y f32 [M, N].
 g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, const uint16_t* x, int M, float* y);

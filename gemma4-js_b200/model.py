@@ -29,7 +29,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import G4Rows, call
+from ._lib import G4Planes, G4Rows, call
 from .runtime import Context, G4Error, KVCache, PleW4Table, W4Linear
 
 
@@ -291,6 +291,13 @@ class Gemma4Model:
     def _w4(self, lin, x, rows, y):
         call("g4_linear_w4a16", self.ctx.handle, lin.handle, _ptr(x), rows, _ptr(y), 0)
 
+    def _w4p(self, lin, x, rows) -> G4Planes:
+        """The linear's f32 output left as split-K planes in the context workspace, read
+        (and summed) by the row-wise operator that follows."""
+        pl = G4Planes()
+        call("g4_linear_w4a16_planes", self.ctx.handle, lin.handle, _ptr(x), rows, C.byref(pl))
+        return pl
+
     def _forward(self, ids, rows, rmap: G4Rows, head_rows: int, head_x_row0: int):
         """Issues one forward of `rows` rows (ids: int32 device [rows]) and the greedy pick
         of `head_rows` rows starting at row head_x_row0 into buf["next"]."""
@@ -308,28 +315,28 @@ class Gemma4Model:
             s = Ly["spec"]
             hd = s["hd"]
             # encodeLayer (gemma4-webgpu.js:215-310)
-            self._w4(Ly["qkv"], b["x"], rows, b["qkv"])
             kv = Ly["kv"]
             kp, vp = C.c_void_p(), C.c_void_p()
             call("g4_kv_buffers", kv.handle, C.byref(kp), C.byref(vp))
-            call("g4_qkv_post", h, _ptr(b["qkv"]), Ly["qkv"].out_dim, cfg.heads, hd, 0 if s["shared"] else 1,
+            qkv = self._w4p(Ly["qkv"], b["x"], rows)
+            call("g4_qkv_post_planes", h, C.byref(qkv), cfg.heads, hd, 0 if s["shared"] else 1,
                  _ptr(Ly["qn"]), _ptr(Ly["kn"]), C.c_float(cfg.eps), s["rope_angles"], C.c_float(s["rope_base"]),
                  C.byref(rmap), rows, _ptr(b["q"]), kp, vp, self.max_seq)
             call("g4_attention_rows", h, _ptr(b["q"]), kv.handle, rows, cfg.heads, hd, C.byref(rmap), self.max_seq,
                  0 if s["full"] else 1, cfg.window, _ptr(b["attn"]))
-            self._w4(Ly["o"], b["attn"], rows, b["y"])
-            call("g4_post_norm_add", h, _ptr(b["h"]), _ptr(b["y"]), H, _ptr(Ly["n_pa"]), C.c_float(1.0),
+            y = self._w4p(Ly["o"], b["attn"], rows)
+            call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pa"]), C.c_float(1.0),
                  _ptr(Ly["n_pf"]), rows, H, C.c_float(cfg.eps), _ptr(b["x"]))
-            self._w4(Ly["gu"], b["x"], rows, b["gu"])
-            call("g4_gelu_mul", h, _ptr(b["gu"]), rows, s["inter"], _ptr(b["act"]))
-            self._w4(Ly["down"], b["act"], rows, b["y"])
-            call("g4_post_norm_add", h, _ptr(b["h"]), _ptr(b["y"]), H, _ptr(Ly["n_pff"]), C.c_float(1.0), None,
+            gu = self._w4p(Ly["gu"], b["x"], rows)
+            call("g4_gelu_mul_planes", h, C.byref(gu), rows, s["inter"], _ptr(b["act"]))
+            y = self._w4p(Ly["down"], b["act"], rows)
+            call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pff"]), C.c_float(1.0), None,
                  rows, H, C.c_float(cfg.eps), _ptr(b["x"]))
-            self._w4(Ly["pg"], b["x"], rows, b["pg"])
-            call("g4_gelu_ple", h, _ptr(b["pg"]), _ptr(b["per_layer"]), i, L, P, rows, _ptr(b["pa"]))
-            self._w4(Ly["pp"], b["pa"], rows, b["y"])
+            pg = self._w4p(Ly["pg"], b["x"], rows)
+            call("g4_gelu_ple_planes", h, C.byref(pg), _ptr(b["per_layer"]), i, L, P, rows, _ptr(b["pa"]))
+            y = self._w4p(Ly["pp"], b["pa"], rows)
             w_next = self.layers[i + 1]["n_in"] if i + 1 < L else self.final_norm  # :404 final rms fused here
-            call("g4_post_norm_add", h, _ptr(b["h"]), _ptr(b["y"]), H, _ptr(Ly["n_pple"]), C.c_float(Ly["skip"]),
+            call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pple"]), C.c_float(Ly["skip"]),
                  _ptr(w_next), rows, H, C.c_float(cfg.eps), _ptr(b["x"]))
         # logits + greedy (gemma4-webgpu.js:413-480)
         xh = b["x"][head_x_row0:head_x_row0 + head_rows]

@@ -115,6 +115,21 @@ g4_status g4_linear_w4a16(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16,
 g4_status g4_linear_w4a16_impl(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
                                void* y, g4_dtype y_dtype, int impl);
 
+/* The FP32 output of a linear as `count` partial planes (K split over `count` slices):
+ * y[r][c] = base[0*stride + r*ld + c] + base[1*stride + r*ld + c] + ... added in slice
+ * order (the same bits g4_linear_w4a16 returns with G4_F32). */
+typedef struct {
+    const float* base;
+    int count;
+    long long stride;
+    int ld;
+} g4_planes;
+/* No reference counterpart: g4_linear_w4a16 without its last pass.  The planes live in the
+ * context workspace and stay valid until the next call on this context that uses the
+ * workspace (a linear, a split attention, g4_softcap_argmax); the *_planes row-wise
+ * operators below read them, adding the slices on the way in. */
+g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, g4_planes* out);
+
 /* Dequantises rows [row_start, row_start+row_count) of the weight into out
  * [row_count, K]: f32 = (nibble-8) * f32(scale) exactly as dequantizeOfficialW4A16Rows
  * (browser-tfjs-webgl-distribution/runtime/official-w4a16.js:50-101); G4_BF16 = the
@@ -235,6 +250,16 @@ g4_status g4_gelu_mul(g4_ctx* ctx, const float* gate_up, int rows, int inter, vo
 /* GPUOps.geluPle (GELU_PLE :1159-1173): bf16(gelu(gate) * per_layer[row, layer, :]). */
 g4_status g4_gelu_ple(g4_ctx* ctx, const float* gate, const float* per_layer, int layer, int layers, int dim,
                       int rows, void* out_bf16);
+/* The same four operators reading a linear's output as g4_planes (the row pitch is
+ * planes->ld; no reference counterpart beyond their plain forms). */
+g4_status g4_post_norm_add_planes(g4_ctx* ctx, float* h, const g4_planes* y, const float* w_post, float skip,
+                                  const float* w_next, int rows, int width, float eps, void* x_out_bf16);
+g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd, int has_kv, const float* qnorm,
+                             const float* knorm, float eps, int rope_angles, float rope_base, const g4_rows* map,
+                             int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap);
+g4_status g4_gelu_mul_planes(g4_ctx* ctx, const g4_planes* gate_up, int rows, int inter, void* out_bf16);
+g4_status g4_gelu_ple_planes(g4_ctx* ctx, const g4_planes* gate, const float* per_layer, int layer, int layers,
+                             int dim, int rows, void* out_bf16);
 /* GPUOps.scale + GPUOps.pleMix (SCALE :1130-1137, PLE_MIX :1250-1263, gemma4-webgpu.js:318-321):
  * out = (rms(proj * proj_scale) * norm + tok_ple * sqrt(dim)) / sqrt(2) per [row, layer] segment. */
 g4_status g4_ple_mix(g4_ctx* ctx, const float* proj, float proj_scale, const float* norm, const float* tok_ple,

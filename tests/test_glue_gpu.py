@@ -146,3 +146,49 @@ def test_embed(ctx):
     ref = E[ids.long()].float() * np.float32(math.sqrt(1536))
     assert torch.equal(h, ref)
     assert torch.equal(x, ref.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("M,K,N", [(256, 6144, 1536), (256, 1536, 2560), (40, 1536, 256), (8, 1536, 1536)])
+def test_planes_consumers_match_the_summed_linear(rt, ctx, M, K, N):
+    """g4_linear_w4a16_planes + the *_planes operators give the same bits as the linear's
+    f32 output fed to the plain operators (split K, one plane, and the GEMV)."""
+    gen = g(M + K + N)
+    packed = torch.randint(-2**31, 2**31 - 1, (N, K // 8), device="cuda", dtype=torch.int32, generator=gen)
+    sc = torch.randn((N, K // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+    lin = rt.W4Linear(ctx, packed, sc)
+    x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    L.call("g4_linear_w4a16", ctx.handle, lin.handle, P(x), M, P(y), 0)
+    # post_norm_add
+    h0 = torch.randn((M, N), device="cuda", generator=gen)
+    wp = torch.rand(N, device="cuda", generator=gen) + 0.5
+    wn = torch.rand(N, device="cuda", generator=gen) + 0.5
+    h1, h2 = h0.clone(), h0.clone()
+    x1 = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    x2 = torch.empty_like(x1)
+    L.call("g4_post_norm_add", ctx.handle, P(h1), P(y), N, P(wp), C.c_float(0.9), P(wn), M, N, C.c_float(1e-6), P(x1))
+    pl = L.G4Planes()
+    L.call("g4_linear_w4a16_planes", ctx.handle, lin.handle, P(x), M, C.byref(pl))
+    L.call("g4_post_norm_add_planes", ctx.handle, P(h2), C.byref(pl), P(wp), C.c_float(0.9), P(wn), M, N,
+           C.c_float(1e-6), P(x2))
+    assert torch.equal(h1, h2) and torch.equal(x1, x2)
+    # gelu_mul over [gate | up] halves
+    inter = N // 2
+    a1 = torch.empty((M, inter), dtype=torch.bfloat16, device="cuda")
+    a2 = torch.empty_like(a1)
+    L.call("g4_gelu_mul", ctx.handle, P(y), M, inter, P(a1))
+    L.call("g4_linear_w4a16_planes", ctx.handle, lin.handle, P(x), M, C.byref(pl))
+    L.call("g4_gelu_mul_planes", ctx.handle, C.byref(pl), M, inter, P(a2))
+    assert torch.equal(a1, a2)
+    # gelu_ple over the first 256 columns as the gate of layer 1 of 3
+    dim = 256 if N >= 256 else N
+    per = torch.randn((M, 3, dim), device="cuda", generator=gen)
+    yg = y[:, :dim].contiguous()
+    b1 = torch.empty((M, dim), dtype=torch.bfloat16, device="cuda")
+    b2 = torch.empty_like(b1)
+    L.call("g4_gelu_ple", ctx.handle, P(yg), P(per), 1, 3, dim, M, P(b1))
+    L.call("g4_linear_w4a16_planes", ctx.handle, lin.handle, P(x), M, C.byref(pl))
+    pl_g = L.G4Planes(pl.base, pl.count, pl.stride, pl.ld)  # the gate reads columns 0..dim-1 of each row
+    L.call("g4_gelu_ple_planes", ctx.handle, C.byref(pl_g), P(per), 1, 3, dim, M, P(b2))
+    assert torch.equal(b1, b2)
+    ctx.check_device()
