@@ -317,6 +317,12 @@ inline unsigned blocks_for(long long n, int t) { return (unsigned)((n + t - 1) /
 
 }  // namespace
 
+namespace g4 {
+g4_status launch_argmax_final(g4_ctx* ctx, const float2* part, int nparts, int rows, int32_t* ids, float* vals) {
+    return launch(ctx, "argmax_final_kernel", argmax_final_kernel, dim3(rows), dim3(256), 0, 1, part, nparts, ids, vals);
+}
+}  // namespace g4
+
 extern "C" {
 
 g4_status g4_rms(g4_ctx* ctx, const float* x, const float* scale, int rows, int width, float eps, void* out,

@@ -7,7 +7,9 @@
 // tcgen05 GEMM with the bf16 operand loaded by TMA.  The softcap and the argmax are
 // g4_softcap_argmax (g4_glue.cu).
 #include "g4_common.cuh"
+#include "g4_glue.cuh"
 #include "g4_linear.cuh"
+#include "g4_tcgen05.cuh"
 
 struct g4_dense {
     g4_ctx* ctx = nullptr;
@@ -101,6 +103,174 @@ __global__ void __launch_bounds__(kHeadWarps * 32) head_gemv_kernel(const uint16
         }
 }
 
+
+// ---- fused head: logits tiles on tcgen05, softcap + greedy pick in the epilogue ------
+// Tiles of 128 tokens (MMA M, TMEM lanes) x 256 vocabulary rows (MMA N): A = x and B =
+// the bf16 table, both by TMA (128-byte swizzle) into a 4-stage ring; one thread issues
+// 8 MMAs per pair of stages; the accumulator is double-buffered in TMEM (2 x 256 columns)
+// so the epilogue of a tile overlaps the next tile's MMAs.  Epilogue warp w owns TMEM lane
+// quarter w % 4 (32 tokens) and one half of the tile's columns: each thread reduces its
+// token's 128 logits in registers (softcap, then the lowest index of the largest value)
+// and writes one (value, index) pair; the logits never reach memory.
+constexpr int HM = 128, HN = 256, HK = 64;
+constexpr int kHStages = 4;
+constexpr int kHEpi = 8;
+constexpr int kHThreads = (2 + kHEpi) * 32;
+constexpr int kHABytes = HM * HK * 2;              // 16 KB
+constexpr int kHStageBytes = kHABytes + HN * HK * 2;  // + 32 KB
+constexpr int kHSmem = kHStages * kHStageBytes + 256 + 1024;
+
+struct HeadParams {
+    int M, N, KB, MT, NT;  // KB = 64-column blocks of K; MT token tiles, NT vocabulary tiles
+    float cap;
+    float2* part;          // [M][2 * NT] (value, index bits)
+    uint32_t* err;
+};
+
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+__global__ void __launch_bounds__(kHThreads, 1)
+head_argmax_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                   const HeadParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kHStages * kHStageBytes);
+    uint64_t* empty = full + kHStages;
+    uint64_t* acc_full = empty + kHStages;  // [2]
+    uint64_t* acc_empty = acc_full + 2;     // [2]
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = p.MT * p.NT;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kHStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kHEpi);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) tmem_alloc(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    pdl_trigger();
+    if (warp >= 2) pdl_wait();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tensor_map(&xmap);
+            prefetch_tensor_map(&wmap);
+            int pre = 0;  // the table is immutable: its first boxes before the predecessor wait
+            for (int t = blockIdx.x; t < ntiles && pre < kHStages; t += gridDim.x)
+                for (int kb = 0; kb < p.KB && pre < kHStages; ++kb, ++pre) {
+                    mbar_arrive_expect_tx(&full[pre], kHStageBytes);
+                    tma_load_2d(smem + pre * kHStageBytes + kHABytes, &wmap, &full[pre], kb * HK, (t / p.MT) * HN);
+                }
+            pdl_wait();
+            bool ok = true;
+            int g = 0;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int mt = t % p.MT, nt = t / p.MT;
+                for (int kb = 0; kb < p.KB; ++kb, ++g) {
+                    const int s = g % kHStages;
+                    if (g >= kHStages) {
+                        if (!mbar_wait(&empty[s], ((g / kHStages) - 1) & 1, p.err, 0x201)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], kHStageBytes);
+                        tma_load_2d(smem + s * kHStageBytes + kHABytes, &wmap, &full[s], kb * HK, nt * HN);
+                    }
+                    tma_load_2d(smem + s * kHStageBytes, &xmap, &full[s], kb * HK, mt * HM);
+                }
+            }
+            for (int j = g > kHStages ? g - kHStages : 0; j < g; ++j)
+                mbar_wait(&full[j % kHStages], (j / kHStages) & 1, p.err, 0x202);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // -------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = mma_idesc_bf16(HM, HN);
+            bool ok = true;
+            int g = 0, tj = 0;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++tj) {
+                const int ab = tj & 1;
+                if (tj >= 2 && !mbar_wait(&acc_empty[ab], ((tj >> 1) - 1) & 1, p.err, 0x203)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + ab * HN;
+                for (int kb = 0; kb < p.KB && ok; kb += 2) {
+                    const int n = min(2, p.KB - kb);
+                    for (int u = 0; u < n && ok; ++u)
+                        ok = mbar_wait(&full[(g + u) % kHStages], ((g + u) / kHStages) & 1, p.err, 0x204);
+                    if (!ok) break;
+                    tc_fence_after();
+                    for (int u = 0; u < n; ++u) {
+                        const uint32_t a0 = smem_u32(smem + ((g + u) % kHStages) * kHStageBytes), b0 = a0 + kHABytes;
+#pragma unroll
+                        for (int ks = 0; ks < HK / 16; ++ks)
+                            tc_mma_ss(acc, sw128_desc(a0 + ks * 32), sw128_desc(b0 + ks * 32), idesc,
+                                      (kb + u > 0 || ks > 0) ? 1u : 0u);
+                    }
+                    for (int u = 0; u < n; ++u) tc_commit(&empty[(g + u) % kHStages]);
+                    g += n;
+                }
+                tc_commit(&acc_full[ab]);  // tile complete (or abandoned after a timeout)
+            }
+        }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------- softcap + argmax
+        const int q = warp & 3, e = (warp - 2) >> 2;
+        int tj = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tj) {
+            const int ab = tj & 1, mt = t % p.MT, nt = t / p.MT;
+            if (!mbar_wait_warp(&acc_full[ab], (tj >> 1) & 1, p.err, 0x205)) break;
+            tc_fence_after();
+            const uint32_t tq = tmem + ab * HN + ((uint32_t)(32 * q) << 16) + 128 * e;
+            const int n0 = nt * HN + 128 * e;
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
+            for (int c = 0; c < 128; c += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(tq + c, v);
+                tmem_ld_wait(v);
+                if (c == 96) {  // the accumulator buffer is free for the tile after next
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                }
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) {
+                    const int n = n0 + c + jj;
+                    const float raw = __uint_as_float(v[jj]);
+                    const float val = p.cap > 0.f ? tanhf(raw / p.cap) * p.cap : raw;
+                    if (n < p.N && val == val) better(bv, bi, val, n);  // NaN skipped, as g4_softcap_argmax
+                }
+            }
+            const int m = mt * HM + 32 * q + lane;
+            if (m < p.M) p.part[(size_t)m * (2 * p.NT) + nt * 2 + e] = make_float2(bv, __int_as_float(bi));
+        }
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
 }  // namespace
 
 extern "C" {
@@ -175,6 +345,43 @@ g4_status g4_dense_matmul(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, in
                           d->N, d->K, x, M, y, ctx->d_err);
     return g4::launch(ctx, "head_gemv_kernel", head_gemv_kernel<2>, dim3(grid), dim3(kHeadWarps * 32), smem, 1, w, d->N,
                       d->K, x, M, y, ctx->d_err);
+}
+
+g4_status g4_dense_argmax(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, int M, float cap, int32_t* ids_out,
+                          float* vals_out) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!d || !x_bf16 || !ids_out || M < 0) return g4::set_error(G4_ERR_INVALID, "g4_dense_argmax: bad arguments");
+    if (M == 0) return G4_OK;
+    if (reinterpret_cast<uintptr_t>(x_bf16) % 16 != 0 || d->K % 8 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_dense_argmax: x must be 16-byte aligned and K a multiple of 8");
+    static std::atomic<uint64_t> attr_set{0};
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(head_argmax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kHSmem));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    HeadParams p{};
+    p.M = M;
+    p.N = d->N;
+    p.KB = (d->K + HK - 1) / HK;
+    p.MT = (M + HM - 1) / HM;
+    p.NT = (d->N + HN - 1) / HN;
+    p.cap = cap;
+    p.err = ctx->d_err;
+    const int nparts = 2 * p.NT;
+    st = g4::ensure_workspace(ctx, (size_t)M * nparts * sizeof(float2));
+    if (st) return st;
+    p.part = static_cast<float2*>(ctx->ws);
+    CUtensorMap xmap;
+    st = g4::encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<void*>(x_bf16), d->K, M,
+                                  (uint64_t)d->K * 2, HK, HM, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st) return st;
+    const long long ntiles = (long long)p.MT * p.NT;
+    const unsigned grid = (unsigned)std::min<long long>(ntiles, ctx->num_sms);
+    st = g4::launch(ctx, "head_argmax_kernel", head_argmax_kernel, dim3(grid), dim3(kHThreads), kHSmem, 1, xmap,
+                    d->bmap, p);
+    if (st) return st;
+    return g4::launch_argmax_final(ctx, p.part, nparts, M, ids_out, vals_out);
 }
 
 }  // extern "C"

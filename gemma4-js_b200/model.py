@@ -340,9 +340,13 @@ class Gemma4Model:
                  _ptr(w_next), rows, H, C.c_float(cfg.eps), _ptr(b["x"]))
         # logits + greedy (gemma4-webgpu.js:413-480)
         xh = b["x"][head_x_row0:head_x_row0 + head_rows]
-        call("g4_dense_matmul", h, self.head.handle, _ptr(xh), head_rows, _ptr(b["logits"]))
-        call("g4_softcap_argmax", h, _ptr(b["logits"]), head_rows, cfg.vocab, C.c_float(cfg.softcap), _ptr(b["next"]),
-             _ptr(b["val"]))
+        if head_rows > 16:  # batched: logits tiles reduced in the head kernel's epilogue, never stored
+            call("g4_dense_argmax", h, self.head.handle, _ptr(xh), head_rows, C.c_float(cfg.softcap), _ptr(b["next"]),
+                 _ptr(b["val"]))
+        else:
+            call("g4_dense_matmul", h, self.head.handle, _ptr(xh), head_rows, _ptr(b["logits"]))
+            call("g4_softcap_argmax", h, _ptr(b["logits"]), head_rows, cfg.vocab, C.c_float(cfg.softcap),
+                 _ptr(b["next"]), _ptr(b["val"]))
 
     def prefill(self, seq: int, ids) -> int:
         """greedy(tokenIds, startPos) for one sequence: appends the tokens at its current

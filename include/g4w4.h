@@ -281,6 +281,12 @@ g4_status g4_dense_destroy(g4_dense* d);
 g4_status g4_dense_weights(const g4_dense* d, void** w);
 /* y[M, N] f32 = x[M, K] bf16 . W^T (headChunk without the softcap, all chunks in one launch). */
 g4_status g4_dense_matmul(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, int M, float* y);
+/* Logits, softcap and greedy pick in one pass, without materialising the [M, N] logits:
+ * ids_out[m] (and vals_out[m], may be NULL) as g4_dense_matmul followed by
+ * g4_softcap_argmax (same bits: the same tensor-core accumulation order).  No reference
+ * counterpart beyond those two; uses the context workspace for [M, 2*ceil(N/256)] pairs. */
+g4_status g4_dense_argmax(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, int M, float cap, int32_t* ids_out,
+                          float* vals_out);
 
 #ifdef __cplusplus
 }

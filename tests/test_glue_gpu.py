@@ -192,3 +192,34 @@ def test_planes_consumers_match_the_summed_linear(rt, ctx, M, K, N):
     L.call("g4_gelu_ple_planes", ctx.handle, C.byref(pl_g), P(per), 1, 3, dim, M, P(b2))
     assert torch.equal(b1, b2)
     ctx.check_device()
+
+
+@pytest.mark.parametrize("M", [1, 17, 40, 300])
+@pytest.mark.parametrize("cap", [30.0, 0.0])
+def test_dense_argmax_fused_matches_two_pass(rt, ctx, M, cap):
+    """g4_dense_argmax (logits tiles + softcap + greedy pick in one kernel) against
+    g4_dense_matmul + g4_softcap_argmax: the same bits above 16 rows (the same tensor-core
+    accumulation order), the torch fp32 pick within rounding below."""
+    model = importlib.import_module("gemma4-js_b200.model")
+    V, K = 20000, 1536  # 79 vocabulary tiles, the last one partial
+    E = (torch.randn((V, K), device="cuda", generator=g(21)) * 0.05).to(torch.bfloat16)
+    d = model.Dense(ctx, E)
+    x = torch.randn((M, K), device="cuda", generator=g(22 + M)).to(torch.bfloat16)
+    ids2 = torch.empty(M, dtype=torch.int32, device="cuda")
+    vals2 = torch.empty(M, dtype=torch.float32, device="cuda")
+    L.call("g4_dense_argmax", ctx.handle, d.handle, P(x), M, C.c_float(cap), P(ids2), P(vals2))
+    ctx.check_device()
+    if M > 16:
+        logits = torch.empty((M, V), dtype=torch.float32, device="cuda")
+        L.call("g4_dense_matmul", ctx.handle, d.handle, P(x), M, P(logits))
+        ids1 = torch.empty(M, dtype=torch.int32, device="cuda")
+        vals1 = torch.empty(M, dtype=torch.float32, device="cuda")
+        L.call("g4_softcap_argmax", ctx.handle, P(logits), M, V, C.c_float(cap), P(ids1), P(vals1))
+        assert torch.equal(ids1, ids2) and torch.equal(vals1, vals2)
+    else:
+        ref = x.float() @ E.float().T
+        capped = torch.tanh(ref / cap) * cap if cap > 0 else ref
+        best = capped.max(dim=1).values
+        picked = capped.gather(1, ids2.long().unsqueeze(1)).squeeze(1)
+        assert torch.all(best - picked < 1e-3)
+        assert torch.allclose(vals2, best, atol=1e-3)
