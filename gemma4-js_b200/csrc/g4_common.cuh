@@ -118,6 +118,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2_bits(float lo, float hi) {
 }
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t b) { return __uint_as_float(b << 16); }
 
+// gelu_tanh of GELU_MUL (custom-webgpu/gpu-runtime.js:1139-1157) with the reference's clamp
+// of the tanh argument to [-10, 10] (:1154).
+__device__ __forceinline__ float gelu_ref(float x) {
+    const float c = 0.7978845608028654f;
+    const float z = c * (x + 0.044715f * x * x * x);
+    const float t = tanhf(fminf(fmaxf(z, -10.f), 10.f));
+    return 0.5f * x * (1.f + t);
+}
+
 // Programmatic dependent launch (no-ops when the kernel was launched without it).
 // Every kernel calls pdl_trigger() first, so its successor can be scheduled early, and
 // pdl_wait() before it reads or writes activations; only immutable weights may be

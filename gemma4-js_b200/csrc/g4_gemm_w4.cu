@@ -77,9 +77,32 @@ struct W4Params {
     int ksplit;      // CTAs sharing one tile, each over a slice of K (1: no split)
     int kper;        // weight blocks per K slice
     float* part;     // ksplit > 1: partial planes [ksplit][Mp][N] f32, Mp = MT * (TT > 128 ? 256 : TT)
+    // geglu: the weight rows of every 128-row slab are 64 gate rows then the 64 matching up
+    // rows; y is bf16 [M, N/2] = gelu(gate) * up (GELU_MUL), computed from the staged tile.
+    int geglu;
     uint32_t* err;
 };
 
+// GeGLU epilogue (W4Params::geglu): bf16 act[m, 64 ws + f] = gelu(gate_f) * up_f from a staged
+// f32 [128 tokens][128 rows] stage; warp (q, e) takes tokens 128e + q, +4, ..., lane l the
+// features 2l, 2l + 1 (each store writes one 128-byte row).  Compiled only into the GeGLU
+// instance of the kernel, so its
+// registers do not add to the plain kernel's (a separate template instance).
+__device__ __forceinline__ void geglu_rows(const uint8_t* stage, int q, int e, int lane, int ms, int ws,
+                                        const W4Params& p) {
+    const int half = TW / 2, ldo = p.N / 2;
+    for (int tl = q; tl < 128; tl += 4) {
+        const int tok = 128 * e + tl;
+        const int m = ms * p.TT + tok;
+        if (tok >= p.TT || m >= p.M) break;
+        const float2 gt = reinterpret_cast<const float2*>(stage + (size_t)tl * TW * 4)[lane];
+        const float2 up = reinterpret_cast<const float2*>(stage + (size_t)tl * TW * 4 + half * 4)[lane];
+        reinterpret_cast<uint32_t*>(reinterpret_cast<uint16_t*>(p.y) + (size_t)m * ldo + ws * half)[lane] =
+            pack_bf16x2_bits(gelu_ref(gt.x) * up.x, gelu_ref(gt.y) * up.y);
+    }
+}
+
+template <bool kGeglu>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap ymap,
                     const W4Params p) {
@@ -111,7 +134,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     // the tile's last MMAs read (bf16: one stage holds [T][128]; f32: one stage per 128
     // tokens); those stages are handed back to the producer by the epilogue (after the
     // stores have read them) instead of by the MMA commit.
-    const bool out_f32 = p.y_f32 || S > 1;  // partial planes are f32
+    const bool out_f32 = p.y_f32 || S > 1 || kGeglu;  // partial planes and GeGLU inputs are f32
     const int out_stages = (out_f32 && p.TT > 128) ? 2 : 1;
     const bool staged = NST >= out_stages;
     const int plane_row0 = kslice * p.MT * (p.TT > 128 ? 256 : p.TT);  // first row of this CTA's output plane
@@ -302,6 +325,14 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                         }
                     }
                 }
+                if constexpr (kGeglu) {
+                    asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
+                    geglu_rows(smem + Smem::kOffX + ((glast - e) % kStages) * kXBytes, q, e, lane, ms, ws, p);
+                    asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
+                    if (warp == 2 + kDq && lane == 0)
+                        for (int h = 0; h < out_stages; ++h) mbar_arrive(&load_empty[(glast - h) % kStages]);
+                    continue;
+                }
                 fence_proxy_async_smem();  // the generic stores, before the async-proxy read
                 asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
                 if (warp == 2 + kDq && lane == 0) {
@@ -383,6 +414,25 @@ __global__ void __launch_bounds__(256) splitk_sum_kernel(const float4* __restric
     }
 }
 
+// GeGLU over the f32 planes of a linear whose 128-row slabs are 64 gate rows then the 64
+// matching up rows: out[m, 64 s + j] = bf16(gelu(gate) * up), slices added in order.
+__global__ void __launch_bounds__(256) geglu_planes_kernel(const float* __restrict__ base, int count,
+                                                           long long stride, int ld, int M, int half_n,
+                                                           uint16_t* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)M * half_n) return;
+    const int m = (int)(i / half_n), f = (int)(i - (long long)m * half_n);
+    const size_t gcol = (size_t)m * ld + (f / 64) * 128 + (f % 64);
+    float g = base[gcol], u = base[gcol + 64];
+    for (int s = 1; s < count; ++s) {
+        g += base[(size_t)s * stride + gcol];
+        u += base[(size_t)s * stride + gcol + 64];
+    }
+    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(g) * u);
+}
+
 }  // namespace
 
 namespace g4 {
@@ -394,13 +444,17 @@ namespace g4 {
 // partial planes splitk_sum_kernel adds.
 // planes != nullptr: leave the f32 output as partial planes in the context workspace (no
 // summing pass; y is ignored) and describe them in *planes.
+// geglu != nullptr (and planes == nullptr): write bf16 GeGLU activations [M, N/2] there,
+// fused into the epilogue of an unsplit tile, else planes + geglu_planes_kernel.
 static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32,
-                           g4_planes* planes) {
+                           g4_planes* planes, uint16_t* geglu = nullptr) {
     const g4_linear_dev& L = lin->dev;
     if (!gemm_supported(lin, M)) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: shape K=%d N=%d", L.K, L.N);
     static std::atomic<uint64_t> attr_set{0};
     if (!(attr_set.load() & (1ull << ctx->device))) {
-        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_w4_tmem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_w4_tmem_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           Smem::kBytes));
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemm_w4_tmem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            Smem::kBytes));
         attr_set.fetch_or(1ull << ctx->device);
     }
@@ -425,6 +479,22 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
     p.kper = (p.Kc + S - 1) / S;
     S = (p.Kc + p.kper - 1) / p.kper;  // no empty slice
     p.ksplit = S;
+    if (geglu) {
+        const int nst = (p.kper + kSub - 1) / kSub, out_stages = p.TT > 128 ? 2 : 1;
+        if (S == 1 && nst >= out_stages && L.N % TW == 0) {
+            p.geglu = 1;
+            p.y_f32 = 1;
+            y = geglu;
+            p.y = y;
+        } else {  // the planes, then the GeGLU pass
+            g4_planes pl;
+            g4_status st0 = gemm_core(ctx, lin, x, M, nullptr, 1, &pl);
+            if (st0) return st0;
+            const long long n = (long long)M * (L.N / 2);
+            return launch(ctx, "geglu_planes_kernel", geglu_planes_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256),
+                          0, 1, pl.base, pl.count, pl.stride, pl.ld, M, L.N / 2, geglu);
+        }
+    }
     CUtensorMap xmap, ymap;
     g4_status st = encode_tensor_map_2d(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, const_cast<uint16_t*>(x), L.K, M,
                                         (uint64_t)L.K * 2, TK, p.TT, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -449,6 +519,8 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
         if (planes) *planes = g4_planes{p.part, S, Mp * L.N, L.N};
         st = encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.part, L.N, (uint64_t)(S * Mp),
                                   (uint64_t)L.N * 4, TW, std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else if (p.geglu) {
+        ymap = xmap;  // unused: GeGLU rows leave through plain coalesced stores
     } else {
         // Y tiles leave through TMA stores: bf16 boxes of [T][128], f32 boxes of [min(T, 128)][128]
         st = y_f32 ? encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, L.N, M, (uint64_t)L.N * 4, TW,
@@ -458,8 +530,10 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
     }
     if (st) return st;
     const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
-    st = launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel, dim3(grid), dim3(kThreads), Smem::kBytes, 1, xmap,
-                ymap, p);
+    st = p.geglu ? launch(ctx, "gemm_w4_tmem_kernel<geglu>", gemm_w4_tmem_kernel<true>, dim3(grid), dim3(kThreads),
+                          Smem::kBytes, 1, xmap, ymap, p)
+                 : launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel<false>, dim3(grid), dim3(kThreads),
+                          Smem::kBytes, 1, xmap, ymap, p);
     if (st || S == 1 || planes) return st;
     const long long n4 = (long long)M * (L.N / 4);
     return launch(ctx, "splitk_sum_kernel", splitk_sum_kernel, dim3((unsigned)((n4 + 255) / 256)), dim3(256), 0, 1,
@@ -472,6 +546,16 @@ g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
 
 g4_status launch_gemm_planes(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, g4_planes* planes) {
     return gemm_core(ctx, lin, x, M, nullptr, 1, planes);
+}
+
+g4_status launch_gemm_geglu(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, uint16_t* out) {
+    return gemm_core(ctx, lin, x, M, nullptr, 1, nullptr, out);
+}
+
+g4_status launch_geglu_planes(g4_ctx* ctx, const g4_planes& pl, int M, int N, uint16_t* out) {
+    const long long n = (long long)M * (N / 2);
+    return launch(ctx, "geglu_planes_kernel", geglu_planes_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, 1,
+                  pl.base, pl.count, pl.stride, pl.ld, M, N / 2, out);
 }
 
 }  // namespace g4

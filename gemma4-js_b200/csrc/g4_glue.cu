@@ -65,14 +65,6 @@ __device__ __forceinline__ float4 ld4_planes(const Planes& P, size_t off) {
     return a;
 }
 
-// gelu_tanh with the reference's clamp of the tanh argument to [-10, 10] (:1154).
-__device__ __forceinline__ float gelu_ref(float x) {
-    const float c = 0.7978845608028654f;
-    const float z = c * (x + 0.044715f * x * x * x);
-    const float t = tanhf(fminf(fmaxf(z, -10.f), 10.f));
-    return 0.5f * x * (1.f + t);
-}
-
 // RMS_SHADER: y = x * rsqrt(mean(x^2) + eps) * scale (scale optional).
 __global__ void __launch_bounds__(kRowThreads) rms_kernel(const float* __restrict__ x, const float* __restrict__ scale,
                                                           int width, float eps, void* __restrict__ out, int out_bf16) {

@@ -468,6 +468,24 @@ g4_status g4_linear_w4a16(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16,
     return g4_linear_w4a16_impl(ctx, lin, x_bf16, M, y, y_dtype, 0);
 }
 
+g4_status g4_linear_w4a16_geglu(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!lin || !x_bf16 || !out_bf16 || M < 0) return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_geglu: bad arguments");
+    if (lin->dev.N % 128 != 0)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_linear_w4a16_geglu: N = %d (whole 128-row slabs)", lin->dev.N);
+    if (M == 0) return G4_OK;
+    if (reinterpret_cast<uintptr_t>(x_bf16) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_geglu: x must be 16-byte aligned");
+    const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
+    uint16_t* out = static_cast<uint16_t*>(out_bf16);
+    if (M > 16 && g4::gemm_supported(lin, M)) return g4::launch_gemm_geglu(ctx, lin, x, M, out);
+    g4_planes pl;
+    st = g4_linear_w4a16_planes(ctx, lin, x_bf16, M, &pl);
+    if (st) return st;
+    return g4::launch_geglu_planes(ctx, pl, M, lin->dev.N, out);
+}
+
 g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, g4_planes* out) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;

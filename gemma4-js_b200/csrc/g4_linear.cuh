@@ -29,6 +29,10 @@ bool gemm_supported(const g4_linear* lin, int M);
 g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32);
 // The f32 output left as partial planes in the context workspace (see g4_planes).
 g4_status launch_gemm_planes(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, g4_planes* planes);
+// GeGLU of a linear whose 128-row slabs are 64 gate rows then the 64 matching up rows:
+// out bf16 [M, N/2] (fused into the GEMM epilogue when the tiles are not split).
+g4_status launch_gemm_geglu(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, uint16_t* out);
+g4_status launch_geglu_planes(g4_ctx* ctx, const g4_planes& pl, int M, int N, uint16_t* out);
 // tcgen05 GEMM with a bf16 B operand loaded by TMA (bmap: [N, K] bf16, boxes of 64 x 256,
 // 128B swizzle); y f32 [M, N].
 g4_status launch_gemm_bf16(g4_ctx* ctx, const CUtensorMap& bmap, int N, int K, const uint16_t* x, int M, float* y);

@@ -182,6 +182,18 @@ def random_weights_device(cfg: ModelConfig, seed: int = 0, sigma: float = 0.02, 
     return w
 
 
+def interleave_geglu(a, inter: int):
+    """Rows [gate (inter); up (inter)] -> slabs of 64 gate rows then the 64 matching up rows
+    (the layout g4_linear_w4a16_geglu reads); numpy or torch."""
+    g, u = a[:inter], a[inter:]
+    rest = tuple(a.shape[1:])
+    if isinstance(a, torch.Tensor):
+        return torch.stack([g.reshape(inter // 64, 64, *rest), u.reshape(inter // 64, 64, *rest)], dim=1).reshape(
+            2 * inter, *rest).contiguous()
+    return np.ascontiguousarray(np.stack([g.reshape(inter // 64, 64, *rest), u.reshape(inter // 64, 64, *rest)],
+                                         axis=1).reshape(2 * inter, *rest))
+
+
 def _dev_f32(a, device):
     return (a if isinstance(a, torch.Tensor) else torch.from_numpy(np.asarray(a))).to(device=device, dtype=torch.float32).contiguous()
 
@@ -238,8 +250,11 @@ class Gemma4Model:
         for i, lw in enumerate(w["layers"]):
             s = cfg.spec(i)
             L = {"spec": s, "skip": float(lw["skip"])}
-            for name in ("qkv", "o", "gu", "down", "pg", "pp"):
+            for name in ("qkv", "o", "down", "pg", "pp"):
                 L[name] = W4Linear(ctx, lw[name][0], lw[name][1], name=f"layers.{i}.{name}")
+            # gate and up rows interleaved in 64-row blocks: GeGLU is fused into the linear
+            L["gu"] = W4Linear(ctx, interleave_geglu(lw["gu"][0], s["inter"]), interleave_geglu(lw["gu"][1], s["inter"]),
+                               name=f"layers.{i}.gu")
             for n in ("n_in", "n_pa", "n_pf", "n_pff", "n_pple", "qn", "kn"):
                 L[n] = _dev_f32(lw[n], dev)
             L["kv"] = None if s["shared"] else KVCache(ctx, s["hd"], max_batch * max_seq)
@@ -327,8 +342,7 @@ class Gemma4Model:
             y = self._w4p(Ly["o"], b["attn"], rows)
             call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pa"]), C.c_float(1.0),
                  _ptr(Ly["n_pf"]), rows, H, C.c_float(cfg.eps), _ptr(b["x"]))
-            gu = self._w4p(Ly["gu"], b["x"], rows)
-            call("g4_gelu_mul_planes", h, C.byref(gu), rows, s["inter"], _ptr(b["act"]))
+            call("g4_linear_w4a16_geglu", h, Ly["gu"].handle, _ptr(b["x"]), rows, _ptr(b["act"]))
             y = self._w4p(Ly["down"], b["act"], rows)
             call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pff"]), C.c_float(1.0), None,
                  rows, H, C.c_float(cfg.eps), _ptr(b["x"]))

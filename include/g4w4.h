@@ -129,6 +129,11 @@ typedef struct {
  * workspace (a linear, a split attention, g4_softcap_argmax); the *_planes row-wise
  * operators below read them, adding the slices on the way in. */
 g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, g4_planes* out);
+/* GPUOps.geluMul fused into a linear (GELU_MUL, custom-webgpu/gpu-runtime.js:1139-1157):
+ * out bf16 [M, N/2] = gelu(gate) * up, for a linear whose weight rows come in slabs of
+ * 128 = 64 gate rows then the 64 matching up rows (N % 128 == 0).  Same bits as
+ * g4_linear_w4a16 (G4_F32) + g4_gelu_mul on the un-interleaved rows. */
+g4_status g4_linear_w4a16_geglu(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, void* out_bf16);
 
 /* Dequantises rows [row_start, row_start+row_count) of the weight into out
  * [row_count, K]: f32 = (nibble-8) * f32(scale) exactly as dequantizeOfficialW4A16Rows

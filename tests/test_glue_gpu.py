@@ -223,3 +223,26 @@ def test_dense_argmax_fused_matches_two_pass(rt, ctx, M, cap):
         picked = capped.gather(1, ids2.long().unsqueeze(1)).squeeze(1)
         assert torch.all(best - picked < 1e-3)
         assert torch.allclose(vals2, best, atol=1e-3)
+
+
+@pytest.mark.parametrize("M,K,inter", [(256, 1536, 6144), (40, 512, 1024), (3, 512, 1024), (300, 256, 512)])
+def test_geglu_fused_linear_matches_linear_then_gelu_mul(rt, ctx, M, K, inter):
+    """g4_linear_w4a16_geglu on the interleaved rows gives the same bits as the linear on
+    [gate; up] (f32) followed by g4_gelu_mul: fused epilogue (unsplit tiles), planes +
+    GeGLU pass (split K), GEMV below 17 rows."""
+    model = importlib.import_module("gemma4-js_b200.model")
+    gen = g(M + K + inter)
+    N = 2 * inter
+    packed = torch.randint(-2**31, 2**31 - 1, (N, K // 8), device="cuda", dtype=torch.int32, generator=gen)
+    sc = torch.randn((N, K // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+    lin = rt.W4Linear(ctx, packed, sc)
+    lin_i = rt.W4Linear(ctx, model.interleave_geglu(packed, inter), model.interleave_geglu(sc, inter))
+    x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    L.call("g4_linear_w4a16", ctx.handle, lin.handle, P(x), M, P(y), 0)
+    a1 = torch.empty((M, inter), dtype=torch.bfloat16, device="cuda")
+    L.call("g4_gelu_mul", ctx.handle, P(y), M, inter, P(a1))
+    a2 = torch.empty_like(a1)
+    L.call("g4_linear_w4a16_geglu", ctx.handle, lin_i.handle, P(x), M, P(a2))
+    ctx.check_device()
+    assert torch.equal(a1, a2)
