@@ -185,6 +185,23 @@ def time_graph(torch, ctx, launch, K, W, dist: Dist):
     return dist.max(ms)
 
 
+def time_e2e(torch, dist, step, n):
+    """Device time (ms, max over ranks) of one end-to-end step through the public API:
+    `step(i)` copies its inputs in from pinned host memory, runs, and copies the result out."""
+    for i in range(2):
+        step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(n):
+        step(i)
+    e.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    return dist.max(s.elapsed_time(e)) / n
+
+
 # ----------------------------------------------------------------- workloads
 def ple_setup(torch, rt, ctx, n_batches, T=4096, vocab=262144, width=8960, seed=0):
     gen = torch.Generator(device="cuda").manual_seed(seed)
@@ -301,6 +318,18 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
     per = ms / 1e3 / K
     gbs = byts / per / 1e9
     peak = peaks["hbm_gbs"]
+    # e2e: x from pinned host memory, y back to pinned host memory, every call
+    hx = x.cpu().pin_memory()
+    hy = torch.empty((1, N), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        x.copy_(hx, non_blocking=True)
+        launch(i)
+        hy.copy_(ys[i % 4], non_blocking=True)
+
+    e2e_ms = time_e2e(torch, dist, e2e_step, max(3, min(K, 50)))
+    e2e = {"value": round(GEMV_BYTES / (e2e_ms / 1e3) / 1e9 * dist.world, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": Kd * 2, "d2h_bytes_per_step": N * 2}
     return {
         "metric": "W4A16 decode GEMV throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
         "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
@@ -311,7 +340,7 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
         "roofline": {"bound": "hbm", "kernel": "gemv_w4a16_kernel", "achieved": round(gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
                      "traffic": TRAFFIC["gemv_w4a16_kernel"], "bytes_per_launch": byts},
-        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3),
+        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3), "e2e": e2e,
     }
 
 
@@ -343,6 +372,17 @@ def run_attn(args, torch, rt, ctx, dist, peaks):
     per = ms / 1e3 / K
     gbs = byts / per / 1e9
     peak = peaks["hbm_gbs"]
+    hq = q.cpu().pin_memory()
+    ho = torch.empty((1, 8, hd), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        q.copy_(hq, non_blocking=True)
+        launch(i)
+        ho.copy_(out, non_blocking=True)
+
+    e2e_ms = time_e2e(torch, dist, e2e_step, max(3, min(K, 50)))
+    e2e = {"value": round(ATTN_BYTES / (e2e_ms / 1e3) / 1e9 * dist.world, 2), "unit": "GB/s",
+           "h2d_bytes_per_step": 8 * hd * 2, "d2h_bytes_per_step": 8 * hd * 2}
     return {
         "metric": "GQA decode attention throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
         "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
@@ -352,7 +392,7 @@ def run_attn(args, torch, rt, ctx, dist, peaks):
         "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": round(gbs, 1), "peak": peak,
                      "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
                      "traffic": TRAFFIC["attn_decode_kernel"], "bytes_per_launch": byts},
-        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3),
+        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3), "e2e": e2e,
     }
 
 
@@ -366,6 +406,7 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
     n0 = rt.launch_count()
     clk.start()
     tot_flop, tot_s = 0.0, 0.0
+    e2e = None
     shapes = [(1536, 6144), (6144, 1536), (1536, 262144)]
     ms_list = (16, 128, 512, 2048)
     if args.gemm_shapes:  # "M1,M2:KxN,KxN" e.g. "128,256:1536x2560,6144x1536"
@@ -403,6 +444,19 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
             if M >= 512:
                 tot_flop += flop
                 tot_s += per
+            if (M, Kd, N) == (2048, 1536, 6144) and e2e is None:
+                hx = x.cpu().pin_memory()
+                hy = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+
+                def e2e_step(i, x=x, y=y, hx=hx, hy=hy, launch=launch):
+                    x.copy_(hx, non_blocking=True)
+                    launch(i)
+                    hy.copy_(y, non_blocking=True)
+
+                e2e_ms = time_e2e(torch, dist, e2e_step, max(3, min(K_steps, 10)))
+                e2e = {"value": round(flop / (e2e_ms / 1e3) / 1e12 * dist.world, 2), "unit": "TFLOP/s",
+                       "h2d_bytes_per_step": M * Kd * 2, "d2h_bytes_per_step": M * N * 2,
+                       "point": "M=2048, K=1536, N=6144 (x in from and y out to pinned host memory)"}
             del x, y
         del lins
         torch.cuda.empty_cache()
@@ -423,7 +477,7 @@ def run_gemm(args, torch, rt, ctx, dist, peaks):
                      "peak_source": peaks["source"], "traffic": gemm_traffic(best["M"], best["K"], best["N"]),
                      "traffic_basis": "ncu DRAM bytes at M=2048 K=1536 N=6144 scaled by the weight + X bytes",
                      "point": best},
-        "sweep": points, "gpu_launches": rt.launch_count() - n0, "clocks": clocks,
+        "sweep": points, "gpu_launches": rt.launch_count() - n0, "clocks": clocks, "e2e": e2e,
     }
 
 
