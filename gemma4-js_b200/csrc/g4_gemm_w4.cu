@@ -292,8 +292,10 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             tc_fence_after();
             if (staged) {
                 // Drain the accumulator into the X stage(s) as [token][128 weight rows] (bf16:
-                // all T tokens in the last stage; f32: tokens 128e.. in stage g_last - e),
-                // release it after the last TMEM load, then one thread stores with TMA.
+                // all T tokens in the last stage; f32: tokens 128e.. in stage g_last - e) and
+                // release it after the last TMEM load.  Each 32-token chunk leaves through a
+                // TMA store as soon as the four warps of its half have staged it, so the store
+                // overlaps the rest of the drain.
                 const int glast = (tj + 1) * NST - 1;
                 uint8_t* stg = smem + Smem::kOffX + ((glast - (out_f32 ? e : 0)) % kStages) * kXBytes;
                 for (int c = cbeg; c < cend || (c == cbeg && cbeg >= cend); c += 32) {
@@ -324,6 +326,16 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                             col[(jj + 1) * TW] = (uint16_t)(bits >> 16);
                         }
                     }
+                    if constexpr (!kGeglu) {
+                        fence_proxy_async_smem();  // the generic stores, before the async-proxy read
+                        if (e == 0) asm volatile("bar.sync 2, 128;" ::: "memory");  // the half's 4 warps
+                        else asm volatile("bar.sync 3, 128;" ::: "memory");
+                        if (q == 0 && lane == 0) {
+                            const uint8_t* src = out_f32 ? stg + (size_t)(c - cbeg) * TW * 4 : stg + (size_t)c * TW * 2;
+                            tma_store_2d(&ymap, src, ws * TW, plane_row0 + ms * p.TT + c);
+                            bulk_commit_group();
+                        }
+                    }
                 }
                 if constexpr (kGeglu) {
                     asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
@@ -333,16 +345,10 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                         for (int h = 0; h < out_stages; ++h) mbar_arrive(&load_empty[(glast - h) % kStages]);
                     continue;
                 }
-                fence_proxy_async_smem();  // the generic stores, before the async-proxy read
+                if (q == 0 && lane == 0) bulk_wait_read_all();  // this half's stores have read the stage
                 asm volatile("bar.sync 1, %0;" ::"r"(kEpi * 32) : "memory");
-                if (warp == 2 + kDq && lane == 0) {
-                    for (int h = 0; h < out_stages; ++h)
-                        tma_store_2d(&ymap, smem + Smem::kOffX + ((glast - h) % kStages) * kXBytes, ws * TW,
-                                     plane_row0 + ms * p.TT + 128 * h);
-                    bulk_commit_group();
-                    bulk_wait_read_all();
+                if (warp == 2 + kDq && lane == 0)
                     for (int h = 0; h < out_stages; ++h) mbar_arrive(&load_empty[(glast - h) % kStages]);
-                }
                 continue;
             }
             // Fallback (f32 output, or a partial, with fewer stages than output stages): one
@@ -371,7 +377,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                 }
             }
         }
-        if (staged && warp == 2 + kDq && lane == 0) bulk_wait_all();  // the tile stores have landed
+        if (staged && q == 0 && lane == 0) bulk_wait_all();  // this half's tile stores have landed
         __syncwarp();
     }
 
@@ -511,22 +517,22 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
         *planes = g4_planes{static_cast<const float*>(ctx->ws), 1, 0, L.N};
     }
     if (S > 1) {
-        // partial planes [S][Mp][N] f32 in the context workspace; f32 boxes of [min(T, 128)][128]
+        // partial planes [S][Mp][N] f32 in the context workspace; boxes of [32 tokens][128 rows]
         const size_t bytes = (size_t)S * Mp * L.N * 4;
         st = ensure_workspace(ctx, bytes);
         if (st) return st;
         p.part = static_cast<float*>(ctx->ws);
         if (planes) *planes = g4_planes{p.part, S, Mp * L.N, L.N};
         st = encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, p.part, L.N, (uint64_t)(S * Mp),
-                                  (uint64_t)L.N * 4, TW, std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE);
+                                  (uint64_t)L.N * 4, TW, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
     } else if (p.geglu) {
         ymap = xmap;  // unused: GeGLU rows leave through plain coalesced stores
     } else {
-        // Y tiles leave through TMA stores: bf16 boxes of [T][128], f32 boxes of [min(T, 128)][128]
-        st = y_f32 ? encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, L.N, M, (uint64_t)L.N * 4, TW,
-                                          std::min(p.TT, 128), CU_TENSOR_MAP_SWIZZLE_NONE)
-                   : encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW,
-                                          p.TT, CU_TENSOR_MAP_SWIZZLE_NONE);
+        // Y tiles leave through TMA stores of [32 tokens][128 rows] chunks
+        st = y_f32 ? encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, y, L.N, M, (uint64_t)L.N * 4, TW, 32,
+                                          CU_TENSOR_MAP_SWIZZLE_NONE)
+                   : encode_tensor_map_2d(&ymap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, y, L.N, M, (uint64_t)L.N * 2, TW, 32,
+                                          CU_TENSOR_MAP_SWIZZLE_NONE);
     }
     if (st) return st;
     const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
