@@ -15,13 +15,15 @@ LIB_PATH = PKG / "libg4w4.so"
 HEADER = PKG.parent / "include" / "g4w4.h"
 
 G4_OK = 0
+G4_ROWS_HISTORY_READY = 1
 G4_F32 = 0
 G4_BF16 = 1
 
 
 class G4Rows(C.Structure):
     """g4_rows: where the rows of a batch sit in their sequences (include/g4w4.h)."""
-    _fields_ = [("seq_pos", C.c_void_p), ("seq_base", C.c_int), ("rows_per_seq", C.c_int), ("pos0", C.c_int)]
+    _fields_ = [("seq_pos", C.c_void_p), ("seq_base", C.c_int), ("rows_per_seq", C.c_int), ("pos0", C.c_int),
+                ("flags", C.c_int)]
 
 
 class G4Planes(C.Structure):

@@ -7,7 +7,10 @@
 // pipeline, one producer warp), computes S^T = K Q^T and O^T += V^T P^T on the tensor
 // cores with the 8 query heads as the n = 8 dimension (so no padding is computed),
 // and keeps an online softmax in registers.  Long key ranges are split over CTAs
-// (split-KV) and merged by a small combine kernel through a scratch buffer.
+// (split-KV) and merged by a small combine kernel through a scratch buffer.  Batched
+// decode of a sliding layer with more sequences than SMs uses tiles of half the keys so
+// that two CTAs share an SM: every CTA of the grid is resident from the start and no
+// second wave starts cold behind the first.
 #include <stdio.h>
 
 #include <mutex>
@@ -21,9 +24,9 @@ using namespace g4dev;
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-template <int HD>
+template <int HD, bool kNarrow = false>
 struct AttnCfg {
-    static constexpr int KT = 16384 / HD;       // keys per pipeline stage
+    static constexpr int KT = (kNarrow ? 8192 : 16384) / HD;  // keys per pipeline stage
     static constexpr int WARPS = KT / 16;       // consumer warps, 16 keys each
     static constexpr int BOXES = HD / 64;       // 128-byte wide TMA boxes per row
     static constexpr int BOX_BYTES = KT * 128;  // one box: KT rows x 128 B
@@ -31,13 +34,14 @@ struct AttnCfg {
     static constexpr int STAGES = 3;
     static constexpr int SMEM = STAGES * 2 * TILE_BYTES + 1024 + 256;
     static constexpr int THREADS = (WARPS + 1) * 32;
+    static constexpr int CTAS_PER_SM = kNarrow ? 2 : 1;
 };
 
 // Smem address of (key, d) for ldmatrix in a 128B-swizzled [KT x HD] tile.
-template <int HD>
+template <class C>
 __device__ __forceinline__ uint32_t tile_addr(uint32_t base, int key, int d) {
     const int box = d >> 6, chunk = (d & 63) >> 3;
-    return base + box * AttnCfg<HD>::BOX_BYTES + key * 128 + (((chunk ^ (key & 7))) << 4);
+    return base + box * C::BOX_BYTES + key * 128 + (((chunk ^ (key & 7))) << 4);
 }
 
 struct AttnParams {
@@ -55,13 +59,16 @@ struct AttnParams {
     // rows start at seq * seq_stride.
     const int32_t* seq_pos;
     int seq_base, rows_per_seq, pos0, seq_stride;
+    // G4_ROWS_HISTORY_READY: seq_pos and the cache rows below each row's first position
+    // are final before this grid starts, so they are read before the PDL wait.
+    int history_ready;
 };
 
-template <int HD>
-__global__ void __launch_bounds__(AttnCfg<HD>::THREADS, 1)
+template <int HD, bool kNarrow>
+__global__ void __launch_bounds__(AttnCfg<HD, kNarrow>::THREADS, AttnCfg<HD, kNarrow>::CTAS_PER_SM)
 attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                    AttnParams p) {
-    using C = AttnCfg<HD>;
+    using C = AttnCfg<HD, kNarrow>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // Offset the __shared__ array itself (not an integer round trip) so the compiler keeps
     // shared-memory addressing for every access through `smem`.
@@ -72,13 +79,19 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
     uint64_t* empty = full + C::STAGES;
 
     pdl_trigger();
-    pdl_wait();  // q, the newest K/V rows and the positions come from the predecessors
+    // q and the K/V rows of the current positions come from the predecessors.  With
+    // history_ready the older rows (and the positions) are final already: the producer
+    // streams them while the predecessors drain and waits only before the first tile
+    // that reaches the current positions.
+    const bool early = p.history_ready && p.seq_pos;
+    if (!early) pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r = blockIdx.y, split = blockIdx.x;
-    int qp, keylen, kv_row0;
+    int qp, keylen, kv_row0, first_new = 0;
     if (p.seq_pos) {
         const int seq = p.seq_base + r / p.rows_per_seq;
         const int base = p.seq_pos[seq] + p.pos0;
+        first_new = base;
         qp = base + r % p.rows_per_seq;
         keylen = base + p.rows_per_seq;
         kv_row0 = seq * p.seq_stride;
@@ -108,8 +121,12 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
         if (lane == 0 && ntiles > 0) {
             prefetch_tensor_map(&kmap);
             prefetch_tensor_map(&vmap);
-            bool ok = true;
+            bool ok = true, waited = !early;
             for (int t = 0; t < ntiles && ok; ++t) {
+                if (!waited && s_lo + (t + 1) * C::KT > first_new) {  // the tile reaches the current rows
+                    pdl_wait();
+                    waited = true;
+                }
                 const int s = t % C::STAGES;
                 if (t >= C::STAGES) ok = mbar_wait(&empty[s], ((t / C::STAGES) - 1) & 1, p.err);
                 if (!ok) break;
@@ -134,6 +151,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
     for (int i = 0; i < HD / 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
+    if (early) pdl_wait();  // every thread waits (the producer's lane 0 again: a no-op)
     if (warp < C::WARPS) {
         // Q^T as the B operand: b0b1 = Q[head g][16ks + 2tq ..], b2b3 = Q[g][16ks + 8 + 2tq ..]
         uint32_t qf[HD / 16][2];
@@ -156,7 +174,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks) {
                     uint32_t a[4];
-                    ldmatrix_x4(a, tile_addr<HD>(kb, key, ks * 16 + ((j >> 1) << 3)));
+                    ldmatrix_x4(a, tile_addr<C>(kb, key, ks * 16 + ((j >> 1) << 3)));
                     const uint32_t b[2] = {qf[ks][0], qf[ks][1]};
                     mma_bf16_16816(sc, a, b, sc);
                 }
@@ -205,7 +223,7 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
 #pragma unroll
                 for (int mi = 0; mi < HD / 16; ++mi) {
                     uint32_t a[4];
-                    ldmatrix_x4_trans(a, tile_addr<HD>(vb, key, mi * 16 + ((j & 1) << 3)));
+                    ldmatrix_x4_trans(a, tile_addr<C>(vb, key, mi * 16 + ((j & 1) << 3)));
                     mma_bf16_16816(o[mi], a, pb, o[mi]);
                     mma_bf16_16816(o[mi], a, pl, o[mi]);
                 }
@@ -335,12 +353,12 @@ __global__ void kv_append_f32_kernel(const float* __restrict__ k, const float* _
     vc[i] = (uint16_t)f32_to_bf16_bits(v[i]);
 }
 
-template <int HD>
+template <int HD, bool kNarrow>
 g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& vm, const uint16_t* q,
                         int rows, int heads, int keylen, int qpos0, int sliding, int window, uint16_t* out,
                         int kv_row0, void* fixed_scratch = nullptr, size_t fixed_bytes = 0,
                         const g4_rows* map = nullptr, int seq_stride = 0) {
-    using C = AttnCfg<HD>;
+    using C = AttnCfg<HD, kNarrow>;
     // Longest key range of any row decides the split.  With device-side positions the
     // host does not know the lengths: plan for a full sequence (or a full window).
     int lmax;
@@ -381,6 +399,7 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
         p.rows_per_seq = map->rows_per_seq;
         p.pos0 = map->pos0;
         p.seq_stride = seq_stride;
+        p.history_ready = (map->flags & G4_ROWS_HISTORY_READY) ? 1 : 0;
     }
     if (nsplit > 1) {
         const size_t ob = (size_t)rows * nsplit * 8 * HD * sizeof(float);
@@ -402,10 +421,11 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     }
     static std::atomic<uint64_t> attr_set{0};
     if (!(attr_set.load() & (1ull << ctx->device))) {
-        G4_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+        G4_CHECK_CUDA(cudaFuncSetAttribute(attn_decode_kernel<HD, kNarrow>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           C::SMEM));
         attr_set.fetch_or(1ull << ctx->device);
     }
-    g4_status st = g4::launch(ctx, "attn_decode_kernel", attn_decode_kernel<HD>, dim3(nsplit, rows), dim3(C::THREADS),
+    g4_status st = g4::launch(ctx, "attn_decode_kernel", attn_decode_kernel<HD, kNarrow>, dim3(nsplit, rows), dim3(C::THREADS),
                               C::SMEM, 1, km, vm, p);
     if (st) return st;
     if (nsplit > 1)
@@ -420,23 +440,39 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
 namespace g4 {
 
 g4_status make_kv_maps(g4_kv* kv) {
-    const uint32_t kt = 16384u / (uint32_t)kv->hd;
-    g4_status st = encode_tensor_map_2d(&kv->kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kv->k, kv->hd,
-                                        kv->rows_total, (uint64_t)kv->hd * 2, 64, kt,
-                                        CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st) return st;
-    return encode_tensor_map_2d(&kv->vmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kv->v, kv->hd, kv->rows_total,
-                                (uint64_t)kv->hd * 2, 64, kt, CU_TENSOR_MAP_SWIZZLE_128B);
+    CUtensorMap* maps[4] = {&kv->kmap, &kv->vmap, &kv->kmap_narrow, &kv->vmap_narrow};
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t kt = (i < 2 ? 16384u : 8192u) / (uint32_t)kv->hd;
+        g4_status st = encode_tensor_map_2d(maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, (i & 1) ? kv->v : kv->k,
+                                            kv->hd, kv->rows_total, (uint64_t)kv->hd * 2, 64, kt,
+                                            CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+    }
+    return G4_OK;
+}
+
+template <int HD>
+g4_status launch_attn_hd(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows, int heads,
+                         int keylen, int qpos0, int sliding, int window, uint16_t* out, void* fixed_scratch,
+                         size_t fixed_bytes, const g4_rows* map, int seq_stride) {
+    // Batched decode of sliding layers with more rows than SMs: one CTA per row's short
+    // window, two per SM, so the whole grid is resident at once.  (Global layers stream
+    // long key ranges, where the wide tiles measured faster.)
+    if (map && sliding && rows > ctx->num_sms)
+        return launch_attn_t<HD, true>(ctx, kv->kmap_narrow, kv->vmap_narrow, q, rows, heads, keylen, qpos0, sliding,
+                                       window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+    return launch_attn_t<HD, false>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out,
+                                    kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
 }
 
 g4_status launch_attention(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows, int heads,
                            int keylen, int qpos0, int sliding, int window, uint16_t* out, void* fixed_scratch,
                            size_t fixed_bytes, const g4_rows* map, int seq_stride) {
     switch (kv->hd) {
-        case 64: return launch_attn_t<64>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
-        case 128: return launch_attn_t<128>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
-        case 256: return launch_attn_t<256>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
-        case 512: return launch_attn_t<512>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 64: return launch_attn_hd<64>(ctx, kv, kv_row0, q, rows, heads, keylen, qpos0, sliding, window, out, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 128: return launch_attn_hd<128>(ctx, kv, kv_row0, q, rows, heads, keylen, qpos0, sliding, window, out, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 256: return launch_attn_hd<256>(ctx, kv, kv_row0, q, rows, heads, keylen, qpos0, sliding, window, out, fixed_scratch, fixed_bytes, map, seq_stride);
+        case 512: return launch_attn_hd<512>(ctx, kv, kv_row0, q, rows, heads, keylen, qpos0, sliding, window, out, fixed_scratch, fixed_bytes, map, seq_stride);
         default: return set_error(G4_ERR_UNSUPPORTED, "attention: head dim %d (64/128/256/512 supported)", kv->hd);
     }
 }

@@ -9,6 +9,7 @@ struct g4_kv {
     uint16_t* k = nullptr;      // [capacity, hd] bf16
     uint16_t* v = nullptr;
     CUtensorMap kmap, vmap;     // 128B-swizzled boxes of 64 columns x (16384/hd) rows
+    CUtensorMap kmap_narrow, vmap_narrow;  // the same with boxes of (8192/hd) rows
 };
 
 namespace g4 {

@@ -57,6 +57,7 @@ constexpr int kXSub = TTmax * TK * 2;         // 32 KB: one [T x 64] box
 constexpr int kXBytes = kSub * kXSub;         // 64 KB per stage
 constexpr int kBlkBytes = g4::kTblkBytes;     // 4096 B of nibbles + 512 B of scales
 constexpr int kTmemCols = 512;
+constexpr int kMaxSlices = 8;  // split-K slices (partial planes) per linear
 constexpr int kAccCol = 0, kACol = 256;
 
 struct Smem {
@@ -481,7 +482,9 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
     const long long ntiles = (long long)p.NS * p.MT;
     if (ntiles > 0x7fffffffLL) return set_error(G4_ERR_UNSUPPORTED, "tcgen05 GEMM: M=%d N=%d too large", M, L.N);
     int S = 1;
-    while (ntiles * (S + 1) <= ctx->num_sms && p.Kc / (S + 1) >= 3) ++S;
+    // At most 8 slices: each further partial plane costs its consumer more L2 reads than
+    // the extra CTAs save (decode step at M = 256).
+    while (ntiles * (S + 1) <= ctx->num_sms && p.Kc / (S + 1) >= 3 && S < kMaxSlices) ++S;
     p.kper = (p.Kc + S - 1) / S;
     S = (p.Kc + p.kper - 1) / p.kper;  // no empty slice
     p.ksplit = S;

@@ -48,19 +48,41 @@ struct Planes {
     long long stride;
     int count, ld;
 };
+// The planes are summed in slice order (a = p0; a += p1; ...), the order of the
+// splitk_sum pass; the loads of up to 8 slices are issued before their adds, so a
+// thread waits for one L2 round trip per 8 slices instead of one per slice.
+constexpr int kPlaneBatch = 8;
 __device__ __forceinline__ float ld_planes(const Planes& P, size_t off) {
-    float a = P.base[off];
-    for (int s = 1; s < P.count; ++s) a += P.base[(size_t)s * P.stride + off];
+    const float* p = P.base + off;
+    float a = __ldg(p);
+    for (int s0 = 1; s0 < P.count; s0 += kPlaneBatch) {
+        float b[kPlaneBatch];
+#pragma unroll
+        for (int j = 0; j < kPlaneBatch; ++j) b[j] = s0 + j < P.count ? __ldg(p + (size_t)(s0 + j) * P.stride) : 0.f;
+#pragma unroll
+        for (int j = 0; j < kPlaneBatch; ++j)
+            if (s0 + j < P.count) a += b[j];
+    }
     return a;
 }
 __device__ __forceinline__ float4 ld4_planes(const Planes& P, size_t off) {
-    float4 a = *reinterpret_cast<const float4*>(P.base + off);
-    for (int s = 1; s < P.count; ++s) {
-        const float4 b = *reinterpret_cast<const float4*>(P.base + (size_t)s * P.stride + off);
-        a.x += b.x;
-        a.y += b.y;
-        a.z += b.z;
-        a.w += b.w;
+    const float* p = P.base + off;
+    float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    for (int s0 = 1; s0 < P.count; s0 += kPlaneBatch) {
+        float4 b[kPlaneBatch];
+#pragma unroll
+        for (int j = 0; j < kPlaneBatch; ++j)
+            b[j] = s0 + j < P.count ? __ldg(reinterpret_cast<const float4*>(p + (size_t)(s0 + j) * P.stride))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < kPlaneBatch; ++j) {
+            if (s0 + j < P.count) {
+                a.x += b[j].x;
+                a.y += b[j].y;
+                a.z += b[j].z;
+                a.w += b[j].w;
+            }
+        }
     }
     return a;
 }
@@ -156,8 +178,32 @@ __global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __re
 // NORM_ROPE_SHADER for the q heads and the k head of one row, RMS_SHADER (no scale)
 // for v; q goes to q_out (bf16 [rows, H, hd]); k and v are written straight into the
 // bf16 caches at the row's absolute position (KVCache.append, gemma4-webgpu.js:128-135).
-// One CTA per (row, head slot); slot < H: q head, H: k, H + 1: v.  Thread i owns
-// elements i and i + hd/2 (a rotation pair).
+// Slot < H: q head, H: k, H + 1: v.
+
+// Destination row of (row r, slot) and the output pair (i, i + hd/2) of one rotation
+// pair a0 = y[i], a1 = y[i + hd/2] once the head's 1/rms is known.
+__device__ __forceinline__ uint16_t* qkv_dst(int slot, int H, int hd, int r, const G4Rows& R, int pos,
+                                             uint16_t* q_out, uint16_t* kcache, uint16_t* vcache, int cache_cap) {
+    if (slot < H) return q_out + ((size_t)r * H + slot) * hd;
+    return (slot == H ? kcache : vcache) + ((size_t)row_seq(R, r) * cache_cap + pos) * hd;
+}
+__device__ __forceinline__ float2 qkv_pair(int slot, int H, int hd, int i, float a0, float a1, float inv,
+                                           const float* __restrict__ qnorm, const float* __restrict__ knorm,
+                                           int rope_angles, float rope_base, int pos) {
+    if (slot == H + 1) return make_float2(a0 * inv, a1 * inv);  // v: RMS without scale (official-w4a16-layer0.js:176-182)
+    const float* sc = slot < H ? qnorm : knorm;
+    const float x0 = a0 * inv * sc[i], x1 = a1 * inv * sc[i + (hd >> 1)];
+    float sn = 0.f, cs = 1.f;
+    if (i < rope_angles) {
+        const float theta = (float)pos / powf(rope_base, 2.f * (float)i / (float)hd);
+        sn = sinf(theta);
+        cs = cosf(theta);
+    }
+    return make_float2(x0 * cs - x1 * sn, x1 * cs + x0 * sn);
+}
+
+// Any hd % 64 == 0: one CTA per (row, head slot), thread i owns the rotation pair
+// (i, i + hd/2).
 __global__ void qkv_post_kernel(Planes y, int H, int hd, int has_kv,
                                 const float* __restrict__ qnorm, const float* __restrict__ knorm, float eps,
                                 int rope_angles, float rope_base, G4Rows R, uint16_t* __restrict__ q_out,
@@ -172,25 +218,83 @@ __global__ void qkv_post_kernel(Planes y, int H, int hd, int has_kv,
     const float a0 = ld_planes(y, src + i), a1 = ld_planes(y, src + i + half);
     const float inv = rsqrtf(block_sum(a0 * a0 + a1 * a1, red) / (float)hd + eps);
     const int pos = row_position(R, r);
-    if (slot == H + 1) {  // v: RMS without scale (official-w4a16-layer0.js:176-182)
-        uint16_t* dst = vcache + ((size_t)row_seq(R, r) * cache_cap + pos) * hd;
-        dst[i] = (uint16_t)f32_to_bf16_bits(a0 * inv);
-        dst[i + half] = (uint16_t)f32_to_bf16_bits(a1 * inv);
-        return;
+    const float2 o = qkv_pair(slot, H, hd, i, a0, a1, inv, qnorm, knorm, rope_angles, rope_base, pos);
+    uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kcache, vcache, cache_cap);
+    dst[i] = (uint16_t)f32_to_bf16_bits(o.x);
+    dst[i + half] = (uint16_t)f32_to_bf16_bits(o.y);
+}
+
+// hd = 256 * NF: one warp per (row, head slot), 8 per CTA, so a decode batch is a few
+// hundred CTAs that are all resident at once (the attention behind it launches early).
+// Lane l owns the float4 groups 4 (l + 32 f) .. + 3 of both halves of the head row, i.e.
+// 4 NF rotation pairs.  The planes are summed in slice order with the loads of a batch
+// of slices for all the lane's groups in flight together.
+constexpr int kQkvWarps = 8;
+template <int NF>
+__global__ void __launch_bounds__(kQkvWarps * 32)
+qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restrict__ qnorm,
+                     const float* __restrict__ knorm, float eps, int rope_angles, float rope_base, G4Rows R,
+                     uint16_t* __restrict__ q_out, uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache,
+                     int cache_cap) {
+    constexpr int hd = 256 * NF, half = hd / 2, G = 2 * NF;  // float4 groups per lane
+    constexpr int PB = NF <= 2 ? 4 : 2;                        // slices per load batch
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int slots = H + (has_kv ? 2 : 0);
+    const int unit = blockIdx.x * kQkvWarps + (threadIdx.x >> 5);
+    if (unit >= rows * slots) return;
+    const int r = unit / slots, slot = unit - r * slots;
+    const float* src = y.base + (size_t)r * y.ld + (size_t)slot * hd;
+    auto goff = [&](int g) { return (g < NF ? 0 : half) + 4 * (lane + 32 * (g % NF)); };
+    float4 a[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) a[g] = __ldg(reinterpret_cast<const float4*>(src + goff(g)));
+    for (int s0 = 1; s0 < y.count; s0 += PB) {
+        float4 b[PB][G];
+#pragma unroll
+        for (int k = 0; k < PB; ++k)
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                b[k][g] = s0 + k < y.count
+                              ? __ldg(reinterpret_cast<const float4*>(src + (size_t)(s0 + k) * y.stride + goff(g)))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < PB; ++k) {
+            if (s0 + k < y.count) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    a[g].x += b[k][g].x;
+                    a[g].y += b[k][g].y;
+                    a[g].z += b[k][g].z;
+                    a[g].w += b[k][g].w;
+                }
+            }
+        }
     }
-    const float* sc = slot < H ? qnorm : knorm;
-    const float x0 = a0 * inv * sc[i], x1 = a1 * inv * sc[i + half];
-    float sn = 0.f, cs = 1.f;
-    if (i < rope_angles) {
-        const float theta = (float)pos / powf(rope_base, 2.f * (float)i / (float)hd);
-        sn = sinf(theta);
-        cs = cosf(theta);
+    float ss = 0.f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) ss += a[g].x * a[g].x + a[g].y * a[g].y + a[g].z * a[g].z + a[g].w * a[g].w;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float inv = rsqrtf(ss / (float)hd + eps);
+    const int pos = row_position(R, r);
+    uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kcache, vcache, cache_cap);
+#pragma unroll
+    for (int f = 0; f < NF; ++f) {
+        const int i0 = 4 * (lane + 32 * f);
+        const float lo[4] = {a[f].x, a[f].y, a[f].z, a[f].w}, hi[4] = {a[NF + f].x, a[NF + f].y, a[NF + f].z, a[NF + f].w};
+        float o0[4], o1[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const float2 o = qkv_pair(slot, H, hd, i0 + c, lo[c], hi[c], inv, qnorm, knorm, rope_angles, rope_base, pos);
+            o0[c] = o.x;
+            o1[c] = o.y;
+        }
+        *reinterpret_cast<uint2*>(dst + i0) = make_uint2(pack_bf16x2_bits(o0[0], o0[1]), pack_bf16x2_bits(o0[2], o0[3]));
+        *reinterpret_cast<uint2*>(dst + i0 + half) =
+            make_uint2(pack_bf16x2_bits(o1[0], o1[1]), pack_bf16x2_bits(o1[2], o1[3]));
     }
-    const float o0 = x0 * cs - x1 * sn, o1 = x1 * cs + x0 * sn;
-    uint16_t* dst = slot < H ? q_out + ((size_t)r * H + slot) * hd
-                             : kcache + ((size_t)row_seq(R, r) * cache_cap + pos) * hd;
-    dst[i] = (uint16_t)f32_to_bf16_bits(o0);
-    dst[i + half] = (uint16_t)f32_to_bf16_bits(o1);
 }
 
 // GELU_MUL over a fused [gate | up] projection: out = bf16(gelu(gate) * up), four
@@ -380,10 +484,25 @@ g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd,
         return g4::set_error(G4_ERR_INVALID, "g4_qkv_post: bad arguments");
     if (hd % 64 != 0 || hd > 1024) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_qkv_post: hd %d", hd);
     if (rows == 0) return G4_OK;
+    const Planes P = planes_of(y);
+    // the warp kernel reads float4 groups and writes 4 bf16 at a time
+    const bool f4 = y->ld % 4 == 0 && (y->count == 1 || y->stride % 4 == 0) &&
+                    (reinterpret_cast<uintptr_t>(y->base) & 15) == 0 && (reinterpret_cast<uintptr_t>(q_out_bf16) & 7) == 0 &&
+                    (!has_kv || ((reinterpret_cast<uintptr_t>(kcache_bf16) | reinterpret_cast<uintptr_t>(vcache_bf16)) & 7) == 0);
+    const long long units = (long long)rows * (heads + (has_kv ? 2 : 0));
+    const dim3 wgrid((unsigned)((units + kQkvWarps - 1) / kQkvWarps)), wblock(kQkvWarps * 32);
+    uint16_t* qo = static_cast<uint16_t*>(q_out_bf16);
+    uint16_t* kc = static_cast<uint16_t*>(kcache_bf16);
+    uint16_t* vc = static_cast<uint16_t*>(vcache_bf16);
+    if (f4 && hd == 256)
+        return g4::launch(ctx, "qkv_post_warp_kernel", qkv_post_warp_kernel<1>, wgrid, wblock, 0, 1, P, heads, has_kv,
+                          rows, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kc, vc, cache_cap);
+    if (f4 && hd == 512)
+        return g4::launch(ctx, "qkv_post_warp_kernel", qkv_post_warp_kernel<2>, wgrid, wblock, 0, 1, P, heads, has_kv,
+                          rows, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kc, vc, cache_cap);
     return g4::launch(ctx, "qkv_post_kernel", qkv_post_kernel, dim3(heads + (has_kv ? 2 : 0), rows), dim3(hd / 2), 0,
-                      1, planes_of(y), heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map,
-                      static_cast<uint16_t*>(q_out_bf16), static_cast<uint16_t*>(kcache_bf16),
-                      static_cast<uint16_t*>(vcache_bf16), cache_cap);
+                      1, P, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kc, vc,
+                      cache_cap);
 }
 
 g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,

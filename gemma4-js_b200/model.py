@@ -270,6 +270,7 @@ class Gemma4Model:
         self.seq_pos = torch.zeros(max_batch, dtype=torch.int32, device=dev)
         self._alloc(self.max_rows)
         self.graph = None
+        self._capturing = False
 
     # ------------------------------------------------------------ buffers ---
     def _alloc(self, R):
@@ -387,7 +388,10 @@ class Gemma4Model:
         if ids_dev is not None:
             self.buf["next"][:B].copy_(ids_dev[:B])
         self.buf["ids"][:B].copy_(self.buf["next"][:B])
-        rmap = G4Rows(self.seq_pos.data_ptr(), 0, 1, 0)
+        # Inside a captured graph the positions and the cached history come from earlier
+        # launches of the graph, so the attention may stream them before its wait.
+        flags = _lib.G4_ROWS_HISTORY_READY if self._capturing else 0
+        rmap = G4Rows(self.seq_pos.data_ptr(), 0, 1, 0, flags)
         self._forward(self.buf["ids"], B, rmap, B, 0)
         call("g4_advance_positions", self.ctx.handle, _ptr(self.seq_pos), 0, B, 1)
         return self.buf["next"][:B]
@@ -407,8 +411,12 @@ class Gemma4Model:
         n0 = launch_count()
         with torch.cuda.stream(stream):
             self.ctx.set_stream(stream)
-            with torch.cuda.graph(g, stream=stream):
-                self.decode_step(batch=B)
+            self._capturing = True
+            try:
+                with torch.cuda.graph(g, stream=stream):
+                    self.decode_step(batch=B)
+            finally:
+                self._capturing = False
         self.ctx.set_stream(old)
         self.graph_kernels = launch_count() - n0   # libg4w4 kernels per replayed step
         self.graph, self.graph_stream, self.graph_batch = g, stream, B

@@ -205,7 +205,7 @@ class KVCache:
         call("g4_kv_reset", self.handle)
 
     def tensors(self) -> tuple[torch.Tensor, torch.Tensor]:
-        """Views of the bf16 K and V storage [max_seq, head_dim] (for tests)."""
+        """Copies of the bf16 K and V storage [max_seq, head_dim] (for tests)."""
         kp, vp = C.c_void_p(), C.c_void_p()
         call("g4_kv_buffers", self.handle, C.byref(kp), C.byref(vp))
         n = self.max_seq * self.head_dim

@@ -53,12 +53,20 @@ typedef struct g4_dense g4_dense;
  * seq_pos is a device array (one entry per sequence), so a captured decode step
  * stays valid as g4_advance_positions moves the sequences forward.
  * Prefill of one sequence s: {seq_pos, s, T, 0}; batched decode: {seq_pos, 0, 1, 0};
- * the reference's host-side position (startPos): {NULL, 0, rows, startPos}. */
+ * the reference's host-side position (startPos): {NULL, 0, rows, startPos}.
+ * flags: G4_ROWS_HISTORY_READY (used by g4_attention_rows under programmatic dependent
+ * launch) promises that seq_pos and every cache row below each row's first position
+ * were written before the current CUDA graph launch, or before the last host
+ * synchronisation of the stream: no kernel that may still be running writes them.
+ * The attention kernel then streams that history while its predecessors drain and
+ * waits for them only before q and the rows of the current positions. */
+#define G4_ROWS_HISTORY_READY 1
 typedef struct {
     const int32_t* seq_pos;
     int seq_base;
     int rows_per_seq;
     int pos0;
+    int flags;
 } g4_rows;
 
 /* ---------------------------------------------------------------- context --

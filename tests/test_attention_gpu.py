@@ -83,3 +83,35 @@ def test_attention_argument_errors(rt, ctx, ops, g4):
         ops.attention(q, cache, 1, 8, 256, 8, 8, False, 512)
     with pytest.raises(g4.G4Error, match="heads"):
         ops.attention(torch.zeros(1, 16, 256, device="cuda", dtype=torch.bfloat16), cache, 1, 16, 256, 8, 7, False, 512)
+
+
+@pytest.mark.parametrize("nseq,sliding", [(40, True), (40, False), (160, True), (160, False), (300, True)])
+def test_attention_rows_batched(rt, ctx, oracle, nseq, sliding):
+    """g4_attention_rows: one decode row for each of nseq independent sequences at their own
+    device-side positions in one cache object (sequence s at rows s * stride).  Above the
+    SM count the two-CTAs-per-SM tiles run; below it the keys are split over CTAs."""
+    import ctypes as C
+    from importlib import import_module
+    L = import_module("gemma4-js_b200._lib")
+    hd, heads, stride, window = 256, 8, 1100, 512
+    rng = np.random.default_rng(nseq * 7 + int(sliding))
+    cache = rt.KVCache(ctx, hd, nseq * stride)
+    k = bf16_round((rng.standard_normal((nseq * stride, hd)) * 0.3).astype(np.float32))
+    v = bf16_round(rng.standard_normal((nseq * stride, hd)).astype(np.float32))
+    cache.append(torch.from_numpy(k).to(torch.bfloat16).cuda(), torch.from_numpy(v).to(torch.bfloat16).cuda(),
+                 nseq * stride, 0)
+    pos = rng.integers(0, stride, nseq).astype(np.int32)
+    pos[:3] = [0, stride - 1, window]
+    q = bf16_round((rng.standard_normal((nseq, heads, hd)) * 0.25).astype(np.float32))
+    qd = torch.from_numpy(q).to(torch.bfloat16).cuda()
+    posd = torch.from_numpy(pos).cuda()
+    out = torch.empty_like(qd)
+    rmap = L.G4Rows(posd.data_ptr(), 0, 1, 0)
+    L.call("g4_attention_rows", ctx.handle, C.c_void_p(qd.data_ptr()), cache.handle, nseq, heads, hd, C.byref(rmap),
+           stride, int(sliding), window, C.c_void_p(out.data_ptr()))
+    ctx.check_device()
+    got = out.float().cpu().numpy()
+    for s in range(nseq):
+        p, r0 = int(pos[s]), s * stride
+        ref = oracle.attention(q[s:s + 1], k[r0:r0 + p + 1], v[r0:r0 + p + 1], p, sliding, window)
+        assert max_rel(got[s:s + 1], ref) < TOL, s

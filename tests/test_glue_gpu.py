@@ -194,6 +194,42 @@ def test_planes_consumers_match_the_summed_linear(rt, ctx, M, K, N):
     ctx.check_device()
 
 
+@pytest.mark.parametrize("hd", [256, 512])
+def test_qkv_post_planes_match_the_summed_linear(rt, ctx, hd):
+    """g4_qkv_post_planes over the split-K planes of the qkv linear gives the bits of
+    g4_qkv_post over the linear's summed output (the planes are added in slice order)."""
+    H, M, K, cap = 8, 40, 1536, 64
+    N = (H + 2) * hd
+    gen = torch.Generator(device="cuda").manual_seed(hd)
+    packed = torch.randint(-2**31, 2**31 - 1, (N, K // 8), device="cuda", dtype=torch.int32, generator=gen)
+    sc = torch.randn((N, K // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+    lin = rt.W4Linear(ctx, packed, sc)
+    x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    L.call("g4_linear_w4a16", ctx.handle, lin.handle, P(x), M, P(y), 0)
+    qn = torch.rand(hd, device="cuda", generator=gen) + 0.5
+    kn = torch.rand(hd, device="cuda", generator=gen) + 0.5
+    seq_pos = torch.tensor([7], dtype=torch.int32, device="cuda")
+    rmap = L.G4Rows(seq_pos.data_ptr(), 0, M, 0)
+    outs = []
+    for planes in (False, True):
+        q = torch.empty((M, H, hd), dtype=torch.bfloat16, device="cuda")
+        kc = torch.zeros((cap, hd), dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros((cap, hd), dtype=torch.bfloat16, device="cuda")
+        args = (H, hd, 1, P(qn), P(kn), C.c_float(1e-6), hd // 4, C.c_float(1e6), C.byref(rmap), M, P(q), P(kc), P(vc), cap)
+        if planes:
+            pl = L.G4Planes()
+            L.call("g4_linear_w4a16_planes", ctx.handle, lin.handle, P(x), M, C.byref(pl))
+            assert pl.count > 1
+            L.call("g4_qkv_post_planes", ctx.handle, C.byref(pl), *args)
+        else:
+            L.call("g4_qkv_post", ctx.handle, P(y), N, *args)
+        outs.append((q, kc, vc))
+    ctx.check_device()
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
+
+
 @pytest.mark.parametrize("M", [1, 17, 40, 300])
 @pytest.mark.parametrize("cap", [30.0, 0.0])
 def test_dense_argmax_fused_matches_two_pass(rt, ctx, M, cap):

@@ -82,6 +82,35 @@ def test_graph_replay_matches_eager(rt, ctx):
     assert int(b.seq_pos[0].item()) == len(prompt) + 20
 
 
+def test_graph_replay_with_pdl_matches_eager(rt, ctx):
+    """A batched decode step captured with programmatic dependent launch on (every
+    kernel overlaps its predecessor; the attention streams the cached history before its
+    wait, G4_ROWS_HISTORY_READY) gives the tokens of the plain eager step."""
+    cfg = small_cfg(window=100)  # sliding windows and global ranges of several 64-key tiles
+    w = model.random_weights(cfg, seed=16, **W_KW)
+    rng = np.random.default_rng(16)
+    prompts = [list(rng.integers(0, cfg.vocab, n)) for n in (150, 70, 5)]
+    B = len(prompts)
+    ctx_pdl = rt.Context(0)
+    ctx_pdl.set_pdl(True)
+    a = model.Gemma4Model(ctx, cfg, w, max_batch=B, max_seq=256, max_rows=160)
+    b = model.Gemma4Model(ctx_pdl, cfg, w, max_batch=B, max_seq=256, max_rows=160)
+    fa = [a.prefill(s, pr) for s, pr in enumerate(prompts)]
+    fb = [b.prefill(s, pr) for s, pr in enumerate(prompts)]
+    assert fa == fb
+    a.buf["next"][:B] = torch.tensor(fa, dtype=torch.int32, device="cuda")
+    b.buf["next"][:B] = torch.tensor(fb, dtype=torch.int32, device="cuda")
+    ta, tb = [], []
+    for _ in range(24):
+        ta.append(a.decode_step(batch=B).tolist())
+    b.capture_decode(batch=B)
+    for _ in range(24):
+        tb.append(b.replay_decode().tolist())
+    torch.cuda.synchronize()
+    ctx_pdl.check_device()
+    assert ta == tb
+
+
 def test_batched_decode_matches_single_sequences(rt, ctx):
     cfg = small_cfg()
     w = model.random_weights(cfg, seed=13, **W_KW)

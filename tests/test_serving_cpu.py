@@ -2,6 +2,7 @@
 world-size-2 gloo group, and failure detection when a rank dies (no GPU involved)."""
 import importlib
 import os
+import queue
 import socket
 import time
 
@@ -35,6 +36,15 @@ def _free_port():
     return p
 
 
+def _put_and_exit(q, msg):
+    """Leaves without the process group's shutdown, after the queue's feeder thread has
+    handed msg to the pipe (os._exit would otherwise drop it)."""
+    q.put(msg)
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
 def _worker(rank, world, port, mode, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
     try:
@@ -53,15 +63,14 @@ def _worker(rank, world, port, mode, q):
             local = torch.arange(start, start + count, dtype=torch.int32)
             g.gather(local)
             if rank == 1:
-                q.put((rank, "left", None))
-                os._exit(0)
+                _put_and_exit(q, (rank, "left", None))
             t0 = time.time()
             try:
                 g.gather(local)
-                q.put((rank, "no-error", time.time() - t0))
-            except Exception as e:  # the process group reports the dead peer
-                q.put((rank, "error", time.time() - t0))
-            os._exit(0)
+                msg = (rank, "no-error", time.time() - t0)
+            except Exception:  # the process group reports the dead peer
+                msg = (rank, "error", time.time() - t0)
+            _put_and_exit(q, msg)
     except Exception as e:
         q.put((rank, "exception", repr(e)))
 
@@ -79,9 +88,11 @@ def _run(mode, world=2, wait=60):
         if p.is_alive():
             p.kill()
     out = []
-    while not q.empty():
-        out.append(q.get())
-    return out
+    while True:
+        try:
+            out.append(q.get(timeout=2.0))
+        except queue.Empty:
+            return out
 
 
 def test_token_gather_two_ranks():
