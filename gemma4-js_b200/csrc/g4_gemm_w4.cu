@@ -477,6 +477,11 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
     p.Kc = L.Kc;
     p.NS = L.NS;
     p.TT = M >= TTmax ? TTmax : (M + 31) / 32 * 32;
+    // A decode-size batch (128 < M <= 256) of a linear with few weight tiles: two 128-token
+    // tiles instead of one 256-token tile double the CTAs without adding split-K planes and
+    // halve each CTA's X load and output store, which is what such a GEMM waits on.
+    // (Where the doubled tiles would not fit in one wave, the 256-token tile is faster.)
+    if (M > 128 && M <= TTmax && (long long)L.NS * 2 <= ctx->num_sms) p.TT = 128;
     p.MT = (M + p.TT - 1) / p.TT;
     p.err = ctx->d_err;
     const long long ntiles = (long long)p.NS * p.MT;
