@@ -240,7 +240,11 @@ head_argmax_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
             tc_fence_after();
             const uint32_t tq = tmem + ab * HN + ((uint32_t)(32 * q) << 16) + 128 * e;
             const int n0 = nt * HN + 128 * e;
-            float bv = -INFINITY;
+            // A thread meets its columns in increasing index order and the softcap is
+            // non-decreasing, so a logit no larger than the largest raw logit seen so far
+            // can neither exceed the pick nor win a tie against it (its index is higher):
+            // the softcap is evaluated only on a new raw maximum.
+            float bv = -INFINITY, rmax = -INFINITY;
             int bi = 0x7fffffff;
             for (int c = 0; c < 128; c += 32) {
                 uint32_t v[32];
@@ -255,8 +259,15 @@ head_argmax_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_consta
                 for (int jj = 0; jj < 32; ++jj) {
                     const int n = n0 + c + jj;
                     const float raw = __uint_as_float(v[jj]);
-                    const float val = p.cap > 0.f ? tanhf(raw / p.cap) * p.cap : raw;
-                    if (n < p.N && val == val) better(bv, bi, val, n);  // NaN skipped, as g4_softcap_argmax
+                    // NaN skipped, as g4_softcap_argmax; the first valid column always taken
+                    if (n < p.N && raw == raw && (raw > rmax || bi == 0x7fffffff)) {
+                        rmax = raw;
+                        const float val = p.cap > 0.f ? tanhf(raw / p.cap) * p.cap : raw;
+                        if (val > bv || bi == 0x7fffffff) {
+                            bv = val;
+                            bi = n;
+                        }
+                    }
                 }
             }
             const int m = mt * HM + 32 * q + lane;

@@ -231,7 +231,7 @@ def test_qkv_post_planes_match_the_summed_linear(rt, ctx, hd):
 
 
 @pytest.mark.parametrize("M", [1, 17, 40, 300])
-@pytest.mark.parametrize("cap", [30.0, 0.0])
+@pytest.mark.parametrize("cap", [30.0, 0.0, 0.05])  # 0.05: most logits saturate, ties everywhere
 def test_dense_argmax_fused_matches_two_pass(rt, ctx, M, cap):
     """g4_dense_argmax (logits tiles + softcap + greedy pick in one kernel) against
     g4_dense_matmul + g4_softcap_argmax: the same bits above 16 rows (the same tensor-core
