@@ -330,6 +330,9 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
     e2e_ms = time_e2e(torch, dist, e2e_step, max(3, min(K, 50)))
     e2e = {"value": round(GEMV_BYTES / (e2e_ms / 1e3) / 1e9 * dist.world, 2), "unit": "GB/s",
            "h2d_bytes_per_step": Kd * 2, "d2h_bytes_per_step": N * 2}
+    del lins
+    torch.cuda.empty_cache()
+    wide = gemv_wide(torch, rt, ctx, lib, peak)
     return {
         "metric": "W4A16 decode GEMV throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
         "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
@@ -341,7 +344,36 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
                      "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
                      "traffic": TRAFFIC["gemv_w4a16_kernel"], "bytes_per_launch": byts},
         "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3), "e2e": e2e,
+        "wide_gemv": wide,
     }
+
+
+def gemv_wide(torch, rt, ctx, lib, peak, N=262144, Kd=1536, reps=10):
+    """The same GEMV kernel where streaming dominates its fixed latency: one token
+    through a W4A16 linear of the tied-head shape (N = 262144, 226 MB of nibbles and
+    scales, larger than L2), back to back in a CUDA graph."""
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    packed = torch.randint(-2**31, 2**31 - 1, (N, Kd // 8), device="cuda", dtype=torch.int32, generator=gen)
+    sc = torch.randn((N, Kd // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+    lin = rt.W4Linear(ctx, packed, sc)
+    del packed, sc
+    x = torch.randn((1, Kd), device="cuda", generator=gen).to(torch.bfloat16)
+    y = torch.empty((1, N), dtype=torch.bfloat16, device="cuda")
+
+    def launch(i):
+        st = lib.g4_linear_w4a16_impl(ctx.handle, lin.handle, C.c_void_p(x.data_ptr()), 1, C.c_void_p(y.data_ptr()), 1, 1)
+        if st:
+            raise RuntimeError(lib.g4_last_error_string())
+
+    one = Dist()  # this GPU alone
+    ms = time_graph(torch, ctx, launch, reps, 3, one)
+    byts = N * Kd // 2 + N * Kd // 32 * 2 + Kd * 2 + N * 2
+    per = ms / 1e3 / reps
+    gbs = byts / per / 1e9
+    lin.close()
+    return {"N": N, "K": Kd, "M": 1, "bytes_per_call": byts, "us_per_call": round(per * 1e6, 2),
+            "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "note": "latency-free regime of gemv_w4a16_kernel; the headline line is the config-1 shape"}
 
 
 def run_attn(args, torch, rt, ctx, dist, peaks):

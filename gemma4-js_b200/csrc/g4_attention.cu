@@ -372,9 +372,12 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     const int ntiles = (lmax + C::KT - 1) / C::KT;
     int nsplit = (2 * ctx->num_sms + rows - 1) / rows;
     nsplit = min(nsplit, max(1, (ntiles + 1) / 2));
-    // Batched rows: split a row's keys only as far as needed to give every SM a CTA.  At
-    // rows >= SMs each CTA streams a whole key range (HBM-bound, no combine pass).
-    if (map) nsplit = max(1, min((ctx->num_sms + rows - 1) / rows, (ntiles + 1) / 2));
+    // Batched rows: split a row's keys only as far as needed to give every SM a CTA, and
+    // not at all from a third of the SM count up: there one CTA per row streams the whole
+    // key range (HBM-bound) and the combine pass, a link more in the decode chain, costs
+    // more than the idle SMs (measured at 64 and 128 rows; at 32 rows the split wins).
+    if (map)
+        nsplit = rows * 3 > ctx->num_sms ? 1 : max(1, min((ctx->num_sms + rows - 1) / rows, (ntiles + 1) / 2));
     nsplit = max(nsplit, 1);
     const int tiles_per_split = (ntiles + nsplit - 1) / nsplit;
     nsplit = (ntiles + tiles_per_split - 1) / tiles_per_split;

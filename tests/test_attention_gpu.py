@@ -85,11 +85,13 @@ def test_attention_argument_errors(rt, ctx, ops, g4):
         ops.attention(torch.zeros(1, 16, 256, device="cuda", dtype=torch.bfloat16), cache, 1, 16, 256, 8, 7, False, 512)
 
 
-@pytest.mark.parametrize("nseq,sliding", [(40, True), (40, False), (160, True), (160, False), (300, True)])
+@pytest.mark.parametrize("nseq,sliding", [(40, True), (40, False), (64, True), (64, False), (160, True), (160, False),
+                                          (300, True)])
 def test_attention_rows_batched(rt, ctx, oracle, nseq, sliding):
     """g4_attention_rows: one decode row for each of nseq independent sequences at their own
-    device-side positions in one cache object (sequence s at rows s * stride).  Above the
-    SM count the two-CTAs-per-SM tiles run; below it the keys are split over CTAs."""
+    device-side positions in one cache object (sequence s at rows s * stride).  40 rows:
+    keys split over CTAs + combine; 64: one CTA per row; above the SM count: two CTAs per
+    SM on the sliding layers."""
     import ctypes as C
     from importlib import import_module
     L = import_module("gemma4-js_b200._lib")

@@ -91,9 +91,10 @@ def test_graph_replay_with_pdl_matches_eager(rt, ctx):
     rng = np.random.default_rng(16)
     prompts = [list(rng.integers(0, cfg.vocab, n)) for n in (150, 70, 5)]
     B = len(prompts)
+    ctx_plain = rt.Context(0)  # no programmatic dependent launch: every kernel waits for the last
     ctx_pdl = rt.Context(0)
     ctx_pdl.set_pdl(True)
-    a = model.Gemma4Model(ctx, cfg, w, max_batch=B, max_seq=256, max_rows=160)
+    a = model.Gemma4Model(ctx_plain, cfg, w, max_batch=B, max_seq=256, max_rows=160, pdl=False)
     b = model.Gemma4Model(ctx_pdl, cfg, w, max_batch=B, max_seq=256, max_rows=160)
     fa = [a.prefill(s, pr) for s, pr in enumerate(prompts)]
     fb = [b.prefill(s, pr) for s, pr in enumerate(prompts)]
@@ -108,6 +109,7 @@ def test_graph_replay_with_pdl_matches_eager(rt, ctx):
         tb.append(b.replay_decode().tolist())
     torch.cuda.synchronize()
     ctx_pdl.check_device()
+    ctx_plain.check_device()
     assert ta == tb
 
 
