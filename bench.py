@@ -428,6 +428,124 @@ def run_attn(args, torch, rt, ctx, dist, peaks):
     }
 
 
+def run_attn_rows(args, torch, rt, ctx, dist, peaks):
+    """Batched decode attention as in the config 5 step: one query row for each of
+    --batch sequences at position 4096 (device-side positions), global (4097 keys) or,
+    with --sliding, the 512-key window of a sliding layer."""
+    lib = importlib.import_module("gemma4-js_b200._lib")
+    K, W = args.steps, args.warmup
+    B, hd, pos = args.batch, 256, 4096
+    stride = pos + 8
+    sliding = bool(args.sliding)
+    ctx.set_pdl(True)
+    cache = rt.KVCache(ctx, hd, B * stride)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    for s in range(B):  # K ~ N(0, 0.3^2), V ~ N(0, 1): the scale of normed keys and values
+        k = (torch.randn((stride, hd), device="cuda", generator=gen) * 0.3).to(torch.bfloat16)
+        v = torch.randn((stride, hd), device="cuda", generator=gen).to(torch.bfloat16)
+        cache.append(k, v, stride, s * stride)
+    seq_pos = torch.full((B,), pos, dtype=torch.int32, device="cuda")
+    q = (torch.randn((B, 8, hd), device="cuda", generator=gen) * 0.3).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    rmap = lib.G4Rows(seq_pos.data_ptr(), 0, 1, 0, lib.G4_ROWS_HISTORY_READY)
+
+    def launch(i):
+        lib.call("g4_attention_rows", ctx.handle, C.c_void_p(q.data_ptr()), cache.handle, B, 8, hd, C.byref(rmap),
+                 stride, int(sliding), 512, C.c_void_p(out.data_ptr()))
+
+    n0 = rt.launch_count()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    ms = time_graph(torch, ctx, launch, K, W, dist)
+    clocks = clk.stop()
+    launches = rt.launch_count() - n0 - W
+    ctx.check_device()
+    keys = 512 if sliding else pos + 1
+    byts = B * keys * hd * 2 * 2 + 2 * B * 8 * hd * 2
+    per = ms / 1e3 / K
+    gbs = byts / per / 1e9
+    peak = peaks["hbm_gbs"]
+    hq = q.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+
+    def e2e_step(i):
+        q.copy_(hq, non_blocking=True)
+        launch(i)
+        ho.copy_(out, non_blocking=True)
+
+    e2e_ms = time_e2e(torch, dist, e2e_step, max(3, min(K, 50)))
+    return {
+        "metric": "batched decode attention throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
+        "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "decode_attention_rows_" + ("sliding" if sliding else "global"), "batch": B,
+                   "keys": keys, "hd": hd, "heads": 8,
+                   "l2": f"{byts / 2**20:.0f} MB of K/V per launch" + (" (> L2)" if byts > 126e6 else " (L2-resident)")},
+        "roofline": {"bound": "hbm", "kernel": "attn_decode_kernel", "achieved": round(gbs, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"], "traffic": None,
+                     "bytes_per_launch": byts},
+        "e2e": {"value": round(byts / (e2e_ms / 1e3) / 1e9 * dist.world, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": B * 8 * hd * 2, "d2h_bytes_per_step": B * 8 * hd * 2},
+        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3),
+    }
+
+
+def run_head(args, torch, rt, ctx, dist, peaks):
+    """The fused LM head of the config 5 step: logits of --batch rows against the tied
+    bf16 table [262144, 1536] on tcgen05, softcap 30 and the greedy pick in the epilogue
+    (g4_dense_argmax)."""
+    lib = importlib.import_module("gemma4-js_b200._lib")
+    model = importlib.import_module("gemma4-js_b200.model")
+    K, W = args.steps, args.warmup
+    M, V, Kd = args.batch, 262144, 1536
+    ctx.set_pdl(True)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    E = (torch.randn((V, Kd), device="cuda", generator=gen) * 0.05).to(torch.bfloat16)
+    head = model.Dense(ctx, E)
+    del E
+    x = torch.randn((M, Kd), device="cuda", generator=gen).to(torch.bfloat16)
+    ids = torch.empty(M, dtype=torch.int32, device="cuda")
+    vals = torch.empty(M, dtype=torch.float32, device="cuda")
+
+    def launch(i):
+        lib.call("g4_dense_argmax", ctx.handle, head.handle, C.c_void_p(x.data_ptr()), M, C.c_float(30.0),
+                 C.c_void_p(ids.data_ptr()), C.c_void_p(vals.data_ptr()))
+
+    n0 = rt.launch_count()
+    clk = ClockSampler(dist.local)
+    clk.start()
+    ms = time_graph(torch, ctx, launch, K, W, dist)
+    clocks = clk.stop()
+    launches = rt.launch_count() - n0 - W
+    ctx.check_device()
+    per = ms / 1e3 / K
+    flops = 2.0 * M * V * Kd
+    tf = flops / per / 1e12
+    hx = x.cpu().pin_memory()
+    hid = torch.empty(M, dtype=torch.int32).pin_memory()
+
+    def e2e_step(i):
+        x.copy_(hx, non_blocking=True)
+        launch(i)
+        hid.copy_(ids, non_blocking=True)
+
+    e2e_ms = time_e2e(torch, dist, e2e_step, max(3, min(K, 50)))
+    return {
+        "metric": "fused LM head (logits + softcap + greedy pick) TFLOP/s", "value": round(tf * dist.world, 1),
+        "unit": "TFLOP/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": {"workload": "lm_head_argmax", "M": M, "vocab": V, "K": Kd,
+                   "l2": "805 MB bf16 table per launch (> L2)",
+                   "hbm_gbs": round(V * Kd * 2 / per / 1e9, 1)},
+        "roofline": {"bound": "tensor", "kernel": "head_argmax_kernel", "achieved": round(tf, 1),
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
+                     "peak_source": peaks["source"], "traffic": None, "flops_per_launch": flops},
+        "e2e": {"value": round(flops / (e2e_ms / 1e3) / 1e12 * dist.world, 1), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": M * Kd * 2, "d2h_bytes_per_step": M * 4},
+        "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3),
+    }
+
+
 def run_gemm(args, torch, rt, ctx, dist, peaks):
     """M in {16,128,512,2048} x (K,N) in {(1536,6144), (6144,1536), (1536,262144)}."""
     lib = importlib.import_module("gemma4-js_b200._lib").load()
@@ -842,6 +960,45 @@ def run_reference(args, dist):
         return _reference_line(args, dist, "W4A16 prefill GEMM throughput (config 3 sweep)", v, "TFLOP/s",
                                dt / K * 1e3, {"workload": "config3_gemm", "sample": f"M={M} K={Kd} N={N}"}, "f32",
                                f"{K} calls at M={M}, (K, N) = ({Kd}, {N}), one point of the config 3 sweep", threads)
+    if args.workload == "attn_rows":
+        # a step: the attention of a bounded sample of the batch's sequences (the same
+        # per-sequence work as the GPU launch), reported as algorithmic GB/s
+        hd, pos, n = 256, 4096, 4
+        keys = 512 if args.sliding else pos + 1
+        kc = rng.standard_normal((pos + 1, hd)).astype(np.float32)
+        vc = rng.standard_normal((pos + 1, hd)).astype(np.float32)
+        q = rng.standard_normal((1, 8, hd)).astype(np.float32)
+        for _ in range(W):
+            oracle.attention(q, kc, vc, pos, bool(args.sliding), 512)
+        t0 = time.perf_counter()
+        for _ in range(K * n):
+            oracle.attention(q, kc, vc, pos, bool(args.sliding), 512)
+        dt = time.perf_counter() - t0
+        byts = keys * hd * 2 * 2 + 2 * 8 * hd * 2
+        v = round(byts * K * n / dt / 1e9, 4)
+        return _reference_line(args, dist, "batched decode attention throughput (algorithmic bytes)", v, "GB/s",
+                               dt / K * 1e3, {"workload": "decode_attention_rows_" + ("sliding" if args.sliding
+                                                                                      else "global"),
+                                              "batch": args.batch, "keys": keys, "hd": hd, "heads": 8}, "f32",
+                               f"{n} of the {args.batch} sequences per step, one thread", 1)
+    if args.workload == "head":
+        # a step: logits + softcap + greedy pick of one row against a bounded vocabulary
+        # sample (the f32 tied head of the CPU decode), reported as TFLOP/s
+        Kd, vs = 1536, 16384
+        E = (rng.standard_normal((vs, Kd)) * 0.05).astype(np.float32)
+        x = rng.standard_normal((1, Kd)).astype(np.float32)
+        for _ in range(W):
+            np.argmax(np.tanh((x @ E.T) / 30.0) * 30.0)
+        t0 = time.perf_counter()
+        for _ in range(K):
+            np.argmax(np.tanh((x @ E.T) / 30.0) * 30.0)
+        dt = time.perf_counter() - t0
+        v = round(2.0 * vs * Kd * K / dt / 1e12, 6)
+        return _reference_line(args, dist, "fused LM head (logits + softcap + greedy pick) TFLOP/s", v, "TFLOP/s",
+                               dt / K * 1e3, {"workload": "lm_head_argmax", "M": args.batch, "vocab": 262144,
+                                              "K": Kd}, "f32",
+                               f"{K} rows against a {vs}-row sample of the table (numpy, host BLAS threads)",
+                               threads)
     if args.workload == "attn":
         keylen, hd = 4096, 256
         kc = rng.standard_normal((keylen, hd)).astype(np.float32)
@@ -887,7 +1044,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="serve", choices=["ple", "gemv", "attn", "gemm", "decode", "serve"])
+    ap.add_argument("--workload", default="serve",
+                    choices=["ple", "gemv", "attn", "attn_rows", "head", "gemm", "decode", "serve"])
+    ap.add_argument("--batch", type=int, default=256, help="attn_rows / head: rows (sequences)")
+    ap.add_argument("--sliding", action="store_true", help="attn_rows: the 512-key window of a sliding layer")
     ap.add_argument("--impl", default="g4", choices=["g4", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--vocab", type=int, default=262144, help="ple: table rows (smaller for ncu captures)")
@@ -910,8 +1070,8 @@ def main():
     rt = importlib.import_module("gemma4-js_b200.runtime")
     ctx = rt.Context(dist.local)
     peaks = load_peaks()
-    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn, "gemm": run_gemm, "decode": run_decode,
-          "serve": run_serve}[args.workload]
+    fn = {"ple": run_ple, "gemv": run_gemv, "attn": run_attn, "attn_rows": run_attn_rows, "head": run_head,
+          "gemm": run_gemm, "decode": run_decode, "serve": run_serve}[args.workload]
     line = fn(args, torch, rt, ctx, dist, peaks)
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
