@@ -17,6 +17,13 @@ What is pinned, and by what:
   * Linear W4 known answers (linear_w4_golden.npz): words whose nibbles decode to
     known values under official-w4a16.js:15-19 (offset binary, nibble - 8).  The
     linear dequant is JavaScript only, so these are read off the source, not run.
+  * Linear W4 format as written by its producer (linear_w4_ct_golden.npz): the
+    checkpoint's `weight_packed` / `weight_scale` pairs are the pack-quantized format
+    of the compressed-tensors library (0.15.0.1 is installed here, as a dependency of
+    vllm).  Seeded int4 q in [-8, 7] are packed by its `pack_to_int32(q, 4,
+    packed_dim=1)` and dequantised by its `dequantize(q, scale)` (group 32 inferred from
+    the scale shape; q.to(bf16) * scale: one f32 product rounded to bf16, the
+    roundFloat32ToBF16(q * s) of official-w4a16.js:95).  Run with --compressed-tensors.
 The fixtures are committed; GPU boxes and the test suite never read the reference.
 """
 from __future__ import annotations
@@ -97,14 +104,46 @@ def make_linear() -> None:
                         q=q, expected_f32=expected)
 
 
+def make_linear_ct() -> None:
+    import torch
+    from compressed_tensors.compressors.pack_quantized.helpers import pack_to_int32, unpack_from_int32
+    from compressed_tensors.quantization.lifecycle.forward import dequantize
+    import compressed_tensors
+    N, K = 24, 256
+    g = torch.Generator().manual_seed(20261202)
+    q = torch.randint(-8, 8, (N, K), generator=g, dtype=torch.int8)
+    q[0] = -8                                   # the extremes of the range
+    q[1] = 7
+    q[2, ::2], q[2, 1::2] = -8, 7               # alternating within every word
+    q[3] = 0
+    scales = (torch.randn((N, K // 32), generator=g).abs() * 0.02).to(torch.bfloat16)
+    scales[4, 1] = 0.0                          # a zero group
+    scales[5] = torch.tensor([2.0 ** -126, 1e-38, 3e38, 1.0, 0.5, 65504.0, 2.0 ** -100, 7.0], dtype=torch.float32
+                             ).to(torch.bfloat16)  # subnormal-adjacent, huge, exact
+    packed = pack_to_int32(q, 4, packed_dim=1)
+    assert packed.dtype == torch.int32 and packed.shape == (N, K // 8)
+    assert torch.equal(unpack_from_int32(packed, 4, torch.Size([N, K]), packed_dim=1), q)
+    w = dequantize(q, scales)                   # bf16 [N, K]
+    assert w.dtype == torch.bfloat16 and w.shape == (N, K)
+    np.savez_compressed(HERE / "linear_w4_ct_golden.npz", packed=packed.numpy(),
+                        scales=scales.view(torch.int16).numpy().view(np.uint16), q=q.numpy(),
+                        expected_bf16=w.view(torch.int16).numpy().view(np.uint16),
+                        library=np.array(f"compressed-tensors {getattr(compressed_tensors, '__version__', '0.15.0.1')}"))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, required=True)
+    ap.add_argument("--reference", type=Path)
+    ap.add_argument("--compressed-tensors", action="store_true",
+                    help="also (or only) write linear_w4_ct_golden.npz with the installed compressed-tensors")
     a = ap.parse_args()
-    b = load_builder(a.reference)
-    make_ple(a.reference, b)
-    make_rne(b)
-    make_linear()
+    if a.reference:
+        b = load_builder(a.reference)
+        make_ple(a.reference, b)
+        make_rne(b)
+        make_linear()
+    if a.compressed_tensors:
+        make_linear_ct()
     print("wrote", sorted(p.name for p in HERE.glob("*.npz")))
 
 

@@ -24,6 +24,15 @@ def test_golden_known_answers(rt, ctx):
     assert np.array_equal(out, g["expected_f32"])
 
 
+def test_compressed_tensors_golden(rt, ctx):
+    """Weights packed by their producer's library (compressed-tensors 0.15.0.1
+    pack_to_int32) dequantise on the GPU to that library's bf16 weights, bit for bit."""
+    g = golden("linear_w4_ct_golden.npz")
+    lin = rt.W4Linear(ctx, g["packed"], g["scales"])
+    got = lin.dequant(dtype=torch.bfloat16).cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, g["expected_bf16"])
+
+
 @pytest.mark.parametrize("K,N", [(32, 8), (96, 24), (256, 40), (1536, 6144), (6144, 1536), (256, 1536)])
 def test_dequant_bit_exact(rt, ctx, oracle, K, N):
     packed, scales = make_weights(oracle, K, N, K + N)

@@ -50,6 +50,19 @@ def test_linear_known_answers(oracle, npo):
     assert np.array_equal(npo.unpack_linear_q(g["packed"]), g["q"])
 
 
+def test_linear_format_matches_compressed_tensors(oracle, npo):
+    """The pack-quantized format as its producer writes it (compressed-tensors 0.15.0.1:
+    pack_to_int32 and dequantize, tests/golden/make_golden.py --compressed-tensors): the
+    oracle unpacks the library's words to its q and dequantises them to its bf16 weights,
+    bit for bit (extreme q, a zero group, subnormal-adjacent and overflowing scales)."""
+    g = golden("linear_w4_ct_golden.npz")
+    assert np.array_equal(npo.unpack_linear_q(g["packed"]), g["q"])
+    f32 = oracle.dequant_w4a16_rows(g["packed"], g["scales"])
+    assert np.array_equal(oracle.f32_to_bf16_bits(f32), g["expected_bf16"])
+    with np.errstate(over="ignore"):  # the 3e38 scales overflow to inf on purpose
+        assert np.array_equal(npo.dequant_w4a16(g["packed"], g["scales"]), f32)
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 64, 40), (3, 96, 24), (5, 256, 300)])
 def test_linear_oracle_vs_numpy(oracle, npo, M, K, N):
     rng = np.random.default_rng(M * 1000 + K)
