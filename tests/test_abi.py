@@ -49,3 +49,30 @@ def test_context_creation_fails_cleanly_without_gpu(g4):
 def importlib_lib():
     import importlib
     return importlib.import_module("gemma4-js_b200._lib")
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors of g4_rows and g4_planes have the C header's size and field
+    offsets (compiled by the host C compiler from include/g4w4.h)."""
+    from pathlib import Path
+    L = importlib_lib()
+    inc = Path(L.HEADER).parent
+    src = tmp_path / "layout.c"
+    src.write_text(
+        '#include <stddef.h>\n#include <stdio.h>\n#include "g4w4.h"\n'
+        "int main(void) {\n"
+        '  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(g4_rows), offsetof(g4_rows, seq_base),\n'
+        "         offsetof(g4_rows, rows_per_seq), offsetof(g4_rows, pos0), offsetof(g4_rows, flags), 0ul);\n"
+        '  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(g4_planes), offsetof(g4_planes, base),\n'
+        "         offsetof(g4_planes, count), offsetof(g4_planes, stride), offsetof(g4_planes, ld), 0ul);\n"
+        '  printf("%d\\n", G4_ROWS_HISTORY_READY);\n'
+        "  return 0;\n}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", str(inc), str(src), "-o", str(exe)], check=True)
+    lines = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    rows = [int(v) for v in lines[0].split()]
+    planes = [int(v) for v in lines[1].split()]
+    R, P = L.G4Rows, L.G4Planes
+    assert rows[:5] == [C.sizeof(R), R.seq_base.offset, R.rows_per_seq.offset, R.pos0.offset, R.flags.offset]
+    assert planes[:5] == [C.sizeof(P), P.base.offset, P.count.offset, P.stride.offset, P.ld.offset]
+    assert int(lines[2]) == L.G4_ROWS_HISTORY_READY
