@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the g4w4 hot path on B200 (one JSON line on rank 0).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload serve|decode|ple|gemv|attn|gemm]
-                  [--impl g4|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W]
+                  [--workload serve|decode|ple|gemv|attn|attn_rows|head|gemm] [--impl g4|reference]
 
 Workloads (inputs are seeded synthetic data with the configs'
 shapes and value distributions -- the reference publishes no dataset):
@@ -16,6 +16,12 @@ shapes and value distributions -- the reference publishes no dataset):
   gemv  config 1: W4A16 decode GEMV, x [1,1536], W [6144,1536]; a step is one call,
         rotating over 64 weight copies (340 MB > L2).
   attn  decode attention, 8 q heads / 1 KV head, hd 256, one sequence at keylen 4096.
+  attn_rows  the serving step's batched decode attention: --batch sequences (256) at
+        position 4096, a global layer or (--sliding) a 512-key window.
+  head  the serving step's fused LM head: --batch rows (256) against the tied bf16
+        table [262144, 1536], softcap 30 and the greedy pick in the epilogue.
+  gemm  config 3: the W4A16 GEMM sweep, M in {16,128,512,2048} x (K,N) in
+        {(1536,6144), (6144,1536), (1536,262144)}.
 Timing: W warm-up steps, then K steps captured in one CUDA graph and timed with
 CUDA events on the launching stream between barriers; max over ranks.
 --impl reference times the CPU restatement of the reference's TFJS path (the
