@@ -200,3 +200,34 @@ def test_full_size_teacher_forced_32(full_size):
     toks, ties, margins = greedy_compare(gpu, orc, [5, 6, 7, 8], 32, forced=forced)
     print("picks", toks, "distinct", len(set(toks)), "near ties", ties, "min margin", round(min(margins), 4))
     assert len(toks) == 33 and len(ties) <= 1
+
+
+def test_model_from_distribution_files(rt, ctx, tmp_path):
+    """checkpoint.load_model: a checkpoint in the reference's tensor naming and a PLE shard
+    set on disk build the model that the same weights build in memory (norms and layer
+    scalars as the checkpoint's bf16): the same greedy tokens."""
+    from test_checkpoint_cpu import _bf16, _f32, write_checkpoint, write_ple_shards
+    ckpt = importlib.import_module("gemma4-js_b200.checkpoint")
+    cfg = model.ModelConfig.reference_spec().small(hidden=512, layers=7, vocab=4096, intermediate=1024,
+                                                   intermediate_late=2048, first_shared=5, window=16)
+    w = model.random_weights(cfg, seed=21, **W_KW)
+    write_checkpoint(tmp_path / "core.safetensors", cfg, w)
+    manifest = write_ple_shards(tmp_path, w["ple_packed"], w["ple_scales"], rows_per_shard=1000)
+    for lw in w["layers"]:  # what the checkpoint holds
+        for key in ("n_in", "n_pa", "n_pf", "n_pff", "n_pple", "qn", "kn"):
+            lw[key] = _f32(_bf16(lw[key]))
+        lw["skip"] = float(_f32(_bf16(np.array([lw["skip"]], np.float32)))[0])
+    for key in ("ple_norm", "final_norm"):
+        w[key] = _f32(_bf16(w[key]))
+    for i, lw in enumerate(w["layers"]):
+        if cfg.spec(i)["shared"]:
+            lw["kn"] = np.ones_like(lw["kn"])
+    a = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+    b = ckpt.load_model(ctx, cfg, tmp_path / "core.safetensors", manifest, max_batch=1, max_seq=64, max_rows=16)
+    prompt = [5, 17, 4000, 9, 123]
+    ta, tb = [a.prefill(0, prompt)], [b.prefill(0, prompt)]
+    for _ in range(12):
+        ta.append(int(a.decode_step(ids_dev=torch.tensor([ta[-1]], dtype=torch.int32, device="cuda"), batch=1)[0]))
+        tb.append(int(b.decode_step(ids_dev=torch.tensor([tb[-1]], dtype=torch.int32, device="cuda"), batch=1)[0]))
+    ctx.check_device()
+    assert ta == tb
