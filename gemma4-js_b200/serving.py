@@ -8,11 +8,13 @@ CUDA graph.  The only exchange is the gather of the step's token ids to every ra
 
 The reference has no multi-GPU code; this is the partitioning of the serving config.
 A rank that dies or never joins surfaces as an error on the others when the process
-group's timeout ends their next collective, never as a hang.
+group's timeout ends their next collective, never as a hang; with a `StepHeartbeat`
+the others learn of it on the host, between steps, before they launch anything more.
 """
 from __future__ import annotations
 
 import datetime
+import time
 
 import torch
 
@@ -62,3 +64,41 @@ class TokenGather:
             self.out[off:off + c].copy_(self.bufs[r][:c])
             off += c
         return self.out
+
+
+class RankFailure(RuntimeError):
+    """A peer rank stopped stepping (it died, hung or left the job)."""
+
+
+class StepHeartbeat:
+    """Host-side liveness between decode steps over a c10d key-value store (the process
+    group's TCPStore, or any `torch.distributed.Store`).  Each rank calls `enter(step)`
+    before launching a step: it announces the step and returns once every peer has
+    announced it too, or raises RankFailure naming the ranks that did not within
+    `timeout_s` -- so a rank that left between steps is reported before the others
+    enqueue a kernel or a collective that would wait for it."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 2.0, prefix: str = "g4hb"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}/{r}"
+
+    def _announced(self, r: int) -> int:
+        if not self.store.check([self._key(r)]):
+            return -1
+        return int(self.store.get(self._key(r)).decode())
+
+    def enter(self, step: int) -> None:
+        self.store.set(self._key(self.rank), str(step))
+        deadline = time.monotonic() + self.timeout_s
+        behind = [r for r in range(self.world) if r != self.rank]
+        while True:
+            behind = [r for r in behind if self._announced(r) < step]
+            if not behind:
+                return
+            if time.monotonic() > deadline:
+                raise RankFailure(f"rank {self.rank}: rank(s) {behind} did not reach step {step} "
+                                  f"within {self.timeout_s:.1f} s")
+            time.sleep(0.002)

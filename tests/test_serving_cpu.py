@@ -59,6 +59,20 @@ def _worker(rank, world, port, mode, q):
                 q.put((rank, step, out.tolist()))
             dist.barrier()
             dist.destroy_process_group()
+        elif mode == "heartbeat":  # rank 1 leaves after step 1; rank 0 learns it on the host
+            from torch.distributed import distributed_c10d as c10d
+            hb = serving.StepHeartbeat(c10d._get_default_store(), rank, world, timeout_s=1.5)
+            local = torch.arange(start, start + count, dtype=torch.int32)
+            for step in range(3):
+                t0 = time.time()
+                try:
+                    hb.enter(step)
+                except serving.RankFailure as e:
+                    _put_and_exit(q, (rank, "failure", step, time.time() - t0, str(e)))
+                g.gather(local)
+                if rank == 1 and step == 1:
+                    _put_and_exit(q, (rank, "left", step, 0.0, ""))
+            _put_and_exit(q, (rank, "no-failure", 3, 0.0, ""))
         else:  # rank 1 leaves between steps; rank 0 must get an error, not hang
             local = torch.arange(start, start + count, dtype=torch.int32)
             g.gather(local)
@@ -109,3 +123,13 @@ def test_dead_rank_surfaces_as_an_error():
     r0 = [x for x in res if x[0] == 0]
     assert r0 and r0[0][1] == "error", res
     assert r0[0][2] < 30.0  # bounded by the process-group timeout, not a hang
+
+
+def test_heartbeat_reports_a_rank_that_left_between_steps():
+    """Rank 1 leaves after step 1: rank 0's entry into step 2 names it within the
+    heartbeat limit (1.5 s), on the host, before any collective of step 2 is enqueued."""
+    res = _run("heartbeat")
+    r0 = [x for x in res if x[0] == 0]
+    assert r0 and r0[0][1] == "failure" and r0[0][2] == 2, res
+    assert r0[0][3] < 10.0 and "[1]" in r0[0][4]
+    assert any(x[0] == 1 and x[1] == "left" for x in res)
