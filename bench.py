@@ -339,6 +339,7 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
     del lins
     torch.cuda.empty_cache()
     wide = gemv_wide(torch, rt, ctx, lib, peak)
+    sweep = gemv_sweep(torch, rt, ctx, lib, peak, steps=max(K, 20))
     return {
         "metric": "W4A16 decode GEMV throughput (algorithmic bytes)", "value": round(gbs * dist.world, 2),
         "unit": "GB/s", "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 5),
@@ -350,8 +351,43 @@ def run_gemv(args, torch, rt, ctx, dist, peaks):
                      "unit": "GB/s", "frac": round(gbs / peak, 4), "peak_source": peaks["source"],
                      "traffic": TRAFFIC["gemv_w4a16_kernel"], "bytes_per_launch": byts},
         "gpu_launches": launches, "clocks": clocks, "us_per_call": round(per * 1e6, 3), "e2e": e2e,
-        "wide_gemv": wide,
+        "wide_gemv": wide, "decode_shape_sweep": sweep,
     }
+
+
+GEMV_SWEEP = [(1536, 2048), (1536, 4096), (1536, 256), (1536, 512), (1536, 8960), (2048, 1536), (4096, 1536),
+              (1536, 12288), (12288, 1536), (256, 1536)]
+
+
+def gemv_sweep(torch, rt, ctx, lib, peak, steps=20):
+    """The same GEMV at the model's decode shapes (K, N), M = 1, back to back in a CUDA
+    graph over enough weight copies that each rotation exceeds L2 (>= 256 MB)."""
+    out = []
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    for Kd, N in GEMV_SWEEP:
+        byts = N * Kd // 2 + N * Kd // 32 * 2 + Kd * 2 + N * 2
+        copies = max(2, -(-(256 << 20) // byts))
+        packed = torch.randint(-2**31, 2**31 - 1, (N, Kd // 8), device="cuda", dtype=torch.int32, generator=gen)
+        sc = torch.randn((N, Kd // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+        lins = [rt.W4Linear(ctx, packed, sc) for _ in range(copies)]  # the same bits, distinct buffers
+        x = torch.randn((1, Kd), device="cuda", generator=gen).to(torch.bfloat16)
+        y = torch.empty((1, N), dtype=torch.bfloat16, device="cuda")
+
+        def launch(i, lins=lins, x=x, y=y):
+            st = lib.g4_linear_w4a16_impl(ctx.handle, lins[i % len(lins)].handle, C.c_void_p(x.data_ptr()), 1,
+                                          C.c_void_p(y.data_ptr()), 1, 1)
+            if st:
+                raise RuntimeError(lib.g4_last_error_string())
+
+        ms = time_graph(torch, ctx, launch, steps, 3, Dist())
+        per = ms / 1e3 / steps
+        out.append({"K": Kd, "N": N, "us_per_call": round(per * 1e6, 2), "achieved_gbs": round(byts / per / 1e9, 1),
+                    "frac": round(byts / per / 1e9 / peak, 4)})
+        for L in lins:
+            L.close()
+        del lins, packed, sc
+        torch.cuda.empty_cache()
+    return out
 
 
 def gemv_wide(torch, rt, ctx, lib, peak, N=262144, Kd=1536, reps=10):

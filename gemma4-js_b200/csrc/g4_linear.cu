@@ -319,9 +319,11 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
                                            gemv_smem_bytes(kGemvPass, 16)));
         attr_set.fetch_or(1ull << ctx->device);
     }
-    // Split K over a cluster until there are ~2 CTAs per SM, keeping >= 4 blocks per CTA.
+    // Split K over a cluster until there are ~2 CTAs per SM, but only while each CTA keeps
+    // >= 24 blocks (1536 columns): a decode GEMV is latency-bound, and the cluster's
+    // DSMEM reduction costs more than a short K slice saves (measured at K <= 2048).
     int S = 1;
-    while (S < 8 && ((L.NT * S < 2 * ctx->num_sms && (L.Kc + 2 * S - 1) / (2 * S) >= 4) ||
+    while (S < 8 && ((L.NT * S < 2 * ctx->num_sms && (L.Kc + 2 * S - 1) / (2 * S) >= 24) ||
                      (L.Kc + S - 1) / S > kGemvPass))
         S *= 2;
     const int cps = (L.Kc + S - 1) / S;
