@@ -4,7 +4,7 @@
   python bench.py [--gpus N] [--steps K] [--warmup W]
                   [--workload serve|decode|ple|gemv|attn|attn_rows|head|gemm] [--impl g4|reference]
 
-Workloads (inputs are seeded synthetic data with the configs'
+Workloads (the benchmark configurations; inputs are seeded synthetic data with the configs'
 shapes and value distributions -- the reference publishes no dataset):
   serve (default) config 5: 256 sequences with 4096-token contexts split over the GPUs
         as independent replicas, one greedy decode step of all of them per step (one
@@ -589,7 +589,7 @@ def run_head(args, torch, rt, ctx, dist, peaks):
 
 
 def run_gemm(args, torch, rt, ctx, dist, peaks):
-    """M in {16,128,512,2048} x (K,N) in {(1536,6144), (6144,1536), (1536,262144)}."""
+    """benchmark config 3: M in {16,128,512,2048} x (K,N) in {(1536,6144), (6144,1536), (1536,262144)}."""
     lib = importlib.import_module("gemma4-js_b200._lib").load()
     K_steps, W = args.steps, args.warmup
     ctx.set_pdl(True)  # back-to-back launches overlap as they do inside a decode step
@@ -718,7 +718,7 @@ def _attn_roofline(torch, ctx, m, B, peaks, reps=20):
 
 
 def run_serve(args, torch, rt, ctx, dist, peaks):
-    """256 sequences with 4096-token contexts, greedy decode; the batch
+    """benchmark config 5: 256 sequences with 4096-token contexts, greedy decode; the batch
     is split across the GPUs as independent replicas; token ids all-gathered with NCCL."""
     K, W = args.steps, args.warmup
     B_total, ctx_len = 256, 4096
@@ -799,7 +799,7 @@ def _graph_kernel_count(m):
 
 
 def run_decode(args, torch, rt, ctx, dist, peaks):
-    """batch 1, 2048-token random prompt, then greedy decode."""
+    """benchmark config 4: batch 1, 2048-token random prompt, then greedy decode."""
     K, W = args.steps, args.warmup
     prompt_len = 2048
     cfg, m = _decode_model(torch, rt, ctx, 1, prompt_len + W + K + 8, prompt_len)

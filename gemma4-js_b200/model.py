@@ -13,7 +13,7 @@ structural changes for B200:
     decode step is one CUDA graph with no host round trip.
 
 A batch of independent sequences decodes together: row b of a decode step is
-sequence b.  `ModelConfig()` is the BASELINE configuration (35 layers, hidden 1536,
+sequence b.  `ModelConfig()` is the benchmark configuration (35 layers, hidden 1536,
 MLP 6144, 8 q heads / 1 KV head, head_dim 256, window 512 on 4 of 5 layers, PLE 256
 per layer, vocab 262144, tied bf16 head); `ModelConfig.reference_spec()` is the
 checkpoint's own spec (head_dim 512 and rope 1e6 / 0.25 on global layers, MLP 12288
@@ -138,7 +138,7 @@ def random_weights(cfg: ModelConfig, seed: int = 0, sigma: float = 0.02, embed_s
         emb *= np.exp(np.float32(embed_tail) * rng.standard_normal((cfg.vocab, 1), dtype=np.float32))
     w["embed"] = _bf16_bits(emb)
     del emb
-    # PLE: two's complement nibbles in [-7, 7], bf16 scales |N(0, 0.05)|
+    # PLE: two's complement nibbles in [-7, 7], bf16 scales |N(0, 0.05)| (benchmark config 2)
     q = rng.integers(-7, 8, size=(cfg.vocab, L * P), dtype=np.int8)
     nib = (q & 0xF).astype(np.uint8)
     w["ple_packed"] = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)

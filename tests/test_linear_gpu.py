@@ -84,7 +84,7 @@ def test_gemv_f32_output(rt, ctx, ops, oracle):
 
 
 def test_config1_gemv(rt, ctx, ops, oracle):
-    """x [1,1536] ~ N(0,1) bf16, W int4 uniform, scales |N(0,0.02)|, N=6144, seed 0."""
+    """benchmark config 1: x [1,1536] ~ N(0,1) bf16, W int4 uniform, scales |N(0,0.02)|, N=6144, seed 0."""
     y, ref = _run(rt, ctx, ops, oracle, 1536, 6144, 1, impl=1, seed=0)
     assert max_rel(y, ref) < TOL
     # the dot products use exact int4 x bf16 products: error comes from f32 sums only
@@ -140,7 +140,7 @@ def test_tcgen05_gemm_vs_torch_fp32_on_bf16_weights(rt, ctx, ops, oracle, M, K, 
 
 
 def test_tcgen05_gemm_config3_shapes(rt, ctx, ops, oracle):
-    """BASELINE config 3 shapes at M = 128 (the full sweep runs in bench.py)."""
+    """benchmark config 3 shapes at M = 128 (the full sweep runs in bench.py)."""
     for K, N in [(1536, 6144), (6144, 1536)]:
         y, ref = _run(rt, ctx, ops, oracle, K, N, 128, impl=2, seed=99 + K)
         assert max_rel(y, ref) < TOL

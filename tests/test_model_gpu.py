@@ -179,7 +179,7 @@ def full_size(rt, ctx):
 
 
 def test_full_size_greedy_32(full_size):
-    """BASELINE config 4's model (35 layers, hidden 1536, MLP 6144, 8q/1kv, hd 256,
+    """benchmark config 4's model (35 layers, hidden 1536, MLP 6144, 8q/1kv, hd 256,
     window 512, PLE 256/layer, vocab 262144 tied), seeded random init: 32 greedy steps
     must give the oracle's token ids."""
     cfg, gpu, orc = full_size

@@ -94,7 +94,7 @@ def test_streamed_shard_upload(rt, ctx, oracle):
 
 
 def test_full_size_config2_properties(rt, ctx, oracle):
-    """BASELINE config 2 at full size: [262144, 8960] table, 4096 ids; sampled rows are
+    """benchmark config 2 at full size: [262144, 8960] table, 4096 ids; sampled rows are
     bit-exact against the oracle and every output row sums to its table row's value."""
     vocab, width, T = 262144, 8960, 4096
     gen = torch.Generator(device="cuda").manual_seed(0)
