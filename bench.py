@@ -889,7 +889,7 @@ def cpu_ple(sample_s: float, threads: int, vocab_sample: int = 8192):
         oracle.ple_read_rows(packed, scales, ids, bf16=True, nthreads=threads, L=L)
         n += 1
     dt = time.perf_counter() - t0
-    return {"value": round(PLE_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+    return {"value": round(PLE_BYTES * n / dt / 1e9, 4), "unit": "GB/s", "cores": threads, "kind": "port", "cpu": _cpu_model(),
             "sample": f"{n} x 4096-id gathers (bf16 out) over a {vocab_sample}-row host table, {dt:.1f} s",
             "calls_per_s": round(n / dt, 4)}
 
@@ -940,16 +940,29 @@ class CpuDecode:
 def cpu_decode(batch: int, ctx_len: int, threads: int = 1, model_layers: int = 35):
     """The cpu_baseline object: one decode step of CpuDecode on `threads` host threads."""
     dt = CpuDecode(ctx_len, threads, model_layers).step(batch)
-    return {"value": round(batch / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port",
+    return {"value": round(batch / dt, 5), "unit": "tok/s", "cores": threads, "kind": "port", "cpu": _cpu_model(),
             "sample": f"one decode step of {batch} sequence(s) at context {ctx_len}: {model_layers} layers x 6 W4A16 linears "
                       f"(dequantised per call) + attention + f32 tied head, {dt:.1f} s"}
+
+
+def _cpu_model() -> str:
+    """The host CPU's model name (first /proc/cpuinfo entry) and its logical core count."""
+    name = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                name = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    return f"{name} ({os.cpu_count()} logical cores)"
 
 
 def _reference_line(args, dist, metric, value, unit, ms, config, dtype, sample, threads, hib=True, scaling="weak"):
     return {"impl": "reference", "metric": metric, "value": value, "unit": unit, "n_gpus": dist.world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": hib,
             "scaling": scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)", "config": config,
-            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "port", "cpu": _cpu_model(), "sample": sample},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -1075,7 +1088,7 @@ def run_reference(args, dist):
             "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded int4 table, uniform ids)",
             "config": {"workload": "config2_ple_gather", "tokens_per_step_per_gpu": 4096},
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads, "kind": "port", "cpu": _cpu_model(),
                              "sample": f"{K} x 4096-id gathers over an {vs}-row host table (C restatement of "
                                        f"ple-w4-shard-reader.js:65-104; the JS reference has no runtime here)"},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
