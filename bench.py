@@ -289,7 +289,7 @@ def run_ple(args, torch, rt, ctx, dist, peaks):
                      "traffic": TRAFFIC["ple_gather_kernel"], "bytes_per_launch": PLE_BYTES},
         "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
     }
-    if dist.rank == 0 and dist.world == 1:
+    if dist.rank == 0 and dist.world == 1 and not getattr(args, "no_cpu", False):
         line["cpu_baseline"] = cpu_ple(sample_s=args.cpu_seconds, threads=1)
     return line
 
@@ -717,6 +717,112 @@ def _attn_roofline(torch, ctx, m, B, peaks, reps=20):
             "bytes_per_launch": byts, "us_per_launch": round(per * 1e6, 2)}
 
 
+SERVE_METRIC = "batched greedy decode throughput (config 5)"
+
+
+def serve_config(world: int) -> dict:
+    """The config object of the config-5 line, the same for both arms."""
+    return {"workload": "config5_serving", "model": "gemma4-e2b-shaped (35L, hidden 1536, MLP 6144, 8q/1kv, hd 256)",
+            "global_batch": 256, "batch_per_gpu": 256 // world, "seq_len": 4096, "new_tokens_per_step": 1,
+            "parallelism": f"replicas x{world}, NCCL all-gather of token ids",
+            "l2": "per step 1.5 GB of weights + KV of 256 x 4096 tokens (>> 126 MB L2)"}
+
+
+def _serve_step_bytes(m, B: int, pos: int) -> dict:
+    """Algorithmic HBM bytes of one decode step of B sequences at position `pos`: every
+    W4A16 weight once (nibbles + scales), the tied bf16 head once, the embedding and PLE
+    rows of the B tokens, each layer's K/V reads (window-limited on sliding layers) and
+    the new K/V rows."""
+    cfg = m.cfg
+    w4 = sum(L[n].in_dim * L[n].out_dim * 9 // 16 for L in m.layers for n in ("qkv", "o", "gu", "down", "pg", "pp"))
+    w4 += m.top.in_dim * m.top.out_dim * 9 // 16
+    head = cfg.vocab * cfg.hidden * 2
+    rows = B * (cfg.hidden * 2 + 5040)
+    kv = 0
+    for L in m.layers:
+        s = L["spec"]
+        keys = pos + 1 if s["full"] else min(pos + 1, cfg.window)
+        kv += B * keys * s["hd"] * 4
+        if not s["shared"]:
+            kv += B * s["hd"] * 4
+    return {"w4": w4, "head": head, "rows": rows, "kv": kv, "total": w4 + head + rows + kv}
+
+
+def _step_linears(m, B: int):
+    """(issue, flops, traffic) of every W4A16 linear of one decode step, in step order: per
+    layer q/k/v, o, gate/up + GeGLU, down, PLE gate, PLE projection; then the per-layer
+    model projection of the next step's inputs."""
+    lib = importlib.import_module("gemma4-js_b200._lib")
+    b, h = m.buf, m.ctx.handle
+    P = lambda t: C.c_void_p(t.data_ptr())  # noqa: E731
+    out = []
+    for L in m.layers:
+        for name, x in (("qkv", b["x"]), ("o", b["attn"]), ("gu", b["x"]), ("down", b["act"]), ("pg", b["x"]),
+                        ("pp", b["pa"])):
+            lin = L[name]
+            if name == "gu":
+                def issue(lin=lin, x=x):
+                    lib.call("g4_linear_w4a16_geglu", h, lin.handle, P(x), B, P(b["act"]))
+            else:
+                def issue(lin=lin, x=x):
+                    pl = lib.G4Planes()
+                    lib.call("g4_linear_w4a16_planes", h, lin.handle, P(x), B, C.byref(pl))
+            out.append((issue, 2.0 * B * lin.in_dim * lin.out_dim, gemm_traffic(B, lin.in_dim, lin.out_dim)))
+
+    def top():
+        lib.call("g4_linear_w4a16", h, m.top.handle, P(b["x"]), B, P(b["proj"]), 0)
+    out.append((top, 2.0 * B * m.top.in_dim * m.top.out_dim, gemm_traffic(B, m.top.in_dim, m.top.out_dim)))
+    return out
+
+
+def _gemm_family_roofline(torch, ctx, m, B, peaks, reps=10):
+    """The step's dominant kernel family by launch-list share: every W4A16 linear of one
+    decode step (gemm_w4_tmem_kernel, plain and GeGLU instances, at M = B), issued back to
+    back in step order with programmatic dependent launch, captured in a CUDA graph and
+    timed with CUDA events on its launching stream.  The row-wise operators and the
+    attention that sit between them inside the real step are left out, so this is the
+    linears' own rate, not their in-step latency."""
+    calls = _step_linears(m, B)
+    flops = sum(f for _, f, _ in calls)
+    traffic = sum(t for _, _, t in calls)
+    for fn, _, _ in calls:  # eager warm-up: sizes the workspace, sets kernel attributes
+        fn()
+    ctx.sync()
+    stream = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    old = ctx.stream
+    n0 = importlib.import_module("gemma4-js_b200.runtime").launch_count()
+    with torch.cuda.stream(stream):
+        ctx.set_stream(stream)
+        with torch.cuda.graph(g, stream=stream):
+            for fn, _, _ in calls:
+                fn()
+    ctx.set_stream(old)
+    launches = importlib.import_module("gemma4-js_b200.runtime").launch_count() - n0
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        s.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e.record(stream)
+    torch.cuda.synchronize()
+    per = s.elapsed_time(e) / 1e3 / reps
+    del g
+    tf = flops / per / 1e12
+    return {"bound": "tensor", "kernel": "gemm_w4_tmem_kernel: the step's W4A16 linears (6 per layer x 35 + the PLE "
+                                        "model projection), back to back",
+            "achieved": round(tf, 1), "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+            "frac": round(tf / peaks["bf16_tflops"], 4), "peak_source": peaks["source"],
+            "traffic": traffic,
+            "traffic_basis": "per launch packed weights + scales + X once (ncu DRAM bytes at M=2048 K=1536 N=6144 "
+                             "match this to 0.4%), summed over the step's linears",
+            "flops_per_step": flops, "launches_per_step": launches, "us_per_step": round(per * 1e6, 1),
+            "us_per_launch": round(per * 1e6 / max(launches, 1), 2)}
+
+
 def run_serve(args, torch, rt, ctx, dist, peaks):
     """benchmark config 5: 256 sequences with 4096-token contexts, greedy decode; the batch
     is split across the GPUs as independent replicas; token ids all-gathered with NCCL."""
@@ -773,24 +879,66 @@ def run_serve(args, torch, rt, ctx, dist, peaks):
     e2.record()
     torch.cuda.synchronize()
     e2e_ms = dist.max(s2.elapsed_time(e2)) / e2e_steps
-    roof = _attn_roofline(torch, ctx, m, B, peaks)
+    roof_attn = _attn_roofline(torch, ctx, m, B, peaks)
+    roof_gemm = _gemm_family_roofline(torch, ctx, m, B, peaks)
+    # per-GPU step: the slowest rank's step time and the algorithmic bytes of its batch
+    sb = _serve_step_bytes(m, B, ctx_len + W + K // 2)
+    step_s = ms / K / 1e3
     line = {
-        "metric": "batched greedy decode throughput (config 5)", "value": round(tok_s, 1), "unit": "tok/s",
+        "metric": SERVE_METRIC, "value": round(tok_s, 1), "unit": "tok/s",
         "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init W4A16 weights, random bf16 K/V for the 4096-token contexts, random ids)",
-        "config": {"workload": "config5_serving", "model": "gemma4-e2b-shaped (35L, hidden 1536, MLP 6144, 8q/1kv, hd 256)",
-                   "global_batch": B_total, "batch_per_gpu": B, "seq_len": ctx_len,
-                   "parallelism": f"replicas x{dist.world}, NCCL all-gather of token ids",
-                   "l2": "per step 1.5 GB of weights + KV of 256 x 4096 tokens (>> 126 MB L2)"},
-        "roofline": roof,
+        "config": serve_config(dist.world),
+        "roofline": roof_gemm,
+        "roofline_attention": roof_attn,
+        "step_frac": round(sb["total"] / step_s / 1e9 / peaks["hbm_gbs"], 4),
+        "per_gpu": {"batch": B, "step_ms": round(ms / K, 4), "tok_s": round(B / step_s, 1),
+                    "step_bytes": sb, "step_hbm_gbs": round(sb["total"] / step_s / 1e9, 1),
+                    "step_frac_basis": "algorithmic bytes per step (weights, head, rows, K/V) / ms_per_step / HBM peak"},
         "e2e": {"value": round(B_total / (e2e_ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
                 "d2h_bytes_per_step": B_total * 4},
-        "gpu_launches": _graph_kernel_count(m) * K, "clocks": clocks,
+        "gpu_launches": _graph_kernel_count(m) * K, "launches_per_step": _graph_kernel_count(m), "clocks": clocks,
     }
     if dist.rank == 0 and dist.world == 1:
         line["cpu_baseline"] = cpu_decode(batch=1, ctx_len=ctx_len)
+    m.close()
+    del m
+    torch.cuda.empty_cache()
+    if dist.world == 1 and not args.no_extras:
+        line.update(_extras(args, torch, rt, ctx, dist, peaks))
     return line
+
+
+def _extras(args, torch, rt, ctx, dist, peaks) -> dict:
+    """The other north_star numbers in the same run (one GPU): config 1 GEMV, config 3
+    GEMM sweep, config 2 PLE gather and config 4 batch-1 decode, each with its own value,
+    roofline fraction, clocks and step time."""
+    import copy
+
+    def sub(fn, **kw):
+        a = copy.copy(args)
+        a.no_cpu = True
+        for k, v in kw.items():
+            setattr(a, k, v)
+        try:
+            ln = fn(a, torch, rt, ctx, dist, peaks)
+        except Exception as ex:  # report, keep the headline line
+            return {"error": f"{type(ex).__name__}: {ex}"}
+        keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "roofline", "clocks", "e2e", "config",
+                "us_per_call", "gpu_launches")
+        out = {k: ln[k] for k in keep if k in ln}
+        for k in ("sweep", "decode_shape_sweep", "wide_gemv"):
+            if k in ln:
+                out[k] = ln[k]
+        torch.cuda.empty_cache()
+        return out
+
+    ctx.set_pdl(True)
+    return {"gemv": sub(run_gemv, steps=200, copies=0, no_pdl=False),
+            "gemm": sub(run_gemm, steps=20, gemm_shapes="", gemm_impl=0),
+            "ple": sub(run_ple, steps=50, vocab=262144),
+            "decode": sub(run_decode, steps=128)}
 
 
 def _graph_kernel_count(m):
@@ -858,7 +1006,7 @@ def run_decode(args, torch, rt, ctx, dist, peaks):
         "e2e": {"value": round(1 / (e2e_ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
         "gpu_launches": _graph_kernel_count(m) * K, "clocks": clocks,
     }
-    if dist.rank == 0 and dist.world == 1:
+    if dist.rank == 0 and dist.world == 1 and not getattr(args, "no_cpu", False):
         line["cpu_baseline"] = cpu_decode(batch=1, ctx_len=prompt_len)
     return line
 
@@ -937,6 +1085,85 @@ class CpuDecode:
         return dt
 
 
+class CpuServeStep:
+    """One greedy decode step of a whole batch on the host, as the reference's TFJS path
+    computes a batch: each linear's weight dequantised to f32 once per call
+    (official-quantized-linear.js:100-111, here all rows at once on the host threads) and
+    multiplied by the batch's activations with tf.matMul(x, W^T) (:113-117, a BLAS sgemm
+    here); attention per sequence over its own context, window 512 on 4 of 5 layers
+    (official-w4a16-layer0.js:30-62: Q.K^T, softmax, P.V as batched BLAS); the f32 tied
+    head over 262144 rows with the softcap and the greedy pick (gemma4-webgpu.js:413-480).
+    Every sequence has its own K/V rows; the 35 layers cycle over one set of per-shape
+    weights and one global-length K/V set, so host memory stays ~6 GB."""
+
+    SHAPES = CpuDecode.SHAPES
+
+    def __init__(self, batch: int, ctx_len: int, threads: int, layers: int = 35):
+        self.oracle, self.L = native_oracle()
+        self.batch, self.ctx_len, self.threads, self.layers = batch, ctx_len, threads, layers
+        rng = np.random.default_rng(0)
+        self.W, self.deq, self.x = {}, {}, {}
+        for k, (n, kk) in self.SHAPES.items():
+            self.W[k] = (rng.integers(0, 2**32, size=(n, kk // 8), dtype=np.uint64).astype(np.uint32).view(np.int32),
+                         self.oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.02, (n, kk // 32))).astype(np.float32)))
+            self.deq[k] = np.empty((n, kk), np.float32)
+            self.x[k] = rng.standard_normal((batch, kk), dtype=np.float32)
+        # large operands tiled from one seeded 16 MB block (values do not change the cost)
+        blk = rng.standard_normal(1 << 22, dtype=np.float32)
+        self.head = self._tiled(blk, (262144, 1536), 0.05)
+        keys = ctx_len + 1
+        self.kc = self._tiled(blk[::-1], (batch, keys, 256), 0.3)
+        self.vc = self._tiled(blk, (batch, keys, 256), 1.0)
+        self.q = rng.standard_normal((batch, 8, 256), dtype=np.float32)
+        from concurrent.futures import ThreadPoolExecutor
+        self.pool = ThreadPoolExecutor(max_workers=threads)
+
+    @staticmethod
+    def _tiled(blk, shape, scale):
+        n = int(np.prod(shape))
+        out = np.empty(n, np.float32)
+        for i in range(0, n, blk.size):
+            j = min(n, i + blk.size)
+            np.multiply(blk[:j - i], np.float32(scale), out=out[i:j])
+        return out.reshape(shape)
+
+    def _linear(self, k):
+        self.oracle.dequant_w4a16_par(*self.W[k], out=self.deq[k], nthreads=self.threads, L=self.L)
+        return self.x[k] @ self.deq[k].T
+
+    def _attention_seqs(self, lo, hi, keys):
+        out = np.empty((hi - lo, 8, 256), np.float32)
+        for b in range(lo, hi):
+            logits = self.q[b] @ self.kc[b, -keys:].T
+            logits -= logits.max(-1, keepdims=True)
+            p = np.exp(logits)
+            p /= p.sum(-1, keepdims=True)
+            out[b - lo] = p @ self.vc[b, -keys:]
+        return out
+
+    def _attention(self, keys):
+        """Sequences split over the host threads, one single-threaded BLAS call per product."""
+        from threadpoolctl import threadpool_limits
+        n, B = self.threads, self.batch
+        with threadpool_limits(1):
+            parts = list(self.pool.map(lambda t: self._attention_seqs(B * t // n, B * (t + 1) // n, keys), range(n)))
+        return np.concatenate(parts)
+
+    def step(self) -> float:
+        """Runs one decode step of the batch; returns its wall time in seconds."""
+        t0 = time.perf_counter()
+        self._linear("top")
+        for layer in range(self.layers):
+            full = (layer + 1) % 5 == 0
+            self._linear("qkv")
+            self._attention(self.ctx_len + 1 if full else min(self.ctx_len + 1, 512))
+            for k in ("o", "gu", "down", "pg", "pp"):
+                self._linear(k)
+        logits = self.x["top"][:, :1536] @ self.head.T
+        np.argmax(np.tanh(logits / np.float32(30.0)) * np.float32(30.0), axis=1)
+        return time.perf_counter() - t0
+
+
 def cpu_decode(batch: int, ctx_len: int, threads: int = 1, model_layers: int = 35):
     """The cpu_baseline object: one decode step of CpuDecode on `threads` host threads."""
     dt = CpuDecode(ctx_len, threads, model_layers).step(batch)
@@ -973,25 +1200,30 @@ def run_reference(args, dist):
     threads = os.cpu_count() or 1
     K, W = args.steps, args.warmup
     import numpy as np
-    if args.workload in ("serve", "decode"):
-        # a step: one greedy decode step of one sequence of the batch (all 35 layers, the
-        # full head); serve at context 4096, decode (config 4) at the 2048-token prompt
-        ctx_len = 4096 if args.workload == "serve" else 2048
-        m = CpuDecode(ctx_len, threads)
+    if args.workload == "serve":
+        # a step: one greedy decode step of the whole 256-sequence batch at context 4096,
+        # the GPU arm's config
+        m = CpuServeStep(256, 4096, threads)
+        for _ in range(W):
+            m.step()
+        dt = sum(m.step() for _ in range(K))
+        v = round(256 * K / dt, 4)
+        return _reference_line(args, dist, SERVE_METRIC, v, "tok/s", dt / K * 1e3, serve_config(dist.world), "f32",
+                               f"{K} decode steps of all 256 sequences at context 4096: 35 layers x 6 W4A16 linears "
+                               f"dequantised once per call and multiplied as one f32 GEMM over the batch, attention "
+                               f"per sequence, f32 tied head + softcap + argmax", threads,
+                               scaling="strong")
+    if args.workload == "decode":
+        # a step: one greedy decode step of one sequence at the 2048-token prompt
+        m = CpuDecode(2048, threads)
         for _ in range(W):
             m.step(1)
         dt = sum(m.step(1) for _ in range(K))
         v = round(K / dt, 5)
-        if args.workload == "serve":
-            metric, config = "batched greedy decode throughput (config 5)", {
-                "workload": "config5_serve", "global_batch": 256, "seq_len": 4096, "parallelism": f"replicas{dist.world}"}
-        else:
-            metric, config = "greedy decode throughput, batch 1 (config 4)", {
-                "workload": "config4_decode", "global_batch": 1, "seq_len": 2048, "parallelism": "replica"}
-        return _reference_line(args, dist, metric, v, "tok/s", dt / K * 1e3, config, "f32",
-                               f"{K} decode steps of 1 sequence at context {ctx_len} (35 layers x 6 W4A16 linears "
-                               f"dequantised per call, attention, f32 tied head)", threads,
-                               scaling="strong" if args.workload == "serve" else "weak")
+        config = {"workload": "config4_decode_b1", "prompt": 2048, "l2": "1.5 GB of weights per token (>> L2)"}
+        return _reference_line(args, dist, "greedy decode throughput, batch 1 (config 4)", v, "tok/s", dt / K * 1e3,
+                               config, "f32", f"{K} decode steps of 1 sequence at context 2048 (35 layers x 6 W4A16 "
+                                              f"linears dequantised per call, attention, f32 tied head)", threads)
     oracle, L = native_oracle()
     rng = np.random.default_rng(0)
     if args.workload in ("gemv", "gemm"):
@@ -1110,6 +1342,8 @@ def main():
     ap.add_argument("--gemm-shapes", default="", help='gemm: "M1,M2:KxN,KxN" instead of the config 3 sweep')
     ap.add_argument("--gemm-impl", type=int, default=0, help="gemm: 0 auto, 1 GEMV, 2 tcgen05")
     ap.add_argument("--no-pdl", action="store_true", help="gemv: launch without programmatic dependent launch")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="serve: skip the config 1-4 sub-measurements that the 1-GPU line carries")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -51,6 +51,8 @@ def lib(path: Path | None = None) -> C.CDLL:
     L.g4o_f32_to_bf16_bits.argtypes = [C.c_float]
     L.g4o_dequant_w4a16_rows.restype = I
     L.g4o_dequant_w4a16_rows.argtypes = [i32p, u16p, I, I, I, I, I, f32p]
+    L.g4o_dequant_w4a16_par.restype = I
+    L.g4o_dequant_w4a16_par.argtypes = [i32p, u16p, I, I, I, f32p, I]
     L.g4o_linear_w4a16.restype = I
     L.g4o_linear_w4a16.argtypes = [f32p, I, i32p, u16p, I, I, I, f32p, I]
     L.g4o_ple_read_rows.restype = I
@@ -81,6 +83,19 @@ def dequant_w4a16_rows(packed: np.ndarray, scales_bf16: np.ndarray, row_start: i
     _ok(lib().g4o_dequant_w4a16_rows(np.ascontiguousarray(packed, np.int32).reshape(-1),
                                      np.ascontiguousarray(scales_bf16, np.uint16).reshape(-1),
                                      N, K, row_start, rc, group, out.reshape(-1)), "dequant")
+    return out
+
+
+def dequant_w4a16_par(packed: np.ndarray, scales_bf16: np.ndarray, out: np.ndarray | None = None,
+                      group: int = 32, nthreads: int = 1, L: C.CDLL | None = None) -> np.ndarray:
+    """Every row of a W4A16 weight dequantised to f32 (official-w4a16.js:50-101) on
+    nthreads host threads; `out` ([N, K] f32) is reused when given."""
+    N, K = packed.shape[0], packed.shape[1] * 8
+    if out is None:
+        out = np.empty((N, K), np.float32)
+    _ok((L or lib()).g4o_dequant_w4a16_par(np.ascontiguousarray(packed, np.int32).reshape(-1),
+                                           np.ascontiguousarray(scales_bf16, np.uint16).reshape(-1), N, K, group,
+                                           out.reshape(-1), nthreads), "dequant_par")
     return out
 
 

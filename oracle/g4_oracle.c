@@ -65,6 +65,45 @@ int g4o_dequant_w4a16_rows(const int32_t* packed, const uint16_t* scales_bf16, i
 }
 
 typedef struct {
+    const int32_t* packed;
+    const uint16_t* scales;
+    int N, K, group, t, nt;
+    float* out;
+} dequant_job;
+
+static void* dequant_worker(void* arg) {
+    dequant_job* j = (dequant_job*)arg;
+    const int r0 = (int)((long long)j->N * j->t / j->nt), r1 = (int)((long long)j->N * (j->t + 1) / j->nt);
+    g4o_dequant_w4a16_rows(j->packed, j->scales, j->N, j->K, r0, r1 - r0, j->group, j->out + (size_t)r0 * j->K);
+    return NULL;
+}
+
+/* official-quantized-linear.js:100-111 for a whole weight: every row dequantised to f32 once,
+ * rows split over nthreads host threads (the same values as g4o_dequant_w4a16_rows). */
+int g4o_dequant_w4a16_par(const int32_t* packed, const uint16_t* scales_bf16, int N, int K, int group,
+                          float* out, int nthreads) {
+    if (K % 8 != 0 || group <= 0 || K % group != 0 || N < 0) return -1;
+    if (nthreads < 1) nthreads = 1;
+    if (nthreads > N) nthreads = N > 0 ? N : 1;
+    pthread_t* th = (pthread_t*)malloc(sizeof(pthread_t) * nthreads);
+    dequant_job* jobs = (dequant_job*)malloc(sizeof(dequant_job) * nthreads);
+    if (!th || !jobs) {
+        free(th);
+        free(jobs);
+        return -3;
+    }
+    for (int i = 0; i < nthreads; ++i) {
+        dequant_job j = {packed, scales_bf16, N, K, group, i, nthreads, out};
+        jobs[i] = j;
+        pthread_create(&th[i], NULL, dequant_worker, &jobs[i]);
+    }
+    for (int i = 0; i < nthreads; ++i) pthread_join(th[i], NULL);
+    free(th);
+    free(jobs);
+    return 0;
+}
+
+typedef struct {
     const float* x;
     int M, K, N, group;
     const int32_t* packed;

@@ -29,6 +29,9 @@ int g4o_dequant_w4a16_rows(const int32_t* packed, const uint16_t* scales_bf16, i
 /* OfficialW4A16Linear.apply (official-quantized-linear.js:82-128): dequantise 256 output
  * rows at a time, then y = x . W^T in f32.  x f32 [M,K], y f32 [M,N].
  * nthreads > 1 splits the output chunks over pthreads (CPU baseline only). */
+/* g4o_dequant_w4a16_rows over all N rows, split over nthreads host threads. */
+int g4o_dequant_w4a16_par(const int32_t* packed, const uint16_t* scales_bf16, int N, int K, int group,
+                          float* out, int nthreads);
 int g4o_linear_w4a16(const float* x, int M, const int32_t* packed, const uint16_t* scales_bf16,
                      int K, int N, int group, float* y, int nthreads);
 

@@ -8,9 +8,14 @@ RoPE angle :1197-1198, PLE mix :1259-1262, head softcap :1275), for one sequence
 It mirrors the rounding points of the bf16 activations the B200 path uses (inputs of
 every W4A16 linear, q, K, V and the attention output are bf16) so greedy decoding can
 be compared token for token.  Linear weights are the exact dequantised values
-q * scale (official-w4a16.js:95) for calls of <= 16 rows and their bf16
-materialisation (roundFloat32ToBF16 of q * scale) above, as the GPU's decode GEMV and
-prefill GEMM compute them.  Matmuls run in float32 BLAS, reductions in f32/f64.
+q * scale (official-w4a16.js:95, the reference's own f32 weights) for calls of at most
+`gemm_rows` rows and their bf16 materialisation (roundFloat32ToBF16 of q * scale) above.
+`gemm_rows=EXACT` (no limit) is the reference's arithmetic everywhere: the primary
+comparison.  The default of 16 mirrors where the GPU switches from the decode GEMV
+(exact q * scale) to the tcgen05 GEMM (bf16 weights): a secondary, tighter check of the
+GEMM path.  Matmuls run in float32/float64 BLAS, reductions in f32/f64.  One instance
+holds one sequence at a time; `state()` / `set_state()` swap sequences in and out while
+the dequantised weights stay shared.
 """
 from __future__ import annotations
 
@@ -20,6 +25,9 @@ import numpy as np
 
 from . import bf16_bits_to_f32, f32_to_bf16_bits
 from . import numpy_oracle as npo
+
+
+EXACT = 1 << 62  # gemm_rows that keeps the exact f32 weights for every call
 
 
 def bf16r(x: np.ndarray) -> np.ndarray:
@@ -91,15 +99,26 @@ class OracleModel:
             lin["bf16"] = bf16r(lin["exact"])
         return lin[key]
 
-    def reset(self):
-        self.pos = 0
-        self.k = {}
-        self.v = {}
+    def fresh_state(self) -> dict:
+        """An empty sequence: position 0 and zeroed K/V caches of every non-shared layer."""
+        st = {"pos": 0, "k": {}, "v": {}}
         for i, L in enumerate(self.layers):
             if not L["spec"]["shared"]:
                 hd = L["spec"]["hd"]
-                self.k[i] = np.zeros((self.max_seq, hd), np.float32)
-                self.v[i] = np.zeros((self.max_seq, hd), np.float32)
+                st["k"][i] = np.zeros((self.max_seq, hd), np.float32)
+                st["v"][i] = np.zeros((self.max_seq, hd), np.float32)
+        return st
+
+    def state(self) -> dict:
+        """The current sequence (position and K/V caches), to swap sequences in and out
+        while the dequantised weights stay shared."""
+        return {"pos": self.pos, "k": self.k, "v": self.v}
+
+    def set_state(self, st: dict) -> None:
+        self.pos, self.k, self.v = st["pos"], st["k"], st["v"]
+
+    def reset(self):
+        self.set_state(self.fresh_state())
 
     def linear(self, lin, x):
         w = self._weights(lin, "bf16" if x.shape[0] > self.gemm_rows else "exact")
@@ -111,7 +130,8 @@ class OracleModel:
         cfg = self.cfg
         kk = kc[:keylen].astype(np.float64)
         vv = vc[:keylen].astype(np.float64)
-        logits = np.einsum("rhd,kd->rhk", q.astype(np.float64), kk)
+        R, Hh, D = q.shape
+        logits = (q.astype(np.float64).reshape(R * Hh, D) @ kk.T).reshape(R, Hh, keylen)
         key = np.arange(keylen)[None, :]
         qp = pos[:, None]
         valid = key <= qp
@@ -121,7 +141,7 @@ class OracleModel:
         logits -= logits.max(-1, keepdims=True)
         p = np.exp(logits)
         p /= p.sum(-1, keepdims=True)
-        return bf16r(np.einsum("rhk,kd->rhd", p, vv).astype(np.float32))
+        return bf16r((p.reshape(R * Hh, keylen) @ vv).reshape(R, Hh, D).astype(np.float32))
 
     def forward(self, ids) -> tuple[int, np.ndarray]:
         """Appends ids at the current position; returns (greedy next id, capped logits of the last row)."""

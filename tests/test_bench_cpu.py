@@ -34,6 +34,18 @@ def test_reference_line_contract(workload):
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
 
 
+def test_serve_reference_line_is_the_gpu_arms_config():
+    """The config-5 reference arm times the whole 256-sequence batch and reports the GPU
+    arm's own metric and config object (like-for-like)."""
+    sys.path.insert(0, str(REPO))
+    import bench
+    lines = _run(["--workload", "serve", "--steps", "1", "--warmup", "3"])
+    d = json.loads(lines[0])
+    assert KEYS <= set(d)
+    assert d["metric"] == bench.SERVE_METRIC and d["config"] == bench.serve_config(1)
+    assert d["unit"] == "tok/s" and d["value"] > 0 and "256 sequences" in d["cpu_baseline"]["sample"]
+
+
 def test_reference_arm_other_ranks_are_silent():
     env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
     assert _run(["--workload", "gemv", "--steps", "1", "--warmup", "3"], env=env) == []
