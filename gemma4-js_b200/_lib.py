@@ -67,6 +67,9 @@ SIGNATURES = {
     "g4_linear_shape": (_S, [_P, C.POINTER(_I), C.POINTER(_I)]),
     "g4_linear_w4a16": (_S, [_P, _P, _P, _I, _P, _I]),
     "g4_linear_w4a16_impl": (_S, [_P, _P, _P, _I, _P, _I, _I]),
+    "g4_linear_w4a16_f32": (_S, [_P, _P, _P, _I, _P]),
+    "g4_attention_f32": (_S, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P]),
+    "g4_convert": (_S, [_P, _P, _I, _P, _I, C.c_longlong]),
     "g4_linear_dequant": (_S, [_P, _P, _I, _I, _P, _I]),
     "g4_ple_table_create": (_S, [_P, _P, _P, _I, _I, _I, _I, _PP]),
     "g4_ple_table_upload_rows": (_S, [_P, _P, _I, _I, _P, _P, _I]),
@@ -83,6 +86,11 @@ SIGNATURES = {
     "g4_attention_rows": (_S, [_P, _P, _P, _I, _I, _I, _P, _I, _I, _I, _P]),
     "g4_rms": (_S, [_P, _P, _P, _I, _I, _F, _P, _I]),
     "g4_add_scale": (_S, [_P, _P, _P, C.c_longlong, _F, _P]),
+    "g4_scale": (_S, [_P, _P, C.c_longlong, _F, _P]),
+    "g4_gelu_mul_f32": (_S, [_P, _P, _P, C.c_longlong, _P]),
+    "g4_gelu_ple_f32": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "g4_norm_rope": (_S, [_P, _P, _I, _I, _I, _I, _P, _I, _F, _F, _P]),
+    "g4_softcap": (_S, [_P, _P, C.c_longlong, _F]),
     "g4_post_norm_add": (_S, [_P, _P, _P, _I, _P, _F, _P, _I, _I, _F, _P]),
     "g4_embed": (_S, [_P, _P, _I, _I, _P, _I, _F, _P, _P]),
     "g4_qkv_post": (_S, [_P, _P, _I, _I, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P, _P, _I]),

@@ -577,24 +577,48 @@ g4_status g4_kv_buffers(const g4_kv* kv, void** k, void** v) {
     return G4_OK;
 }
 
-g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads, int hd,
-                       int keylen, int qpos0, int sliding, int window, void* out_bf16) {
+}  // extern "C"
+
+namespace g4 {
+
+// The argument rules of GPUOps.attention with host-side positions, shared by g4_attention
+// and g4_attention_noalloc (`name` prefixes the messages).  *empty is set when rows == 0.
+g4_status check_attention_args(const char* name, g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows,
+                               int heads, int hd, int keylen, int qpos0, int sliding, int window, const void* out_bf16,
+                               bool* empty) {
+    *empty = false;
     g4_status st = g4::use_device(ctx);
     if (st) return st;
-    if (!kv || !q_bf16 || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_attention: null argument");
-    if (rows < 0) return g4::set_error(G4_ERR_INVALID, "g4_attention: rows %d", rows);
-    if (rows == 0) return G4_OK;
-    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "g4_attention: hd %d != cache hd %d", hd, kv->hd);
+    if (!kv || !q_bf16 || !out_bf16) return g4::set_error(G4_ERR_INVALID, "%s: null argument", name);
+    if (rows < 0) return g4::set_error(G4_ERR_INVALID, "%s: rows %d", name, rows);
+    if (rows == 0) {
+        *empty = true;
+        return G4_OK;
+    }
+    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "%s: hd %d != cache hd %d", name, hd, kv->hd);
     if (heads < 1 || heads > 8)
-        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_attention: %d heads per KV head (1..8 supported)", heads);
+        return g4::set_error(G4_ERR_UNSUPPORTED, "%s: %d heads per KV head (1..8 supported)", name, heads);
     if (keylen < 1 || keylen > kv->length)
-        return g4::set_error(G4_ERR_INVALID, "g4_attention: keylen %d outside cache length %d", keylen, kv->length);
+        return g4::set_error(G4_ERR_INVALID, "%s: keylen %d outside cache length %d", name, keylen, kv->length);
     if (qpos0 < 0 || qpos0 + rows > keylen)
-        return g4::set_error(G4_ERR_INVALID, "g4_attention: query positions [%d,%d) not below keylen %d", qpos0,
+        return g4::set_error(G4_ERR_INVALID, "%s: query positions [%d,%d) not below keylen %d", name, qpos0,
                              qpos0 + rows, keylen);
-    if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "g4_attention: window %d", window);
+    if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "%s: window %d", name, window);
     if (reinterpret_cast<uintptr_t>(q_bf16) % 16 != 0)
-        return g4::set_error(G4_ERR_INVALID, "g4_attention: q must be 16-byte aligned");
+        return g4::set_error(G4_ERR_INVALID, "%s: q must be 16-byte aligned", name);
+    return G4_OK;
+}
+
+}  // namespace g4
+
+extern "C" {
+
+g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads, int hd,
+                       int keylen, int qpos0, int sliding, int window, void* out_bf16) {
+    bool empty = false;
+    g4_status st = g4::check_attention_args("g4_attention", ctx, q_bf16, kv, rows, heads, hd, keylen, qpos0, sliding,
+                                            window, out_bf16, &empty);
+    if (st || empty) return st;
     return g4::launch_attention(ctx, kv, 0, static_cast<const uint16_t*>(q_bf16), rows, heads, keylen, qpos0,
                                 sliding ? 1 : 0, window, static_cast<uint16_t*>(out_bf16));
 }
@@ -656,23 +680,10 @@ g4_status noalloc_scratch(int device, void** out) {
 
 extern "C" g4_status g4_attention_noalloc(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
                                           int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16) {
-    g4_status st = g4::use_device(ctx);
-    if (st) return st;
-    if (!kv || !q_bf16 || !out_bf16) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: null argument");
-    if (rows < 0) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: rows %d", rows);
-    if (rows == 0) return G4_OK;
-    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: hd %d != cache hd %d", hd, kv->hd);
-    if (heads < 1 || heads > 8)
-        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_attention_noalloc: %d heads per KV head (1..8 supported)", heads);
-    if (keylen < 1 || keylen > kv->length)
-        return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: keylen %d outside cache length %d", keylen,
-                             kv->length);
-    if (qpos0 < 0 || qpos0 + rows > keylen)
-        return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: query positions [%d,%d) not below keylen %d",
-                             qpos0, qpos0 + rows, keylen);
-    if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: window %d", window);
-    if (reinterpret_cast<uintptr_t>(q_bf16) % 16 != 0)
-        return g4::set_error(G4_ERR_INVALID, "g4_attention_noalloc: q must be 16-byte aligned");
+    bool empty = false;
+    g4_status st = g4::check_attention_args("g4_attention_noalloc", ctx, q_bf16, kv, rows, heads, hd, keylen, qpos0,
+                                            sliding, window, out_bf16, &empty);
+    if (st || empty) return st;
     void* scratch = nullptr;
     st = noalloc_scratch(ctx->device, &scratch);
     if (st) return st;

@@ -27,6 +27,9 @@ struct g4_ctx {
     void* ws = nullptr;             // grow-only scratch for split-K / split-KV partials
     size_t ws_bytes = 0;
     std::vector<void*> ws_retired;  // outgrown workspaces: kept until destroy (captured graphs may use them)
+    void* stage = nullptr;          // grow-only staging for dtype conversions at the boundary (f32 entry points)
+    size_t stage_bytes = 0;
+    std::vector<void*> stage_retired;
     int32_t* d_ids = nullptr;       // staging for host token ids
     size_t d_ids_cap = 0;
     bool pdl = false;               // launch with programmatic dependent launch (g4_ctx_set_pdl)
@@ -46,6 +49,8 @@ g4_status use_device(const g4_ctx* ctx);
 // Ensures ctx->ws holds at least `bytes` (grow-only).  An outgrown buffer is retired,
 // not freed, so CUDA graphs captured with it stay valid until the context is destroyed.
 g4_status ensure_workspace(g4_ctx* ctx, size_t bytes);
+// The same grow-only rule for ctx->stage, the bf16 copies of f32 boundary arguments.
+g4_status ensure_stage(g4_ctx* ctx, size_t bytes);
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 g4_status encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dtype, void* base,
                                uint64_t inner, uint64_t outer, uint64_t row_pitch_bytes,

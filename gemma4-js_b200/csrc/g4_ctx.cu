@@ -51,6 +51,18 @@ g4_status ensure_workspace(g4_ctx* ctx, size_t bytes) {
     return G4_OK;
 }
 
+g4_status ensure_stage(g4_ctx* ctx, size_t bytes) {
+    if (bytes <= ctx->stage_bytes) return G4_OK;
+    size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+    want = (want + 4095) & ~size_t(4095);
+    void* fresh = nullptr;
+    G4_CHECK_CUDA(cudaMalloc(&fresh, want));
+    if (ctx->stage) ctx->stage_retired.push_back(ctx->stage);
+    ctx->stage = fresh;
+    ctx->stage_bytes = want;
+    return G4_OK;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
@@ -124,6 +136,8 @@ g4_status g4_ctx_destroy(g4_ctx* ctx) {
     cudaFree(ctx->d_err);
     cudaFree(ctx->ws);
     for (void* p : ctx->ws_retired) cudaFree(p);
+    cudaFree(ctx->stage);
+    for (void* p : ctx->stage_retired) cudaFree(p);
     cudaFree(ctx->d_ids);
     delete ctx;
     return G4_OK;

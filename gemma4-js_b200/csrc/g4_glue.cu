@@ -411,6 +411,67 @@ __global__ void advance_pos_kernel(int32_t* seq_pos, int seq_base, int nseq, int
 
 inline unsigned blocks_for(long long n, int t) { return (unsigned)((n + t - 1) / t); }
 
+// ---- the reference operators in their own form: separate f32 buffers in and out, for a
+// host that keeps the reference's model graph and only swaps its runtime.
+
+// SCALE: y = a * s.
+__global__ void scale_kernel(const float* __restrict__ a, long long n, float s, float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = a[i] * s;
+}
+
+// GELU_MUL with separate gate and up buffers: y = gelu(gate) * up.
+__global__ void gelu_mul_f32_kernel(const float* __restrict__ gate, const float* __restrict__ up, long long n,
+                                    float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = gelu_ref(gate[i]) * up[i];
+}
+
+// GELU_PLE: y[row, d] = gelu(gate[row, d]) * ple[row, layer, d] (f32 out).
+__global__ void gelu_ple_f32_kernel(const float* __restrict__ gate, const float* __restrict__ per_layer, int layer,
+                                    int layers, int dim, long long n, float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const long long r = i / dim, d = i - r * dim;
+    y[i] = gelu_ref(gate[i]) * per_layer[(r * layers + layer) * dim + d];
+}
+
+// NORM_ROPE: per (row, head) y = rope(x * rsqrt(mean(x^2) + eps) * scale) at position
+// pos0 + row.  One CTA per (head, row), thread i owns the rotation pair (i, i + hd/2).
+__global__ void norm_rope_kernel(const float* __restrict__ x, const float* __restrict__ scale, int heads, int hd,
+                                 int pos0, int rope_angles, float base, float eps, float* __restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float red[32];
+    const int h = blockIdx.x, r = blockIdx.y, half = hd >> 1, i = threadIdx.x;
+    const size_t src = ((size_t)r * heads + h) * hd;
+    const float a0 = x[src + i], a1 = x[src + i + half];
+    const float inv = rsqrtf(block_sum(a0 * a0 + a1 * a1, red) / (float)hd + eps);
+    const float x0 = a0 * inv * scale[i], x1 = a1 * inv * scale[i + half];
+    float sn = 0.f, cs = 1.f;
+    if (i < rope_angles) {
+        const float theta = (float)(pos0 + r) / powf(base, 2.f * (float)i / (float)hd);
+        sn = sinf(theta);
+        cs = cosf(theta);
+    }
+    y[src + i] = x0 * cs - x1 * sn;
+    y[src + i + half] = x1 * cs + x0 * sn;
+}
+
+// The softcap of BF16_HEAD applied to logits in place: v = tanh(v / cap) * cap.
+__global__ void softcap_kernel(float* __restrict__ v, long long n, float cap) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) v[i] = tanhf(v[i] / cap) * cap;
+}
+
 }  // namespace
 
 namespace g4 {
@@ -575,6 +636,59 @@ g4_status g4_softcap_argmax(g4_ctx* ctx, const float* logits, int rows, int voca
     if (st) return st;
     return g4::launch(ctx, "argmax_final_kernel", argmax_final_kernel, dim3(rows), dim3(256), 0, 1,
                       static_cast<const float2*>(part), nparts, ids_out, vals_out);
+}
+
+g4_status g4_scale(g4_ctx* ctx, const float* a, long long n, float s, float* y) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (n < 0 || (n > 0 && (!a || !y))) return g4::set_error(G4_ERR_INVALID, "g4_scale: bad arguments");
+    if (n == 0) return G4_OK;
+    return g4::launch(ctx, "scale_kernel", scale_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, a, n, s, y);
+}
+
+g4_status g4_gelu_mul_f32(g4_ctx* ctx, const float* gate, const float* up, long long n, float* y) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (n < 0 || (n > 0 && (!gate || !up || !y))) return g4::set_error(G4_ERR_INVALID, "g4_gelu_mul_f32: bad arguments");
+    if (n == 0) return G4_OK;
+    return g4::launch(ctx, "gelu_mul_f32_kernel", gelu_mul_f32_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, gate,
+                      up, n, y);
+}
+
+g4_status g4_gelu_ple_f32(g4_ctx* ctx, const float* gate, const float* per_layer, int rows, int layer, int layers,
+                          int dim, float* y) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || dim <= 0 || layers <= 0 || layer < 0 || layer >= layers)
+        return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple_f32: rows %d layer %d of %d dim %d", rows, layer, layers, dim);
+    if (rows == 0) return G4_OK;
+    if (!gate || !per_layer || !y) return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple_f32: null argument");
+    const long long n = (long long)rows * dim;
+    return g4::launch(ctx, "gelu_ple_f32_kernel", gelu_ple_f32_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, gate,
+                      per_layer, layer, layers, dim, n, y);
+}
+
+g4_status g4_norm_rope(g4_ctx* ctx, const float* x, int rows, int heads, int hd, int pos0, const float* scale,
+                       int rope_angles, float base, float eps, float* y) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (rows < 0 || heads < 1 || heads > 65535 || pos0 < 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_norm_rope: rows %d heads %d pos0 %d", rows, heads, pos0);
+    if (hd < 64 || hd > 2048 || hd % 64 != 0)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_norm_rope: hd %d (a multiple of 64 up to 2048)", hd);
+    if (rows == 0) return G4_OK;
+    if (!x || !scale || !y) return g4::set_error(G4_ERR_INVALID, "g4_norm_rope: null argument");
+    return g4::launch(ctx, "norm_rope_kernel", norm_rope_kernel, dim3(heads, rows), dim3(hd / 2), 0, 1, x, scale,
+                      heads, hd, pos0, rope_angles, base, eps, y);
+}
+
+g4_status g4_softcap(g4_ctx* ctx, float* logits, long long n, float cap) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (n < 0 || (n > 0 && !logits) || !(cap > 0.f))
+        return g4::set_error(G4_ERR_INVALID, "g4_softcap: n %lld cap %g", n, (double)cap);
+    if (n == 0) return G4_OK;
+    return g4::launch(ctx, "softcap_kernel", softcap_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1, logits, n, cap);
 }
 
 g4_status g4_advance_positions(g4_ctx* ctx, int32_t* seq_pos, int seq_base, int nseq, int by) {

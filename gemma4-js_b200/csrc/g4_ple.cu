@@ -19,78 +19,85 @@ namespace {
 
 using namespace g4dev;
 
-// One thread per (token, group of 32 columns): 16 B of packed nibbles and one bf16
-// scale in, 64 B (bf16) or 128 B (f32) out.  Consecutive threads walk consecutive
-// groups of a row, so loads and stores are fully coalesced.
+// One CTA per token, one thread per packed 32-bit word (8 columns) at a time.  Consecutive
+// threads own consecutive words, so a warp loads 128 contiguous bytes of nibbles (plus the
+// 16 contiguous bytes of their 8 scales) and stores 512 contiguous bytes of bf16 output in
+// one instruction each.  Each thread first issues the loads of all kPleWords of its words,
+// then decodes and stores them (8960 columns = 1120 words = 160 threads x 7).
 //
 // Decode (ple-w4-shard-reader.js:89-95): column c is nibble (c & 1) of byte c >> 1,
 // i.e. bits 4c..4c+3 of the little-endian 32-bit word c >> 3; value = two's
 // complement nibble * f32(scale), exact in f32.
+constexpr int kPleThreads = 160;
+constexpr int kPleWords = 7;
+
 template <bool kF32Out>
-__global__ void __launch_bounds__(256) ple_gather_kernel(const uint4* __restrict__ packed,
-                                                         const uint16_t* __restrict__ scales,
-                                                         const int32_t* __restrict__ ids, int T,
-                                                         int vocab, int groups_per_row,
-                                                         void* __restrict__ out, uint32_t* err) {
+__global__ void __launch_bounds__(kPleThreads) ple_gather_kernel(const uint32_t* __restrict__ packed,
+                                                                 const uint16_t* __restrict__ scales,
+                                                                 const int32_t* __restrict__ ids, int vocab,
+                                                                 int words_per_row, int groups_per_row,
+                                                                 void* __restrict__ out, uint32_t* err) {
     pdl_trigger();
     pdl_wait();
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long total = (long long)T * groups_per_row;
-    if (i >= total) return;
-    const int t = (int)(i / groups_per_row);
-    const int j = (int)(i - (long long)t * groups_per_row);
+    const int t = blockIdx.x;
     const int id = __ldg(ids + t);
     const bool ok = (unsigned)id < (unsigned)vocab;
-    if (!ok && j == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
-    const size_t src = (size_t)(ok ? id : 0) * groups_per_row + j;
-    uint4 p = make_uint4(0, 0, 0, 0);
-    uint32_t sbits = 0;
-    if (ok) {
-        p = __ldg(packed + src);
-        sbits = __ldg(scales + src);
-    }
-    const uint32_t w[4] = {p.x, p.y, p.z, p.w};
-    if constexpr (!kF32Out) {
-        // bf16 out = RNE(q * s).  q * s is exact in f32, so rounding it once to bf16
-        // equals one correctly rounded bf16 multiply of the exact operands q and s.
-        const uint32_t s2 = sbits | (sbits << 16);
-        uint4* o = reinterpret_cast<uint4*>(out) + i * 4;
+    if (!ok && threadIdx.x == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
+    const uint32_t* prow = packed + (size_t)(ok ? id : 0) * words_per_row;
+    const uint16_t* srow = scales + (size_t)(ok ? id : 0) * groups_per_row;
+    const size_t orow = (size_t)t * words_per_row;
+    for (int base = 0; base < words_per_row; base += kPleThreads * kPleWords) {
+        uint32_t w[kPleWords], sb[kPleWords];
 #pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-            uint32_t r[4];
-#pragma unroll
-            for (int pp = 0; pp < 4; ++pp) {
-                // nibbles pp and pp+4 of the word -> bf16x2 (136 + q) -> exact q
-                uint32_t v;
-                asm("lop3.b32 %0, %1, %2, %3, 0x6A;"
-                    : "=r"(v)
-                    : "r"(w[wi] >> (4 * pp)), "r"(0x000F000Fu), "r"(0x43084308u));
-                uint32_t q;
-                asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(0x43084308u));
-                asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[pp]) : "r"(q), "r"(s2));
+        for (int k = 0; k < kPleWords; ++k) {
+            const int j = base + k * kPleThreads + threadIdx.x;
+            w[k] = 0;
+            sb[k] = 0;
+            if (ok && j < words_per_row) {
+                w[k] = __ldg(prow + j);
+                sb[k] = __ldg(srow + (j >> 2));  // 4 words = one group of 32 columns
             }
-            // r[pp] holds columns (pp, pp+4) of this word; emit (0,1) (2,3) (4,5) (6,7)
-            uint4 ov;
-            ov.x = __byte_perm(r[0], r[1], 0x5410);
-            ov.y = __byte_perm(r[2], r[3], 0x5410);
-            ov.z = __byte_perm(r[0], r[1], 0x7632);
-            ov.w = __byte_perm(r[2], r[3], 0x7632);
-            o[wi] = ov;
         }
-    } else {
-        const float s = bf16_bits_to_f32(sbits);
-        float4* o = reinterpret_cast<float4*>(out) + i * 8;
 #pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-            float v[8];
+        for (int k = 0; k < kPleWords; ++k) {
+            const int j = base + k * kPleThreads + threadIdx.x;
+            if (j >= words_per_row) continue;
+            if constexpr (!kF32Out) {
+                // bf16 out = RNE(q * s).  q * s is exact in f32, so rounding it once to bf16
+                // equals one correctly rounded bf16 multiply of the exact operands q and s.
+                const uint32_t s2 = sb[k] | (sb[k] << 16);
+                uint32_t r[4];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                // ((n ^ 8) | 0x4B000000) as f32 = 2^23 + q + 8
-                const uint32_t m = ((w[wi] >> (4 * e)) & 0xFu) ^ 0x4B000008u;
-                v[e] = (__uint_as_float(m) - 8388616.0f) * s;
+                for (int pp = 0; pp < 4; ++pp) {
+                    // nibbles pp and pp+4 of the word -> bf16x2 (128 + (n ^ 8)) -> minus 136 = signed q
+                    uint32_t v;
+                    asm("lop3.b32 %0, %1, %2, %3, 0x6A;"
+                        : "=r"(v)
+                        : "r"(w[k] >> (4 * pp)), "r"(0x000F000Fu), "r"(0x43084308u));
+                    uint32_t q;
+                    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(0x43084308u));
+                    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[pp]) : "r"(q), "r"(s2));
+                }
+                // r[pp] holds columns (pp, pp+4) of this word; emit (0,1) (2,3) (4,5) (6,7)
+                uint4 ov;
+                ov.x = __byte_perm(r[0], r[1], 0x5410);
+                ov.y = __byte_perm(r[2], r[3], 0x5410);
+                ov.z = __byte_perm(r[0], r[1], 0x7632);
+                ov.w = __byte_perm(r[2], r[3], 0x7632);
+                reinterpret_cast<uint4*>(out)[orow + j] = ov;
+            } else {
+                const float s = bf16_bits_to_f32(sb[k]);
+                float v[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    // ((n ^ 8) | 0x4B000000) as f32 = 2^23 + q + 8
+                    const uint32_t m = ((w[k] >> (4 * e)) & 0xFu) ^ 0x4B000008u;
+                    v[e] = (__uint_as_float(m) - 8388616.0f) * s;
+                }
+                float4* o = reinterpret_cast<float4*>(out) + (orow + j) * 2;
+                o[0] = make_float4(v[0], v[1], v[2], v[3]);
+                o[1] = make_float4(v[4], v[5], v[6], v[7]);
             }
-            o[wi * 2 + 0] = make_float4(v[0], v[1], v[2], v[3]);
-            o[wi * 2 + 1] = make_float4(v[4], v[5], v[6], v[7]);
         }
     }
 }
@@ -211,17 +218,14 @@ g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids
                                       cudaMemcpyHostToDevice, ctx->stream));
         d_ids = ctx->d_ids;
     }
-    const int gpr = tab->width / 32;
-    const long long total = (long long)T * gpr;
-    const int threads = 256;
-    const long long blocks = (total + threads - 1) / threads;
-    if (blocks > 0x7fffffffLL) return g4::set_error(G4_ERR_INVALID, "g4_ple_gather: T too large");
-    const uint4* p = reinterpret_cast<const uint4*>(tab->packed);
+    const int gpr = tab->width / 32, wpr = tab->width / 8;
+    const uint32_t* p = reinterpret_cast<const uint32_t*>(tab->packed);
+    const dim3 grid((unsigned)T), block(kPleThreads);
     if (out_dtype == G4_BF16)
-        return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false>, dim3((unsigned)blocks), dim3(threads), 0, 1,
-                          p, static_cast<const uint16_t*>(tab->scales), d_ids, T, tab->vocab, gpr, out, ctx->d_err);
-    return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true>, dim3((unsigned)blocks), dim3(threads), 0, 1, p,
-                      static_cast<const uint16_t*>(tab->scales), d_ids, T, tab->vocab, gpr, out, ctx->d_err);
+        return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false>, grid, block, 0, 1, p,
+                          static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
+    return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true>, grid, block, 0, 1, p,
+                      static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
 }
 
 }  // extern "C"

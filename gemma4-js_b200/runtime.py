@@ -237,35 +237,121 @@ def _wrap_device(ptr: int, n: int, ctx: Context) -> torch.Tensor:
 
 
 class GPUOps:
-    """GPUOps (gpu-runtime.js:1295-1378): w4 and attention over libg4w4."""
+    """GPUOps (gpu-runtime.js:1295-1378) over libg4w4, method for method.
+
+    Every operator takes and returns the reference's f32 buffers (a new output per call,
+    like `emptyF32`); w4 and attention also take bf16 activations (the W4A16 kernels'
+    own input type), returning bf16 unless asked otherwise."""
 
     def __init__(self, ctx: Context):
         self.ctx = ctx
 
-    def w4(self, linear: W4Linear, x: torch.Tensor, rows: int, out_dtype=torch.bfloat16, impl: int = 0,
+    def _f32(self, n: int) -> torch.Tensor:
+        return torch.empty(n, dtype=torch.float32, device=self.ctx.torch_device)
+
+    @staticmethod
+    def _need_f32(name: str, *ts: torch.Tensor) -> None:
+        for t in ts:
+            if t.dtype != torch.float32:
+                raise G4Error(-1, f"{name}: f32 buffers expected, got {t.dtype}")
+
+    def w4(self, linear: W4Linear, x: torch.Tensor, rows: int, out_dtype=None, impl: int = 0,
            out: torch.Tensor | None = None) -> torch.Tensor:
-        """GPUOps.w4(encoder, linear, x, rows): y[rows, outDim] = x . dequant(W)^T."""
-        if x.dtype != torch.bfloat16:
-            raise G4Error(-1, f"{linear.name}: x must be bf16 (W4A16), got {x.dtype}")
+        """GPUOps.w4(encoder, linear, x, rows): y[rows, outDim] = x . dequant(W)^T.  f32 x (the
+        reference's buffers) gives f32 y through g4_linear_w4a16_f32; bf16 x runs the kernels
+        directly (bf16 out unless out_dtype / out say f32)."""
         x = x.contiguous()
         if x.numel() != rows * linear.in_dim:
             raise G4Error(-1, f"{linear.name}: x has {x.numel()} values, expected {rows}x{linear.in_dim}")
+        if x.dtype == torch.float32:
+            if impl != 0 or (out_dtype not in (None, torch.float32)):
+                raise G4Error(-1, f"{linear.name}: f32 x gives f32 y through the automatic kernel choice")
+            if out is None:
+                out = torch.empty((rows, linear.out_dim), dtype=torch.float32, device=self.ctx.torch_device)
+            call("g4_linear_w4a16_f32", self.ctx.handle, linear.handle, _ptr(x), rows, _ptr(out))
+            return out
+        if x.dtype != torch.bfloat16:
+            raise G4Error(-1, f"{linear.name}: x must be f32 or bf16, got {x.dtype}")
         if out is None:
-            out = torch.empty((rows, linear.out_dim), dtype=out_dtype, device=self.ctx.torch_device)
+            out = torch.empty((rows, linear.out_dim), dtype=out_dtype or torch.bfloat16, device=self.ctx.torch_device)
         call("g4_linear_w4a16_impl", self.ctx.handle, linear.handle, _ptr(x), rows, _ptr(out), _DT[out.dtype], impl)
         return out
 
+    def rms(self, x: torch.Tensor, rows: int, width: int, scale: torch.Tensor | None = None) -> torch.Tensor:
+        """GPUOps.rms(encoder, x, rows, width, scale) (RMS_SHADER, eps 1e-6)."""
+        self._need_f32("rms", x, *([scale] if scale is not None else []))
+        y = self._f32(rows * width)
+        call("g4_rms", self.ctx.handle, _ptr(x), _ptr(scale) if scale is not None else None, rows, width,
+             C.c_float(1e-6), _ptr(y), G4_F32)
+        return y
+
+    def addScale(self, a: torch.Tensor, b: torch.Tensor, n: int, scale: float = 1.0) -> torch.Tensor:  # noqa: N802
+        """GPUOps.addScale(encoder, a, b, n, scale)."""
+        self._need_f32("addScale", a, b)
+        y = self._f32(n)
+        call("g4_add_scale", self.ctx.handle, _ptr(a), _ptr(b), n, C.c_float(scale), _ptr(y))
+        return y
+
+    def scale(self, a: torch.Tensor, n: int, s: float) -> torch.Tensor:
+        """GPUOps.scale(encoder, a, n, s)."""
+        self._need_f32("scale", a)
+        y = self._f32(n)
+        call("g4_scale", self.ctx.handle, _ptr(a), n, C.c_float(s), _ptr(y))
+        return y
+
+    def geluMul(self, gate: torch.Tensor, up: torch.Tensor, n: int) -> torch.Tensor:  # noqa: N802
+        """GPUOps.geluMul(encoder, gate, up, n)."""
+        self._need_f32("geluMul", gate, up)
+        y = self._f32(n)
+        call("g4_gelu_mul_f32", self.ctx.handle, _ptr(gate), _ptr(up), n, _ptr(y))
+        return y
+
+    def geluPle(self, gate: torch.Tensor, ple: torch.Tensor, rows: int, layer: int,  # noqa: N802
+                layers: int = 35, dim: int = 256) -> torch.Tensor:
+        """GPUOps.geluPle(encoder, gate, ple, rows, layer): ple is [rows, 35, 256]."""
+        self._need_f32("geluPle", gate, ple)
+        y = self._f32(rows * dim)
+        call("g4_gelu_ple_f32", self.ctx.handle, _ptr(gate), _ptr(ple), rows, layer, layers, dim, _ptr(y))
+        return y
+
+    def normRope(self, x: torch.Tensor, rows: int, heads: int, hd: int, pos0: int, scale: torch.Tensor,  # noqa: N802
+                 ropeProp: float, base: float) -> torch.Tensor:  # noqa: N803
+        """GPUOps.normRope(encoder, x, rows, heads, hd, pos0, scale, ropeProp, base)."""
+        self._need_f32("normRope", x, scale)
+        y = self._f32(rows * heads * hd)
+        call("g4_norm_rope", self.ctx.handle, _ptr(x), rows, heads, hd, pos0, _ptr(scale), int(ropeProp * hd / 2),
+             C.c_float(base), C.c_float(1e-6), _ptr(y))
+        return y
+
     def attention(self, q: torch.Tensor, cache: KVCache, qrows: int, heads: int, hd: int, keylen: int,
                   qpos0: int, sliding: bool, window: int, out: torch.Tensor | None = None) -> torch.Tensor:
-        """GPUOps.attention(encoder, q, kcache, vcache, qrows, heads, hd, keylen, qpos0, sliding, window)."""
-        if q.dtype != torch.bfloat16:
-            raise G4Error(-1, "attention: q must be bf16")
+        """GPUOps.attention(encoder, q, kcache, vcache, qrows, heads, hd, keylen, qpos0, sliding, window):
+        the cache object stands for the reference's kcache/vcache pair.  f32 q (the reference's
+        buffers) gives an f32 result through g4_attention_f32; bf16 q gives bf16."""
         q = q.contiguous()
+        if q.dtype == torch.float32:
+            if out is None:
+                out = torch.empty((qrows, heads, hd), dtype=torch.float32, device=self.ctx.torch_device)
+            call("g4_attention_f32", self.ctx.handle, _ptr(q), cache.handle, qrows, heads, hd, keylen, qpos0,
+                 int(bool(sliding)), window, _ptr(out))
+            return out
+        if q.dtype != torch.bfloat16:
+            raise G4Error(-1, f"attention: q must be f32 or bf16, got {q.dtype}")
         if out is None:
             out = torch.empty((qrows, heads, hd), dtype=torch.bfloat16, device=self.ctx.torch_device)
         call("g4_attention", self.ctx.handle, _ptr(q), cache.handle, qrows, heads, hd, keylen, qpos0,
              int(bool(sliding)), window, _ptr(out))
         return out
+
+    def pleMix(self, proj: torch.Tensor, normScale: torch.Tensor, tokenPle: torch.Tensor, rows: int,  # noqa: N802,N803
+               layers: int = 35, dim: int = 256) -> torch.Tensor:
+        """GPUOps.pleMix(encoder, proj, normScale, tokenPle, rows): the reference scales proj
+        beforehand (ops.scale by 1/sqrt(hidden)); proj here is that scaled projection."""
+        self._need_f32("pleMix", proj, normScale, tokenPle)
+        y = self._f32(rows * layers * dim)
+        call("g4_ple_mix", self.ctx.handle, _ptr(proj), C.c_float(1.0), _ptr(normScale), _ptr(tokenPle), rows,
+             layers, dim, C.c_float(1e-6), _ptr(y))
+        return y
 
 
 def launch_count() -> int:

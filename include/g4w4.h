@@ -118,6 +118,12 @@ g4_status g4_linear_shape(const g4_linear* lin, int* K, int* N);
  * M = 0 is a no-op. */
 g4_status g4_linear_w4a16(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
                           void* y, g4_dtype y_dtype);
+/* GPUOps.w4 with the reference's own buffer types (custom-webgpu/gpu-runtime.js:1316-1324:
+ * x is an f32 buffer [rows, inDim], the result a new f32 buffer [rows, outDim]).  x is
+ * rounded to bf16 (round to nearest even) into a context staging buffer by one extra
+ * kernel, then g4_linear_w4a16 runs with an f32 output.  The staging buffer grows with
+ * cudaMalloc on first use of a larger M (not during stream capture). */
+g4_status g4_linear_w4a16_f32(g4_ctx* ctx, const g4_linear* lin, const float* x, int M, float* y);
 /* Forces one implementation (0 = auto, 1 = decode GEMV, 2 = tcgen05 GEMM) for tests
  * and benchmarks.  The GEMV accepts any M (it runs M in slices of 16). */
 g4_status g4_linear_w4a16_impl(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
@@ -207,6 +213,20 @@ g4_status g4_kv_buffers(const g4_kv* kv, void** k, void** v);
 g4_status g4_attention(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows, int heads,
                        int hd, int keylen, int qpos0, int sliding, int window, void* out_bf16);
 
+/* GPUOps.attention with the reference's f32 q and f32 result (custom-webgpu/gpu-runtime.js:1357-1365,
+ * `emptyF32(qrows * heads * hd)`).  The KV cache stays bf16 (g4_kv_append accepts the
+ * reference's f32 K/V rows and rounds them).  q is rounded to bf16 in the context staging
+ * buffer, g4_attention runs, and its bf16 rows are widened to f32 exactly: two extra
+ * conversion kernels.  Same argument rules and errors as g4_attention. */
+g4_status g4_attention_f32(g4_ctx* ctx, const float* q, const g4_kv* kv, int rows, int heads, int hd, int keylen,
+                           int qpos0, int sliding, int window, float* out);
+
+/* Elementwise dtype conversion of n values on the context stream, for hosts that keep the
+ * reference's f32 buffers: G4_F32 -> G4_BF16 rounds to nearest even, bit-identical to
+ * roundFloat32ToBF16 (browser-tfjs-webgl-distribution/runtime/official-w4a16.js:34-48);
+ * G4_BF16 -> G4_F32 is exact (bits << 16, gpu-runtime.js:1058-1066); equal dtypes copy. */
+g4_status g4_convert(g4_ctx* ctx, const void* src, g4_dtype src_dtype, void* dst, g4_dtype dst_dtype, long long n);
+
 /* g4_attention for callers that cannot allocate device memory.  No counterpart in the
  * reference: its WebGPU runtime allocates a buffer for every op.  g4_attention splits a
  * long key range across CTAs and keeps the partial results in a context workspace that
@@ -243,6 +263,24 @@ g4_status g4_rms(g4_ctx* ctx, const float* x, const float* scale, int rows, int 
                  g4_dtype out_dtype);
 /* GPUOps.addScale (ADD_SCALE :1120-1128): y = (a + b) * scale. */
 g4_status g4_add_scale(g4_ctx* ctx, const float* a, const float* b, long long n, float scale, float* y);
+/* GPUOps.scale (SCALE_SHADER :1130-1137): y = a * s. */
+g4_status g4_scale(g4_ctx* ctx, const float* a, long long n, float s, float* y);
+/* GPUOps.geluMul (GELU_MUL :1139-1157) on the reference's separate f32 gate and up buffers:
+ * y = gelu_tanh(gate) * up, tanh argument clamped to [-10, 10], f32 out. */
+g4_status g4_gelu_mul_f32(g4_ctx* ctx, const float* gate, const float* up, long long n, float* y);
+/* GPUOps.geluPle (GELU_PLE :1159-1173) with f32 out: y[r, d] = gelu(gate[r, d]) * ple[r, layer, d]
+ * (ple f32 [rows, layers, dim]). */
+g4_status g4_gelu_ple_f32(g4_ctx* ctx, const float* gate, const float* per_layer, int rows, int layer, int layers,
+                          int dim, float* y);
+/* GPUOps.normRope (NORM_ROPE_SHADER :1175-1202): per row r and head, RMS-normalise the
+ * head's hd values (eps), multiply by scale[hd], then rotate pairs (i, i + hd/2) for
+ * i < rope_angles (= floor(ropeProp * hd / 2)) by theta = (pos0 + r) / base^(2i/hd).
+ * x, y f32 [rows, heads, hd]; hd a multiple of 64. */
+g4_status g4_norm_rope(g4_ctx* ctx, const float* x, int rows, int heads, int hd, int pos0, const float* scale,
+                       int rope_angles, float base, float eps, float* y);
+/* The softcap of BF16_HEAD (:1265-1277, `tanh(raw / softcap) * softcap`) applied in place to
+ * logits from g4_dense_matmul (GPUOps.headChunk = g4_dense_matmul + g4_softcap). */
+g4_status g4_softcap(g4_ctx* ctx, float* logits, long long n, float cap);
 /* rms + addScale (+ the next rms) of one residual update (gemma4-webgpu.js:264-273, :288-297, :302-307):
  * h = (h + rms(y) * w_post) * skip; x_out = bf16(w_next ? rms(h) * w_next : h) (x_out may be NULL). */
 g4_status g4_post_norm_add(g4_ctx* ctx, float* h, const float* y, int ldy, const float* w_post, float skip,

@@ -94,8 +94,10 @@ def test_config1_gemv(rt, ctx, ops, oracle):
 def test_linear_errors(rt, ctx, ops, oracle, g4):
     packed, scales = make_weights(oracle, 64, 16, 1)
     lin = rt.W4Linear(ctx, packed, scales)
-    with pytest.raises(g4.G4Error):
-        ops.w4(lin, torch.zeros((2, 64), dtype=torch.float32, device="cuda"), 2)
+    with pytest.raises(g4.G4Error, match="f32 or bf16"):
+        ops.w4(lin, torch.zeros((2, 64), dtype=torch.float16, device="cuda"), 2)
+    with pytest.raises(g4.G4Error, match="automatic"):
+        ops.w4(lin, torch.zeros((2, 64), dtype=torch.float32, device="cuda"), 2, impl=2)
     with pytest.raises(g4.G4Error, match="expected"):
         ops.w4(lin, torch.zeros((2, 60), dtype=torch.bfloat16, device="cuda"), 2)
     with pytest.raises(g4.G4Error, match="only 32"):
