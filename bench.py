@@ -989,6 +989,7 @@ def run_decode(args, torch, rt, ctx, dist, peaks):
     e2.record()
     torch.cuda.synchronize()
     e2e_ms = dist.max(s2.elapsed_time(e2)) / n2
+    timeline = _decoder_timeline(torch, m) if m.decoder() is not None else None
     w4_bytes = sum(L[n].in_dim * L[n].out_dim * 9 // 16 for L in m.layers for n in ("qkv", "o", "gu", "down", "pg", "pp"))
     per_tok = w4_bytes + m.top.in_dim * m.top.out_dim * 9 // 16 + cfg.vocab * cfg.hidden * 2
     tok_s = K / (ms / 1e3) * dist.world
@@ -998,17 +999,51 @@ def run_decode(args, torch, rt, ctx, dist, peaks):
         "n_gpus": dist.world, "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompt)",
         "config": {"workload": "config4_decode_b1", "prompt": prompt_len, "prefill_ms": round(prefill_ms, 2),
-                   "l2": "1.5 GB of weights per token (>> L2)"},
-        "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + head bytes per token)",
+                   "l2": "1.5 GB of weights per token (>> L2)",
+                   "decode_kernel": ("decode_step_kernel: the whole token in one persistent launch"
+                                     if m.decoder() is not None else "operator path")},
+        "roofline": {"bound": "hbm", "kernel": ("decode_step_kernel (weights + head bytes per token)"
+                                                if m.decoder() is not None else
+                                                "whole decode step (weights + head bytes per token)"),
                      "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"], "traffic": None,
                      "bytes_per_launch": per_tok},
         "e2e": {"value": round(1 / (e2e_ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
         "gpu_launches": _graph_kernel_count(m) * K, "clocks": clocks,
     }
+    if timeline:
+        line["decode_timeline"] = timeline
     if dist.rank == 0 and dist.world == 1 and not getattr(args, "no_cpu", False):
         line["cpu_baseline"] = cpu_decode(batch=1, ctx_len=prompt_len)
     return line
+
+
+DECODER_PHASES = ("qkv", "attention", "combine", "o", "gate_up", "down", "ple_gate", "ple_proj")
+
+
+def _decoder_timeline(torch, m):
+    """One eager persistent step with its first CTA's globaltimer stamps on: per phase kind,
+    the mean time the CTA worked before each barrier and the mean time it then waited in it
+    (us), and the step's total.  Taken after the timed region (it advances the sequence)."""
+    lib = importlib.import_module("gemma4-js_b200._lib")
+    dec = m.decoder()
+    nb = 8 * m.cfg.layers + 1
+    buf = torch.zeros(2 * nb + 2, dtype=torch.int64, device="cuda")
+    lib.call("g4_decoder_set_timeline", dec.handle, C.c_void_p(buf.data_ptr()), buf.numel())
+    m.decode_step(batch=1)
+    torch.cuda.synchronize()
+    lib.call("g4_decoder_set_timeline", dec.handle, None, 0)
+    t = buf.cpu().numpy().astype(np.float64) / 1e3
+    pairs = t[1:1 + 2 * nb].reshape(nb, 2)
+    passed = np.concatenate([[t[0]], pairs[:-1, 1]])
+    work, wait = pairs[:, 0] - passed, pairs[:, 1] - pairs[:, 0]
+    out = {"total_us": round(float(t[2 * nb + 1] - t[0]), 1), "barriers": nb,
+           "barrier_wait_us": round(float(wait.sum()), 1), "work_us": round(float(work.sum()), 1)}
+    for k, name in enumerate(DECODER_PHASES):
+        out[name] = {"work_us": round(float(work[k:nb - 1:8].mean()), 2), "wait_us": round(float(wait[k:nb - 1:8].mean()), 2)}
+    out["head"] = {"work_us": round(float(work[-1]), 2), "wait_us": round(float(wait[-1]), 2),
+                   "tail_us": round(float(t[2 * nb + 1] - pairs[-1, 1]), 2)}
+    return out
 
 
 # ------------------------------------------------------------ CPU baseline --

@@ -30,6 +30,24 @@ class G4Planes(C.Structure):
     """g4_planes: a linear's f32 output as partial planes summed in slice order (include/g4w4.h)."""
     _fields_ = [("base", C.c_void_p), ("count", C.c_int), ("stride", C.c_longlong), ("ld", C.c_int)]
 
+class G4DecoderLayer(C.Structure):
+    """g4_decoder_layer (include/g4w4.h)."""
+    _fields_ = [("qkv", C.c_void_p), ("o", C.c_void_p), ("gu", C.c_void_p), ("down", C.c_void_p),
+                ("pg", C.c_void_p), ("pp", C.c_void_p),
+                ("n_in", C.c_void_p), ("n_pa", C.c_void_p), ("n_pf", C.c_void_p), ("n_pff", C.c_void_p),
+                ("n_pple", C.c_void_p), ("qn", C.c_void_p), ("kn", C.c_void_p),
+                ("skip", C.c_float), ("kv", C.c_void_p), ("has_kv", C.c_int), ("full", C.c_int),
+                ("rope_angles", C.c_int), ("rope_base", C.c_float), ("inter", C.c_int)]
+
+
+class G4DecoderDesc(C.Structure):
+    """g4_decoder_desc (include/g4w4.h)."""
+    _fields_ = [("layers", C.c_int), ("hidden", C.c_int), ("heads", C.c_int), ("ple_dim", C.c_int),
+                ("window", C.c_int), ("vocab", C.c_int), ("eps", C.c_float), ("softcap", C.c_float),
+                ("top", C.c_void_p), ("ple_norm", C.c_void_p), ("final_norm", C.c_void_p), ("embed", C.c_void_p),
+                ("ple", C.c_void_p)]
+
+
 STATUS_NAMES = {
     0: "G4_OK", -1: "G4_ERR_INVALID", -2: "G4_ERR_OOM", -3: "G4_ERR_CUDA", -4: "G4_ERR_TIMEOUT",
     -5: "G4_ERR_UNSUPPORTED", -6: "G4_ERR_RANGE", -7: "G4_ERR_DEVICE",
@@ -110,6 +128,11 @@ SIGNATURES = {
     "g4_dense_destroy": (_S, [_P]),
     "g4_dense_weights": (_S, [_P, _PP]),
     "g4_dense_matmul": (_S, [_P, _P, _P, _I, _P]),
+    "g4_decoder_create": (_S, [_P, _P, _P, _PP]),
+    "g4_decoder_destroy": (_S, [_P]),
+    "g4_decoder_step": (_S, [_P, _P, _P, _P, _P, _P]),
+    "g4_decoder_reset": (_S, [_P]),
+    "g4_decoder_set_timeline": (_S, [_P, _P, _I]),
 }
 
 _lib = None

@@ -11,12 +11,7 @@
 #include "g4_linear.cuh"
 #include "g4_tcgen05.cuh"
 
-struct g4_dense {
-    g4_ctx* ctx = nullptr;
-    int K = 0, N = 0;
-    uint16_t* w = nullptr;  // [N, K] bf16
-    CUtensorMap bmap;       // boxes of 64 columns x 256 rows, 128B swizzle (tcgen05 B operand)
-};
+#include "g4_dense.cuh"
 
 namespace {
 

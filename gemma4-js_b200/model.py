@@ -233,12 +233,62 @@ class Dense:
             pass
 
 
+class Decoder:
+    """g4_decoder: the whole batch-1 decode step of a Gemma4Model as one persistent launch
+    (one CTA per SM, phases separated by grid barriers, weights streamed ahead of each
+    barrier).  Built from the model's own device objects; see include/g4w4.h."""
+
+    def __init__(self, m: "Gemma4Model"):
+        cfg = m.cfg
+        n = len(m.layers)
+        self._keep = []
+        layers = (_lib.G4DecoderLayer * n)()
+        for i, L in enumerate(m.layers):
+            s = L["spec"]
+            nxt = m.layers[i]["n_in"]
+            layers[i] = _lib.G4DecoderLayer(
+                L["qkv"].handle, L["o"].handle, L["gu"].handle, L["down"].handle, L["pg"].handle, L["pp"].handle,
+                nxt.data_ptr(), L["n_pa"].data_ptr(), L["n_pf"].data_ptr(), L["n_pff"].data_ptr(),
+                L["n_pple"].data_ptr(), L["qn"].data_ptr(), L["kn"].data_ptr(), C.c_float(L["skip"]),
+                L["kv"].handle, 0 if s["shared"] else 1, 1 if s["full"] else 0, s["rope_angles"],
+                C.c_float(s["rope_base"]), s["inter"])
+        desc = _lib.G4DecoderDesc(n, cfg.hidden, cfg.heads, cfg.ple_dim, cfg.window, cfg.vocab, C.c_float(cfg.eps),
+                                  C.c_float(cfg.softcap), m.top.handle, m.ple_norm.data_ptr(),
+                                  m.final_norm.data_ptr(), m.head.handle, m.ple.handle)
+        h = C.c_void_p()
+        call("g4_decoder_create", m.ctx.handle, C.byref(desc), layers, C.byref(h))
+        self.handle = h
+
+    def step(self, ctx: Context, ids, seq_pos, nxt, val):
+        call("g4_decoder_step", ctx.handle, self.handle, _ptr(ids), _ptr(seq_pos), _ptr(nxt), _ptr(val))
+
+    def reset(self):
+        call("g4_decoder_reset", self.handle)
+
+    def close(self):
+        if getattr(self, "handle", None):
+            _lib.load().g4_decoder_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 class Gemma4Model:
-    """Mirror of Gemma4WebGPU over libg4w4 (see the module docstring)."""
+    """Mirror of Gemma4WebGPU over libg4w4 (see the module docstring).
+
+    persistent: decode steps of a single-sequence model (max_batch 1) run as one
+    persistent g4_decoder launch instead of the ~430 operator launches of the op path
+    (prefill and batched decode always use the operators)."""
 
     def __init__(self, ctx: Context, cfg: ModelConfig, w: dict, max_batch: int = 1, max_seq: int = 512,
-                 max_rows: int | None = None, pdl: bool = True):
+                 max_rows: int | None = None, pdl: bool = True, persistent: bool = True):
         self.ctx, self.cfg = ctx, cfg
+        self.persistent = persistent and max_batch == 1
+        self._dec = None
         if pdl:  # the decode step is a long chain of this library's kernels on one stream
             ctx.set_pdl(True)
         self.max_batch, self.max_seq = max_batch, max_seq
@@ -380,6 +430,20 @@ class Gemma4Model:
         self.ctx.check_device()
         return int(self.buf["next"][0].item())
 
+    def decoder(self) -> "Decoder | None":
+        """The persistent decoder of this model (built on first use), or None when the model
+        is batched, persistent decoding is off, or the shapes are outside its range."""
+        if not self.persistent:
+            return None
+        if self._dec is None:
+            try:
+                self._dec = Decoder(self)
+            except G4Error as e:
+                if e.status != -5:  # only an unsupported shape falls back to the operators
+                    raise
+                self._dec = False
+        return self._dec or None
+
     def decode_step(self, ids_dev: torch.Tensor | None = None, batch: int | None = None) -> torch.Tensor:
         """One greedy decode step of sequences 0..batch-1 (row b = sequence b); reads the
         current tokens from ids_dev (default: the previous step's picks) and returns the
@@ -387,6 +451,10 @@ class Gemma4Model:
         B = batch or self.max_batch
         if ids_dev is not None:
             self.buf["next"][:B].copy_(ids_dev[:B])
+        dec = self.decoder() if B == 1 else None
+        if dec is not None:  # the whole step in one launch: reads next[0], writes next[0] and val[0]
+            dec.step(self.ctx, self.buf["next"], self.seq_pos, self.buf["next"], self.buf["val"])
+            return self.buf["next"][:1]
         self.buf["ids"][:B].copy_(self.buf["next"][:B])
         # Inside a captured graph the positions and the cached history come from earlier
         # launches of the graph, so the attention may stream them before its wait.
@@ -455,3 +523,6 @@ class Gemma4Model:
 
     def close(self):
         self.graph = None
+        if self._dec:
+            self._dec.close()
+        self._dec = None

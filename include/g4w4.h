@@ -339,6 +339,58 @@ g4_status g4_dense_matmul(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, in
 g4_status g4_dense_argmax(g4_ctx* ctx, const g4_dense* d, const void* x_bf16, int M, float cap, int32_t* ids_out,
                           float* vals_out);
 
+/* ------------------------------------------------- persistent batch-1 decoder --
+ * The whole greedy decode step of one sequence (Gemma4WebGPU.forward + logits + greedy,
+ * custom-webgpu/gemma4-webgpu.js:311-480: every layer's encodeLayer :215-310 over the
+ * operators above) as ONE kernel launch with one CTA per SM: phases separated by grid-wide
+ * barriers, each CTA streaming its share of the next linear's int4 weights into shared
+ * memory while the barrier before it resolves.  The arithmetic is the op path's (exact
+ * int4 x bf16 products, FP32 accumulation, bf16 activations into the linears, f32 norms);
+ * only summation orders differ.  Built from the same objects the op path uses. */
+typedef struct g4_decoder g4_decoder;
+typedef struct {
+    const g4_linear *qkv, *o, *gu, *down, *pg, *pp; /* gu: gate/up rows in 64-row slabs (g4_linear_w4a16_geglu) */
+    const float *n_in, *n_pa, *n_pf, *n_pff, *n_pple, *qn, *kn; /* f32 norm scales (kn unused without has_kv) */
+    float skip;               /* layer scalar of the PLE residual */
+    const g4_kv* kv;          /* this layer's cache, or the cache it shares */
+    int has_kv;               /* 0: a KV-shared layer (reads kv, appends nothing) */
+    int full;                 /* 1: global attention; 0: sliding window */
+    int rope_angles;          /* floor(rope proportion * hd / 2) */
+    float rope_base;
+    int inter;                /* MLP width (gu has 2 * inter rows) */
+} g4_decoder_layer;
+typedef struct {
+    int layers, hidden, heads, ple_dim, window, vocab;
+    float eps, softcap;
+    const g4_linear* top;      /* per_layer_model_projection [layers * ple_dim, hidden] */
+    const float* ple_norm;     /* [ple_dim] */
+    const float* final_norm;   /* [hidden] */
+    const g4_dense* embed;     /* tied bf16 embedding [vocab, hidden], also the LM head */
+    const g4_ple_table* ple;   /* [vocab, layers * ple_dim] */
+} g4_decoder_desc;
+/* No reference counterpart (the reference dispatches each operator).  Validates the shapes,
+ * plans each CTA's share of every linear and allocates the decoder's device scratch.
+ * G4_ERR_UNSUPPORTED when a CTA's share of a linear does not fit its shared memory or the
+ * caches are longer than 256 key tiles (16384 positions at head dim 256). */
+g4_status g4_decoder_create(g4_ctx* ctx, const g4_decoder_desc* desc, const g4_decoder_layer* layers,
+                            g4_decoder** out);
+g4_status g4_decoder_destroy(g4_decoder* dec);
+/* One greedy decode step of sequence 0 (cache rows = positions): reads the token ids[0] and the
+ * position seq_pos[0] (device), appends K/V at that position in every layer with has_kv,
+ * writes the next token to next[0] (its capped logit to val[0] if val is not NULL) and
+ * advances seq_pos[0].  ids and next may be the same buffer, so a CUDA graph of this call
+ * replays step after step.  A cooperative launch of one CTA per SM: no other kernel of the
+ * device may hold SMs it needs for the length of the step. */
+g4_status g4_decoder_step(g4_ctx* ctx, g4_decoder* dec, const int32_t* ids, int32_t* seq_pos, int32_t* next,
+                          float* val);
+/* After a step reported G4_ERR_TIMEOUT (g4_ctx_check_device): clears the decoder's grid
+ * barrier words so the next step starts clean.  Synchronises the context stream. */
+g4_status g4_decoder_reset(g4_decoder* dec);
+/* Tracing hook (no reference counterpart): while timeline is set, every step writes up to
+ * `entries` globaltimer stamps (ns) of its first CTA into that device buffer: the start,
+ * then an (arrive, pass) pair per grid barrier, then the end.  NULL switches it off. */
+g4_status g4_decoder_set_timeline(g4_decoder* dec, unsigned long long* timeline, int entries);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,13 @@ def test_struct_layouts_match_the_header(tmp_path):
         '  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(g4_planes), offsetof(g4_planes, base),\n'
         "         offsetof(g4_planes, count), offsetof(g4_planes, stride), offsetof(g4_planes, ld), 0ul);\n"
         '  printf("%d\\n", G4_ROWS_HISTORY_READY);\n'
+        '  printf("%zu %zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(g4_decoder_layer), offsetof(g4_decoder_layer, kn),\n'
+        "         offsetof(g4_decoder_layer, skip), offsetof(g4_decoder_layer, kv), offsetof(g4_decoder_layer, has_kv),\n"
+        "         offsetof(g4_decoder_layer, rope_angles), offsetof(g4_decoder_layer, rope_base),\n"
+        "         offsetof(g4_decoder_layer, inter), 0ul);\n"
+        '  printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(g4_decoder_desc), offsetof(g4_decoder_desc, eps),\n'
+        "         offsetof(g4_decoder_desc, softcap), offsetof(g4_decoder_desc, top), offsetof(g4_decoder_desc, embed),\n"
+        "         offsetof(g4_decoder_desc, ple));\n"
         "  return 0;\n}\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-std=c11", "-I", str(inc), str(src), "-o", str(exe)], check=True)
@@ -76,3 +83,8 @@ def test_struct_layouts_match_the_header(tmp_path):
     assert rows[:5] == [C.sizeof(R), R.seq_base.offset, R.rows_per_seq.offset, R.pos0.offset, R.flags.offset]
     assert planes[:5] == [C.sizeof(P), P.base.offset, P.count.offset, P.stride.offset, P.ld.offset]
     assert int(lines[2]) == L.G4_ROWS_HISTORY_READY
+    dl, dd = [int(v) for v in lines[3].split()], [int(v) for v in lines[4].split()]
+    DL, DD = L.G4DecoderLayer, L.G4DecoderDesc
+    assert dl[:8] == [C.sizeof(DL), DL.kn.offset, DL.skip.offset, DL.kv.offset, DL.has_kv.offset,
+                      DL.rope_angles.offset, DL.rope_base.offset, DL.inter.offset]
+    assert dd == [C.sizeof(DD), DD.eps.offset, DD.softcap.offset, DD.top.offset, DD.embed.offset, DD.ple.offset]

@@ -282,3 +282,47 @@ def test_geglu_fused_linear_matches_linear_then_gelu_mul(rt, ctx, M, K, inter):
     L.call("g4_linear_w4a16_geglu", ctx.handle, lin_i.handle, P(x), M, P(a2))
     ctx.check_device()
     assert torch.equal(a1, a2)
+
+
+def test_fused_head_pick_matches_oracle_softcap_and_tie_rule(rt, ctx, oracle):
+    """head_argmax_kernel against the reference's pick computed on the host: f32 softcap
+    tanh(raw / 30) * 30, then the lowest index of the largest capped value
+    (gemma4-webgpu.js:465-478, topK gpu-runtime.js:1396-1425).  The raw logits are exact
+    (one-hot activations times bf16-exact table entries), so only the softcap and the tie
+    rule are under test.  Planted cases per row: exact ties of the maximum at several
+    indices; saturated logits (raw >= 600, where the capped value is exactly 30.0 for every
+    raw) with the largest raw at a higher index than a smaller saturated one; and a
+    near-cap maximum (raw 80.25 against 80.0) that must stay distinct.  The kernel computes
+    the softcap only when a raw maximum improves, which equals this rule for a
+    non-decreasing softcap."""
+    model = importlib.import_module("gemma4-js_b200.model")
+    M, V, K = 24, 20000, 1536  # M > 16: the fused tcgen05 head
+    rng = np.random.default_rng(77)
+    E = (np.round(rng.uniform(-40, 40, (V, K)) * 4) / 4).astype(np.float32)  # multiples of 0.25: bf16-exact
+    expect = []
+    for m in range(M):
+        col = E[:, m]
+        kind = m % 4
+        if kind == 0:    # exact ties of the maximum
+            idx = np.sort(rng.choice(V, 3, replace=False))
+            col[idx] = 64.0
+        elif kind == 1:  # saturated: raw 600 at a low index, raw 1024 and 2048 later: capped 30.0 for all
+            idx = np.sort(rng.choice(V, 3, replace=False))
+            col[idx[0]], col[idx[1]], col[idx[2]] = 600.0, 1024.0, 2048.0
+        elif kind == 2:  # near the cap but distinct
+            idx = np.sort(rng.choice(V, 2, replace=False))
+            col[idx[0]], col[idx[1]] = 80.0, 80.25
+        capped = np.tanh(col / np.float32(30.0)).astype(np.float32) * np.float32(30.0)
+        expect.append(int(np.argmax(capped)))   # numpy argmax: the lowest index of the maximum
+    assert np.array_equal(bf16_round(E), E)
+    d = model.Dense(ctx, torch.from_numpy(oracle.f32_to_bf16_bits(E).view(np.int16)).cuda().view(torch.bfloat16))
+    x = np.zeros((M, K), np.float32)
+    x[np.arange(M), np.arange(M)] = 1.0     # raw[m, r] = E[r, m] exactly
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    ids = torch.empty(M, dtype=torch.int32, device="cuda")
+    vals = torch.empty(M, dtype=torch.float32, device="cuda")
+    L.call("g4_dense_argmax", ctx.handle, d.handle, P(xt), M, C.c_float(30.0), P(ids), P(vals))
+    ctx.check_device()
+    assert ids.cpu().tolist() == expect
+    ref_vals = np.array([np.tanh(E[expect[m], m] / np.float32(30.0)) * np.float32(30.0) for m in range(M)], np.float32)
+    assert np.allclose(vals.cpu().numpy(), ref_vals, rtol=2e-6, atol=0)

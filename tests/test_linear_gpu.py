@@ -164,3 +164,21 @@ def test_tcgen05_gemm_lm_head_shape_property(rt, ctx, ops):
     y2 = ops.w4(lin, (x.float() * 2).to(torch.bfloat16), M, out_dtype=torch.float32, impl=2)
     assert torch.equal(y2, y * 2)  # exact: scaling bf16 inputs by 2 scales every product exactly
     ctx.check_device()
+
+
+def test_tcgen05_gemm_lm_head_shape_vs_oracle(rt, ctx, ops, oracle):
+    """Config 3's largest point, M = 2048 at (K, N) = (1536, 262144), against the oracle's
+    exact f32 dequant-matmul (official-quantized-linear.js:82-128) on 512 sampled output
+    columns (all 2048 rows)."""
+    K, N, M = 1536, 262144, 2048
+    packed, scales = make_weights(oracle, K, N, 262144)
+    lin = rt.W4Linear(ctx, packed, scales)
+    rng = np.random.default_rng(5)
+    x = bf16_round(rng.standard_normal((M, K)).astype(np.float32))
+    y = ops.w4(lin, torch.from_numpy(x).to(torch.bfloat16).cuda(), M, out_dtype=torch.float32, impl=2)
+    ctx.check_device()
+    cols = np.sort(rng.choice(N, 512, replace=False))
+    got = y[:, torch.from_numpy(cols).cuda()].cpu().numpy()
+    del y
+    ref = oracle.linear_w4a16(x, packed[cols], scales[cols], nthreads=8)
+    assert max_rel(got, ref) < TOL
