@@ -950,7 +950,7 @@ def run_decode(args, torch, rt, ctx, dist, peaks):
     """benchmark config 4: batch 1, 2048-token random prompt, then greedy decode."""
     K, W = args.steps, args.warmup
     prompt_len = 2048
-    cfg, m = _decode_model(torch, rt, ctx, 1, prompt_len + W + K + 8, prompt_len)
+    cfg, m = _decode_model(torch, rt, ctx, 1, prompt_len + 2 * (W + K) + 64, prompt_len)
     ids = np.random.default_rng(dist.rank).integers(0, cfg.vocab, prompt_len)
     torch.cuda.synchronize()
     s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -989,7 +989,8 @@ def run_decode(args, torch, rt, ctx, dist, peaks):
     e2.record()
     torch.cuda.synchronize()
     e2e_ms = dist.max(s2.elapsed_time(e2)) / n2
-    timeline = _decoder_timeline(torch, m) if m.decoder() is not None else None
+    op_launches = _graph_kernel_count(m)
+    persistent = _persistent_decode(torch, m, dist, K, W)
     w4_bytes = sum(L[n].in_dim * L[n].out_dim * 9 // 16 for L in m.layers for n in ("qkv", "o", "gu", "down", "pg", "pp"))
     per_tok = w4_bytes + m.top.in_dim * m.top.out_dim * 9 // 16 + cfg.vocab * cfg.hidden * 2
     tok_s = K / (ms / 1e3) * dist.world
@@ -1000,53 +1001,136 @@ def run_decode(args, torch, rt, ctx, dist, peaks):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, random prompt)",
         "config": {"workload": "config4_decode_b1", "prompt": prompt_len, "prefill_ms": round(prefill_ms, 2),
                    "l2": "1.5 GB of weights per token (>> L2)",
-                   "decode_kernel": ("decode_step_kernel: the whole token in one persistent launch"
-                                     if m.decoder() is not None else "operator path")},
-        "roofline": {"bound": "hbm", "kernel": ("decode_step_kernel (weights + head bytes per token)"
-                                                if m.decoder() is not None else
-                                                "whole decode step (weights + head bytes per token)"),
+                   "decode_kernel": "operator path: one CUDA graph of PDL-chained kernels"},
+        "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + head bytes per token)",
                      "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_source": peaks["source"], "traffic": None,
                      "bytes_per_launch": per_tok},
         "e2e": {"value": round(1 / (e2e_ms / 1e3), 1), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4},
-        "gpu_launches": _graph_kernel_count(m) * K, "clocks": clocks,
+        "gpu_launches": op_launches * K, "launches_per_step": op_launches, "clocks": clocks,
     }
-    if timeline:
-        line["decode_timeline"] = timeline
+    if persistent:
+        persistent["achieved_gbs"] = round(per_tok / (persistent["ms_per_step"] / 1e3) / 1e9, 1)
+        persistent["frac"] = round(persistent["achieved_gbs"] / peaks["hbm_gbs"], 4)
+        line["persistent_decoder"] = persistent
     if dist.rank == 0 and dist.world == 1 and not getattr(args, "no_cpu", False):
         line["cpu_baseline"] = cpu_decode(batch=1, ctx_len=prompt_len)
     return line
 
 
-DECODER_PHASES = ("qkv", "attention", "combine", "o", "gate_up", "down", "ple_gate", "ple_proj")
-
-
-def _decoder_timeline(torch, m):
-    """One eager persistent step with its first CTA's globaltimer stamps on: per phase kind,
-    the mean time the CTA worked before each barrier and the mean time it then waited in it
-    (us), and the step's total.  Taken after the timed region (it advances the sequence)."""
-    lib = importlib.import_module("gemma4-js_b200._lib")
-    dec = m.decoder()
-    nb = 8 * m.cfg.layers + 1
-    buf = torch.zeros(2 * nb + 2, dtype=torch.int64, device="cuda")
-    lib.call("g4_decoder_set_timeline", dec.handle, C.c_void_p(buf.data_ptr()), buf.numel())
-    m.decode_step(batch=1)
+def _persistent_decode(torch, m, dist, K, W):
+    """The same decode measured through the persistent g4_decoder (one cooperative launch per
+    token, opt-in): the step time over K graph replays after W warm-ups, then one eager step
+    with the all-CTA timeline.  Runs after the operator path's timed region on the same
+    sequence; None when the model's shapes are outside the decoder's range."""
+    m.persistent, m._dec = True, None
+    if m.decoder() is None:
+        m.persistent = False
+        return None
+    m.capture_decode(batch=1)
+    for _ in range(W):
+        m.replay_decode()
+    dist.barrier()
     torch.cuda.synchronize()
-    lib.call("g4_decoder_set_timeline", dec.handle, None, 0)
-    t = buf.cpu().numpy().astype(np.float64) / 1e3
-    pairs = t[1:1 + 2 * nb].reshape(nb, 2)
-    passed = np.concatenate([[t[0]], pairs[:-1, 1]])
-    work, wait = pairs[:, 0] - passed, pairs[:, 1] - pairs[:, 0]
-    out = {"total_us": round(float(t[2 * nb + 1] - t[0]), 1), "barriers": nb,
-           "barrier_wait_us": round(float(wait.sum()), 1), "work_us": round(float(work.sum()), 1)}
-    for k, name in enumerate(DECODER_PHASES):
-        out[name] = {"work_us": round(float(work[k:nb - 1:8].mean()), 2), "wait_us": round(float(wait[k:nb - 1:8].mean()), 2)}
-    out["head"] = {"work_us": round(float(work[-1]), 2), "wait_us": round(float(wait[-1]), 2),
-                   "tail_us": round(float(t[2 * nb + 1] - pairs[-1, 1]), 2)}
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(K):
+        m.replay_decode()
+    e.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = dist.max(s.elapsed_time(e)) / K
+    m.ctx.check_device()
+    out = {"kernel": "decode_step_kernel: the whole token in one cooperative launch (148 CTAs, grid barriers)",
+           "ms_per_step": round(ms, 4), "value": round(1e3 / ms * dist.world, 1), "unit": "tok/s",
+           "launches_per_step": _graph_kernel_count(m)}
+    out["timeline"] = _decoder_timeline(torch, m)
     return out
 
 
-# ------------------------------------------------------------ CPU baseline --
+def _decoder_timeline(torch, m):
+    """One eager persistent step with every CTA's globaltimer stamps on, summarised per phase
+    kind and averaged over the layers (us, medians over the CTAs): for each grid barrier the
+    arrival skew (last - first CTA) and its own latency (median pass - last arrival); for each
+    linear the wait for its weights and its compute; the attention tile's stages (CTAs with a
+    tile); and each row-wise operator.  Taken after the timed region (it advances the sequence)."""
+    lib = importlib.import_module("gemma4-js_b200._lib")
+    dec = m.decoder()
+    Lc = m.cfg.layers
+    per = 1 + 2 + 39 * Lc + 2 + 1
+    G = torch.cuda.get_device_properties(m.ctx.device).multi_processor_count
+    buf = torch.zeros((G, per), dtype=torch.int64, device=m.ctx.torch_device)
+    lib.call("g4_decoder_set_timeline", dec.handle, C.c_void_p(buf.data_ptr()), per)
+    m.decode_step(batch=1)
+    torch.cuda.synchronize()
+    lib.call("g4_decoder_set_timeline", dec.handle, None, 0)
+    m.ctx.check_device()
+    t = buf.cpu().numpy().astype(np.float64) / 1e3
+    t = t - t[:, 0].min()
+    acc = {}
+    state = {"i": 1, "prev": t[:, 0]}
+
+    def add(key, val):
+        acc.setdefault(key, []).append(float(val))
+
+    def lin(name):
+        i, prev = state["i"], state["prev"]
+        add(f"linear_{name}.weights_wait_us", np.median(t[:, i] - prev))
+        add(f"linear_{name}.compute_us", np.median(t[:, i + 1] - t[:, i]))
+        state["i"], state["prev"] = i + 2, t[:, i + 1]
+
+    def bar(name):
+        i = state["i"]
+        arrive, passed = t[:, i], t[:, i + 1]
+        add(f"barrier_{name}.skew_us", arrive.max() - arrive.min())
+        add(f"barrier_{name}.latency_us", np.median(passed) - arrive.max())
+        state["i"], state["prev"] = i + 2, passed
+
+    def op(name):
+        i, prev = state["i"], state["prev"]
+        add(f"op_{name}_us", np.median(t[:, i] - prev))
+        state["i"], state["prev"] = i + 1, t[:, i]
+
+    def attention():
+        i, prev = state["i"], state["prev"]
+        a = t[:, i:i + 4]
+        busy = (a[:, 3] - a[:, 0]) > 0
+        if busy.any():
+            add("attention_tile.q_ready_us", np.median(a[busy, 1] - a[busy, 0]))
+            add("attention_tile.kv_wait_us", np.median(a[busy, 2] - a[busy, 1]))
+            add("attention_tile.attend_us", np.median(a[busy, 3] - a[busy, 2]))
+            add("attention_tile.ctas", busy.sum())
+            tot = np.where(busy, a[:, 3] - prev, -1.0)
+            c = int(np.argmax(tot))
+            add("attention_tile.slowest_us", tot[c])
+            add("attention_tile.slowest_q_us", a[c, 1] - a[c, 0])
+            add("attention_tile.slowest_kv_us", a[c, 2] - a[c, 1])
+            add("attention_tile.slowest_attend_us", a[c, 3] - a[c, 2])
+            add("attention_tile.slowest_start_us", a[c, 0] - prev[c])
+            add("attention_tile.slowest_is_last_tile", float(c == int(busy.sum()) - 1))
+        state["i"], state["prev"] = i + 4, a[:, 3]
+
+    lin("top")
+    for _ in range(Lc):
+        lin("qkv"), bar("qkv"), attention(), bar("attention"), op("combine"), bar("combine"), op("load_attn")
+        lin("o"), bar("o"), op("post_norm_add_o")
+        lin("gate_up"), bar("gate_up"), op("load_act")
+        lin("down"), bar("down"), op("post_norm_add_down")
+        lin("ple_gate"), bar("ple_gate"), op("ple_mix_gelu")
+        lin("ple_proj"), bar("ple_proj"), op("post_norm_add_ple")
+    i = state["i"]
+    head_arrive = t[:, i]
+    out = {"total_us": round(float(np.median(t[:, per - 1])), 1), "ctas": G, "barriers": 8 * Lc + 1,
+           "head_us": round(float(np.median(head_arrive - state["prev"])), 1)}
+    for k, v in acc.items():
+        group, _, field = k.partition(".")
+        if field:
+            out.setdefault(group, {})[field] = round(float(np.mean(v)), 2)
+        else:
+            out[group] = round(float(np.mean(v)), 2)
+    return out
+
+
 def native_oracle():
     """The oracle's C restatement built for this host's CPU (-march=native)."""
     oracle = importlib.import_module("oracle")

@@ -6,8 +6,6 @@
 // dequantises the rows of a token batch straight into [T, 35, 256].
 #include <stdio.h>
 
-#include <algorithm>
-
 #include "g4_common.cuh"
 #include "g4_ple.cuh"
 
@@ -15,56 +13,49 @@ namespace {
 
 using namespace g4dev;
 
-// The T x words_per_row packed words of a gather form one flat range, split evenly over a
-// grid sized to the SMs' resident capacity, so every CTA finishes at the same time (one
-// CTA per token left a part-empty last wave: 4096 tokens are 2.3 waves).  Inside its range
-// a CTA's consecutive threads own consecutive words, so a warp loads 128 contiguous bytes
-// of nibbles (plus the 16 contiguous bytes of their 8 scales) and stores 512 contiguous
-// bytes of bf16 output per instruction; each thread issues the loads of kPleWords words
-// before decoding and storing them.  A word's token is idx / words_per_row, taken from a
-// float reciprocal and corrected by one step either way (idx < 2^24).
+// One CTA per token, one thread per packed 32-bit word (8 columns) at a time.  Consecutive
+// threads own consecutive words, so a warp loads 128 contiguous bytes of nibbles (plus the
+// 16 contiguous bytes of their 8 scales) and stores 512 contiguous bytes of bf16 output in
+// one instruction each.  Each thread first issues the loads of all kPleWords of its words,
+// then decodes and stores them (8960 columns = 1120 words = 160 threads x 7).
 //
 // Decode (ple-w4-shard-reader.js:89-95): column c is nibble (c & 1) of byte c >> 1,
 // i.e. bits 4c..4c+3 of the little-endian 32-bit word c >> 3; value = two's
 // complement nibble * f32(scale), exact in f32.
 constexpr int kPleThreads = 160;
-constexpr int kPleWords = 8;
+constexpr int kPleWords = 7;
 
 template <bool kF32Out>
 __global__ void __launch_bounds__(kPleThreads) ple_gather_kernel(const uint32_t* __restrict__ packed,
                                                                  const uint16_t* __restrict__ scales,
                                                                  const int32_t* __restrict__ ids, int vocab,
                                                                  int words_per_row, int groups_per_row,
-                                                                 long long total, float inv_wpr,
                                                                  void* __restrict__ out, uint32_t* err) {
     pdl_trigger();
     pdl_wait();
-    const long long begin = total * blockIdx.x / gridDim.x, end = total * (blockIdx.x + 1) / gridDim.x;
-    for (long long base = begin; base < end; base += kPleThreads * kPleWords) {
+    const int t = blockIdx.x;
+    const int id = __ldg(ids + t);
+    const bool ok = (unsigned)id < (unsigned)vocab;
+    if (!ok && threadIdx.x == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
+    const uint32_t* prow = packed + (size_t)(ok ? id : 0) * words_per_row;
+    const uint16_t* srow = scales + (size_t)(ok ? id : 0) * groups_per_row;
+    const size_t orow = (size_t)t * words_per_row;
+    for (int base = 0; base < words_per_row; base += kPleThreads * kPleWords) {
         uint32_t w[kPleWords], sb[kPleWords];
 #pragma unroll
         for (int k = 0; k < kPleWords; ++k) {
-            const long long idx = base + k * kPleThreads + threadIdx.x;
+            const int j = base + k * kPleThreads + threadIdx.x;
             w[k] = 0;
             sb[k] = 0;
-            if (idx < end) {
-                int t = __float2int_rz((float)idx * inv_wpr);
-                if ((long long)t * words_per_row > idx) --t;
-                if ((long long)(t + 1) * words_per_row <= idx) ++t;
-                const int j = (int)(idx - (long long)t * words_per_row);
-                const int id = __ldg(ids + t);
-                if ((unsigned)id < (unsigned)vocab) {
-                    w[k] = __ldg(packed + (size_t)id * words_per_row + j);
-                    sb[k] = __ldg(scales + (size_t)id * groups_per_row + (j >> 2));  // 4 words = one group
-                } else if (j == 0) {
-                    raise_error(err, G4_DEVERR_BAD_INDEX);  // zero row
-                }
+            if (ok && j < words_per_row) {
+                w[k] = __ldg(prow + j);
+                sb[k] = __ldg(srow + (j >> 2));  // 4 words = one group of 32 columns
             }
         }
 #pragma unroll
         for (int k = 0; k < kPleWords; ++k) {
-            const long long idx = base + k * kPleThreads + threadIdx.x;
-            if (idx >= end) continue;
+            const int j = base + k * kPleThreads + threadIdx.x;
+            if (j >= words_per_row) continue;
             if constexpr (!kF32Out) {
                 // bf16 out = RNE(q * s).  q * s is exact in f32, so rounding it once to bf16
                 // equals one correctly rounded bf16 multiply of the exact operands q and s.
@@ -87,17 +78,17 @@ __global__ void __launch_bounds__(kPleThreads) ple_gather_kernel(const uint32_t*
                 ov.y = __byte_perm(r[2], r[3], 0x5410);
                 ov.z = __byte_perm(r[0], r[1], 0x7632);
                 ov.w = __byte_perm(r[2], r[3], 0x7632);
-                reinterpret_cast<uint4*>(out)[idx] = ov;
+                reinterpret_cast<uint4*>(out)[orow + j] = ov;
             } else {
-                const float sc = bf16_bits_to_f32(sb[k]);
+                const float s = bf16_bits_to_f32(sb[k]);
                 float v[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     // ((n ^ 8) | 0x4B000000) as f32 = 2^23 + q + 8
                     const uint32_t m = ((w[k] >> (4 * e)) & 0xFu) ^ 0x4B000008u;
-                    v[e] = (__uint_as_float(m) - 8388616.0f) * sc;
+                    v[e] = (__uint_as_float(m) - 8388616.0f) * s;
                 }
-                float4* o = reinterpret_cast<float4*>(out) + idx * 2;
+                float4* o = reinterpret_cast<float4*>(out) + (orow + j) * 2;
                 o[0] = make_float4(v[0], v[1], v[2], v[3]);
                 o[1] = make_float4(v[4], v[5], v[6], v[7]);
             }
@@ -222,23 +213,13 @@ g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids
         d_ids = ctx->d_ids;
     }
     const int gpr = tab->width / 32, wpr = tab->width / 8;
-    const long long total = (long long)T * wpr;
-    if (total >= (1LL << 24))
-        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_ple_gather: %d tokens x %d words per row (< 2^24 words)", T, wpr);
     const uint32_t* p = reinterpret_cast<const uint32_t*>(tab->packed);
-    // every CTA resident at once: the SMs' capacity of 160-thread CTAs, fewer for short gathers
-    const long long per_sm = 2048 / kPleThreads;
-    long long blocks = std::min<long long>((long long)ctx->num_sms * per_sm, (total + kPleThreads - 1) / kPleThreads);
-    if (blocks < 1) blocks = 1;
-    const dim3 grid((unsigned)blocks), block(kPleThreads);
-    const float inv_wpr = 1.0f / (float)wpr;
+    const dim3 grid((unsigned)T), block(kPleThreads);
     if (out_dtype == G4_BF16)
         return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false>, grid, block, 0, 1, p,
-                          static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, total, inv_wpr, out,
-                          ctx->d_err);
+                          static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
     return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true>, grid, block, 0, 1, p,
-                      static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, total, inv_wpr, out,
-                      ctx->d_err);
+                      static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
 }
 
 }  // extern "C"

@@ -386,9 +386,13 @@ g4_status g4_decoder_step(g4_ctx* ctx, g4_decoder* dec, const int32_t* ids, int3
 /* After a step reported G4_ERR_TIMEOUT (g4_ctx_check_device): clears the decoder's grid
  * barrier words so the next step starts clean.  Synchronises the context stream. */
 g4_status g4_decoder_reset(g4_decoder* dec);
-/* Tracing hook (no reference counterpart): while timeline is set, every step writes up to
- * `entries` globaltimer stamps (ns) of its first CTA into that device buffer: the start,
- * then an (arrive, pass) pair per grid barrier, then the end.  NULL switches it off. */
+/* Tracing hook (no reference counterpart): while timeline is set, every step writes globaltimer
+ * stamps (ns) into that device buffer, `entries` per CTA (row c of a [CTAs][entries] array;
+ * the step runs one CTA per SM): the start, then in program order a (weights ready, linear done)
+ * pair per linear, an (arrive, pass) pair per grid barrier, four stamps per layer's attention
+ * tile (requested, q ready, K/V in, done; all four at once without a tile) and one after each
+ * row-wise operator (combine, attention load, norms, activation load, PLE mix), then the end.  NULL switches it off.  A step already captured in a CUDA
+ * graph keeps the setting it was captured with. */
 g4_status g4_decoder_set_timeline(g4_decoder* dec, unsigned long long* timeline, int entries);
 
 #ifdef __cplusplus

@@ -52,7 +52,7 @@ def test_persistent_decoder_matches_exact_oracle(rt, ctx, cfg_kw, seed):
     rng = np.random.default_rng(seed)
     prompt = [int(t) for t in rng.integers(0, cfg.vocab, 24)]
     forced = rng.integers(0, cfg.vocab, 40)
-    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=80, max_rows=32)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=80, max_rows=32, persistent=True)
     assert gpu.decoder() is not None
     orc = mo.OracleModel(cfg, w, max_seq=80, gemm_rows=mo.EXACT)
     tally = Tally()
@@ -82,7 +82,7 @@ def test_persistent_decoder_reference_spec(rt, ctx):
     rng = np.random.default_rng(43)
     prompt = [int(t) for t in rng.integers(0, cfg.vocab, 20)]
     forced = rng.integers(0, cfg.vocab, 24)
-    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=32)
+    gpu = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=32, persistent=True)
     assert gpu.decoder() is not None
     orc = mo.OracleModel(cfg, w, max_seq=64, gemm_rows=mo.EXACT)
     tally = Tally()
@@ -126,7 +126,7 @@ def test_persistent_graph_replay_is_bitwise_eager(rt, ctx):
     prompt = [3, 1, 4, 1, 5, 9, 2, 6]
     res = []
     for graph in (False, True):
-        m = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16)
+        m = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=64, max_rows=16, persistent=True)
         first = m.prefill(0, prompt)
         m.buf["next"][0] = first
         ids, vals = [], []
@@ -149,7 +149,7 @@ def test_persistent_decoder_position_past_cache_is_reported(rt, ctx):
     error word, next id 0, nothing written, no barrier entered), and the decoder keeps working."""
     cfg = small_cfg()
     w = model.random_weights(cfg, seed=46, **FULL_KW)
-    m = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=32, max_rows=16)
+    m = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=32, max_rows=16, persistent=True)
     m.prefill(0, [7, 8, 9])
     good = m.seq_pos.clone()
     m.seq_pos[0] = 32
@@ -169,7 +169,7 @@ def test_unsupported_shapes_fall_back_to_the_operators(rt, ctx):
     the model decodes through the operators instead."""
     cfg = small_cfg(hidden=320)
     w = model.random_weights(cfg, seed=47, **FULL_KW)
-    m = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=32, max_rows=16)
+    m = model.Gemma4Model(ctx, cfg, w, max_batch=1, max_seq=32, max_rows=16, persistent=True)
     assert m.decoder() is None
     m.prefill(0, [1, 2, 3])
     nxt = m.decode_step(ids_dev=torch.tensor([4], dtype=torch.int32, device="cuda"), batch=1)

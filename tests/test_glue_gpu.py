@@ -292,7 +292,7 @@ def test_fused_head_pick_matches_oracle_softcap_and_tie_rule(rt, ctx, oracle):
     rule are under test.  Planted cases per row: exact ties of the maximum at several
     indices; saturated logits (raw >= 600, where the capped value is exactly 30.0 for every
     raw) with the largest raw at a higher index than a smaller saturated one; and a
-    near-cap maximum (raw 80.25 against 80.0) that must stay distinct.  The kernel computes
+    near-cap maximum (raw 80.5 against 80.0) that must stay distinct.  The kernel computes
     the softcap only when a raw maximum improves, which equals this rule for a
     non-decreasing softcap."""
     model = importlib.import_module("gemma4-js_b200.model")
@@ -311,7 +311,7 @@ def test_fused_head_pick_matches_oracle_softcap_and_tie_rule(rt, ctx, oracle):
             col[idx[0]], col[idx[1]], col[idx[2]] = 600.0, 1024.0, 2048.0
         elif kind == 2:  # near the cap but distinct
             idx = np.sort(rng.choice(V, 2, replace=False))
-            col[idx[0]], col[idx[1]] = 80.0, 80.25
+            col[idx[0]], col[idx[1]] = 80.0, 80.5
         capped = np.tanh(col / np.float32(30.0)).astype(np.float32) * np.float32(30.0)
         expect.append(int(np.argmax(capped)))   # numpy argmax: the lowest index of the maximum
     assert np.array_equal(bf16_round(E), E)
