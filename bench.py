@@ -928,7 +928,7 @@ def _extras(args, torch, rt, ctx, dist, peaks) -> dict:
         keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "roofline", "clocks", "e2e", "config",
                 "us_per_call", "gpu_launches")
         out = {k: ln[k] for k in keep if k in ln}
-        for k in ("sweep", "decode_shape_sweep", "wide_gemv"):
+        for k in ("sweep", "decode_shape_sweep", "wide_gemv", "persistent_decoder", "launches_per_step"):
             if k in ln:
                 out[k] = ln[k]
         torch.cuda.empty_cache()

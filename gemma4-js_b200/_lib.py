@@ -95,6 +95,8 @@ SIGNATURES = {
     "g4_ple_gather": (_S, [_P, _P, _P, _I, _I, _P, _I]),
     "g4_kv_create": (_S, [_P, _I, _I, _PP]),
     "g4_kv_destroy": (_S, [_P]),
+    "g4_kv_create_ring": (_S, [_P, _I, _I, _I, _I, _PP]),
+    "g4_kv_layout": (_S, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
     "g4_kv_append": (_S, [_P, _P, _P, _P, _I, _I, _I]),
     "g4_kv_info": (_S, [_P, C.POINTER(_I), C.POINTER(_I), C.POINTER(_I)]),
     "g4_kv_reset": (_S, [_P]),
@@ -119,6 +121,7 @@ SIGNATURES = {
     "g4_dense_argmax": (_S, [_P, _P, _P, _I, _F, _P, _P]),
     "g4_post_norm_add_planes": (_S, [_P, _P, _P, _P, _F, _P, _I, _I, _F, _P]),
     "g4_qkv_post_planes": (_S, [_P, _P, _I, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P, _P, _I]),
+    "g4_qkv_post_kv": (_S, [_P, _P, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P]),
     "g4_gelu_mul_planes": (_S, [_P, _P, _I, _I, _P]),
     "g4_gelu_ple_planes": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "g4_ple_mix": (_S, [_P, _P, _F, _P, _P, _I, _I, _I, _F, _P]),

@@ -13,6 +13,7 @@
 // second wave starts cold behind the first.
 #include <stdio.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "g4_attention.cuh"
@@ -51,6 +52,7 @@ struct AttnParams {
     float2* part_ml;        // [rows, nsplit, 8]       (nsplit > 1)
     uint32_t* err;
     int heads, keylen, qpos0, sliding, window;
+    int ring;                // ring cache: key j sits in row kv_row0 + j % ring (mirrored past the ring)
     int nsplit, split_keys;  // keys per split (multiple of KT)
     int kv_row0;             // first cache row of this sequence in the tensor map
     // Device-side positions (g4_rows): when seq_pos is set, row r belongs to sequence
@@ -131,7 +133,8 @@ attn_decode_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_consta
                 if (t >= C::STAGES) ok = mbar_wait(&empty[s], ((t / C::STAGES) - 1) & 1, p.err);
                 if (!ok) break;
                 mbar_arrive_expect_tx(&full[s], 2 * C::TILE_BYTES);
-                const int y = kv_row0 + s_lo + t * C::KT;
+                const int j0 = s_lo + t * C::KT;
+                const int y = kv_row0 + (p.ring ? j0 % p.ring : j0);
 #pragma unroll
                 for (int b = 0; b < C::BOXES; ++b) {
                     tma_load_2d(kst + s * C::TILE_BYTES + b * C::BOX_BYTES, &kmap, &full[s], b * 64, y);
@@ -353,11 +356,35 @@ __global__ void kv_append_f32_kernel(const float* __restrict__ k, const float* _
     vc[i] = (uint16_t)f32_to_bf16_bits(v[i]);
 }
 
+// KVCache.append into a ring cache: row i of k/v (f32 or bf16) is position start + i, slot
+// (start + i) % ring, also written to row ring + slot when slot < mirror.  Only the last
+// `ring` rows are written (earlier ones would be overwritten by later rows of the call).
+__global__ void kv_append_ring_kernel(const void* __restrict__ k, const void* __restrict__ v, int src_f32, int rows,
+                                      int start, int hd, int ring, int mirror, uint16_t* __restrict__ kc,
+                                      uint16_t* __restrict__ vc) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const int first = rows > ring ? rows - ring : 0;
+    if (i >= (long long)(rows - first) * hd) return;
+    const int r = first + (int)(i / hd), d = (int)(i % hd);
+    const size_t src = (size_t)r * hd + d;
+    const uint16_t kb = src_f32 ? (uint16_t)f32_to_bf16_bits(static_cast<const float*>(k)[src])
+                                : static_cast<const uint16_t*>(k)[src];
+    const uint16_t vb = src_f32 ? (uint16_t)f32_to_bf16_bits(static_cast<const float*>(v)[src])
+                                : static_cast<const uint16_t*>(v)[src];
+    const int slot = (start + r) % ring;
+    kc[(size_t)slot * hd + d] = kb;
+    vc[(size_t)slot * hd + d] = vb;
+    if (slot < mirror) {
+        kc[(size_t)(ring + slot) * hd + d] = kb;
+        vc[(size_t)(ring + slot) * hd + d] = vb;
+    }
+}
+
 template <int HD, bool kNarrow>
 g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& vm, const uint16_t* q,
                         int rows, int heads, int keylen, int qpos0, int sliding, int window, uint16_t* out,
-                        int kv_row0, void* fixed_scratch = nullptr, size_t fixed_bytes = 0,
-                        const g4_rows* map = nullptr, int seq_stride = 0) {
+                        int kv_row0, void* fixed_scratch, size_t fixed_bytes, const g4_rows* map, int seq_stride,
+                        int ring) {
     using C = AttnCfg<HD, kNarrow>;
     // Longest key range of any row decides the split.  With device-side positions the
     // host does not know the lengths: plan for a full sequence (or a full window).
@@ -393,6 +420,7 @@ g4_status launch_attn_t(g4_ctx* ctx, const CUtensorMap& km, const CUtensorMap& v
     p.qpos0 = qpos0;
     p.sliding = sliding;
     p.window = window;
+    p.ring = ring;
     p.nsplit = nsplit;
     p.split_keys = tiles_per_split * C::KT;
     p.kv_row0 = kv_row0;
@@ -463,9 +491,9 @@ g4_status launch_attn_hd(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16
     // long key ranges, where the wide tiles measured faster.)
     if (map && sliding && rows > ctx->num_sms)
         return launch_attn_t<HD, true>(ctx, kv->kmap_narrow, kv->vmap_narrow, q, rows, heads, keylen, qpos0, sliding,
-                                       window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+                                       window, out, kv_row0, fixed_scratch, fixed_bytes, map, seq_stride, kv->ring);
     return launch_attn_t<HD, false>(ctx, kv->kmap, kv->vmap, q, rows, heads, keylen, qpos0, sliding, window, out,
-                                    kv_row0, fixed_scratch, fixed_bytes, map, seq_stride);
+                                    kv_row0, fixed_scratch, fixed_bytes, map, seq_stride, kv->ring);
 }
 
 g4_status launch_attention(g4_ctx* ctx, const g4_kv* kv, int kv_row0, const uint16_t* q, int rows, int heads,
@@ -516,6 +544,56 @@ g4_status g4_kv_create(g4_ctx* ctx, int hd, int capacity, g4_kv** out) {
     return G4_OK;
 }
 
+g4_status g4_kv_create_ring(g4_ctx* ctx, int hd, int capacity, int ring, int nseq, g4_kv** out) {
+    if (!out) return g4::set_error(G4_ERR_INVALID, "g4_kv_create_ring: null out");
+    *out = nullptr;
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (hd != 64 && hd != 128 && hd != 256 && hd != 512)
+        return g4::set_error(G4_ERR_UNSUPPORTED, "g4_kv_create_ring: head dim %d (64/128/256/512 supported)", hd);
+    const int mirror = 16384 / hd;
+    if (capacity <= 0 || nseq <= 0) return g4::set_error(G4_ERR_INVALID, "g4_kv_create_ring: capacity %d, %d sequences",
+                                                         capacity, nseq);
+    if (ring < mirror)
+        return g4::set_error(G4_ERR_INVALID, "g4_kv_create_ring: ring of %d slots (at least %d at head dim %d)", ring,
+                             mirror, hd);
+    if ((long long)nseq * (ring + mirror) > 0x7fffffffLL)
+        return g4::set_error(G4_ERR_RANGE, "g4_kv_create_ring: %d sequences x %d rows", nseq, ring + mirror);
+    g4_kv* kv = new g4_kv();
+    kv->ctx = ctx;
+    kv->hd = hd;
+    kv->capacity = capacity;
+    kv->ring = ring;
+    kv->mirror = mirror;
+    kv->nseq = nseq;
+    kv->seq_rows = ring + mirror;
+    kv->rows_total = nseq * kv->seq_rows;
+    const size_t bytes = (size_t)kv->rows_total * hd * 2;
+    cudaError_t e = cudaMalloc(&kv->k, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&kv->v, bytes);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->k, 0, bytes, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->v, 0, bytes, ctx->stream);
+    if (e != cudaSuccess) {
+        g4_kv_destroy(kv);
+        return g4::cuda_error(e, "g4_kv_create_ring");
+    }
+    st = g4::make_kv_maps(kv);
+    if (st) {
+        g4_kv_destroy(kv);
+        return st;
+    }
+    *out = kv;
+    return G4_OK;
+}
+
+g4_status g4_kv_layout(const g4_kv* kv, int* ring, int* seq_rows, int* nseq) {
+    if (!kv) return g4::set_error(G4_ERR_INVALID, "null kv");
+    if (ring) *ring = kv->ring;
+    if (seq_rows) *seq_rows = kv->ring ? kv->seq_rows : kv->rows_total;
+    if (nseq) *nseq = kv->nseq;
+    return G4_OK;
+}
+
 g4_status g4_kv_destroy(g4_kv* kv) {
     if (!kv) return G4_OK;
     if (kv->ctx) {
@@ -539,6 +617,20 @@ g4_status g4_kv_append(g4_ctx* ctx, g4_kv* kv, const void* k, const void* v, int
     if (rows < 0 || start_pos + rows > kv->capacity)
         return g4::set_error(G4_ERR_RANGE, "KV cache capacity %d exceeded", kv->capacity);
     if (rows == 0) return G4_OK;
+    if (kv->ring) {
+        if (kv->nseq != 1)
+            return g4::set_error(G4_ERR_INVALID, "g4_kv_append: ring cache of %d sequences (append K/V with "
+                                 "g4_qkv_post_kv)", kv->nseq);
+        if (src_dtype != G4_BF16 && src_dtype != G4_F32)
+            return g4::set_error(G4_ERR_INVALID, "g4_kv_append: dtype %d", (int)src_dtype);
+        const long long n = (long long)std::min(rows, kv->ring) * kv->hd;
+        st = g4::launch(ctx, "kv_append_ring_kernel", kv_append_ring_kernel, dim3((unsigned)((n + 255) / 256)),
+                        dim3(256), 0, 1, k, v, src_dtype == G4_F32 ? 1 : 0, rows, start_pos, kv->hd, kv->ring,
+                        kv->mirror, kv->k, kv->v);
+        if (st) return st;
+        kv->length += rows;
+        return G4_OK;
+    }
     const size_t n = (size_t)rows * kv->hd;
     uint16_t* kd = kv->k + (size_t)start_pos * kv->hd;
     uint16_t* vd = kv->v + (size_t)start_pos * kv->hd;
@@ -581,6 +673,8 @@ g4_status g4_kv_buffers(const g4_kv* kv, void** k, void** v) {
 
 namespace g4 {
 
+g4_status check_ring(const char* name, const g4_kv* kv, int sliding, int window, int span);
+
 // The argument rules of GPUOps.attention with host-side positions, shared by g4_attention
 // and g4_attention_noalloc (`name` prefixes the messages).  *empty is set when rows == 0.
 g4_status check_attention_args(const char* name, g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, int rows,
@@ -606,6 +700,21 @@ g4_status check_attention_args(const char* name, g4_ctx* ctx, const void* q_bf16
     if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "%s: window %d", name, window);
     if (reinterpret_cast<uintptr_t>(q_bf16) % 16 != 0)
         return g4::set_error(G4_ERR_INVALID, "%s: q must be 16-byte aligned", name);
+    return check_ring(name, kv, sliding, window, keylen - qpos0);
+}
+
+// A ring cache holds the last `ring` positions of each sequence: it serves sliding-window
+// attention whose queries, with `span` = keylen - first query position, never reach back
+// further than that (span + window - 1 <= ring).
+g4_status check_ring(const char* name, const g4_kv* kv, int sliding, int window, int span) {
+    if (!kv->ring) return G4_OK;
+    if (!sliding)
+        return g4::set_error(G4_ERR_INVALID, "%s: a ring KV cache (%d slots) serves sliding-window attention only",
+                             name, kv->ring);
+    if ((long long)span + window - 1 > kv->ring)
+        return g4::set_error(G4_ERR_RANGE,
+                             "%s: %d query positions with a window of %d need %lld ring slots; the cache has %d",
+                             name, span, window, (long long)span + window - 1, kv->ring);
     return G4_OK;
 }
 
@@ -638,6 +747,11 @@ g4_status g4_attention_rows(g4_ctx* ctx, const void* q_bf16, const g4_kv* kv, in
     if (seq_stride < 1 || (long long)(map->seq_base + (rows - 1) / map->rows_per_seq + 1) * seq_stride > kv->rows_total)
         return g4::set_error(G4_ERR_RANGE, "g4_attention_rows: sequences beyond the cache (%d rows)", kv->rows_total);
     if (sliding && window < 1) return g4::set_error(G4_ERR_INVALID, "g4_attention_rows: window %d", window);
+    if (kv->ring && seq_stride != kv->seq_rows)
+        return g4::set_error(G4_ERR_INVALID, "g4_attention_rows: seq_stride %d of a ring cache must be its %d rows per "
+                             "sequence", seq_stride, kv->seq_rows);
+    st = g4::check_ring("g4_attention_rows", kv, sliding, window, map->rows_per_seq);
+    if (st) return st;
     return g4::launch_attention(ctx, kv, 0, static_cast<const uint16_t*>(q_bf16), rows, heads, 0, 0, sliding ? 1 : 0,
                                 window, static_cast<uint16_t*>(out_bf16), nullptr, 0, map, seq_stride);
 }

@@ -1155,6 +1155,10 @@ g4_status g4_decoder_create(g4_ctx* ctx, const g4_decoder_desc* desc, const g4_d
         void *kb = nullptr, *vb = nullptr;
         g4_kv_info(a.kv, &len, &hd, &kcap);
         g4_kv_buffers(a.kv, &kb, &vb);
+        int ring = 0;
+        g4_kv_layout(a.kv, &ring, nullptr, nullptr);
+        if (ring)  // the decoder addresses keys by position
+            return fail(g4::set_error(G4_ERR_UNSUPPORTED, "g4_decoder_create: layer %d has a ring KV cache", l));
         if (hd != 256 && hd != 512)
             return fail(g4::set_error(G4_ERR_UNSUPPORTED, "g4_decoder_create: layer %d head dim %d", l, hd));
         if (a.inter < 64 || a.inter % 64 != 0)

@@ -13,6 +13,7 @@
 // so a captured decode step replays correctly as positions advance.
 #include <stdio.h>
 
+#include "g4_attention.cuh"
 #include "g4_common.cuh"
 #include "g4_glue.cuh"
 
@@ -182,10 +183,29 @@ __global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __re
 
 // Destination row of (row r, slot) and the output pair (i, i + hd/2) of one rotation
 // pair a0 = y[i], a1 = y[i + hd/2] once the head's 1/rms is known.
+// Where the K/V rows go: sequence seq's rows start at seq * cache_cap; a linear cache keeps
+// position pos in row pos (pos < pos_limit), a ring cache in slot pos % ring and, for slots
+// below `mirror`, again in row ring + slot.
+struct KvSink {
+    uint16_t *kcache, *vcache;
+    int cache_cap, ring, mirror, pos_limit;
+    uint32_t* err;
+};
 __device__ __forceinline__ uint16_t* qkv_dst(int slot, int H, int hd, int r, const G4Rows& R, int pos,
-                                             uint16_t* q_out, uint16_t* kcache, uint16_t* vcache, int cache_cap) {
+                                             uint16_t* q_out, const KvSink& kv, uint16_t** mirror_dst) {
+    *mirror_dst = nullptr;
     if (slot < H) return q_out + ((size_t)r * H + slot) * hd;
-    return (slot == H ? kcache : vcache) + ((size_t)row_seq(R, r) * cache_cap + pos) * hd;
+    uint16_t* base = (slot == H ? kv.kcache : kv.vcache) + (size_t)row_seq(R, r) * kv.cache_cap * hd;
+    if (!kv.ring) return base + (size_t)pos * hd;
+    const int s = pos % kv.ring;
+    if (s < kv.mirror) *mirror_dst = base + (size_t)(kv.ring + s) * hd;
+    return base + (size_t)s * hd;
+}
+// A K/V row at or past the cache capacity is not written; it raises the device error word.
+__device__ __forceinline__ bool kv_row_ok(int slot, int H, int pos, const KvSink& kv) {
+    if (slot < H || (pos >= 0 && pos < kv.pos_limit)) return true;
+    if (kv.err) atomicOr(kv.err, G4_DEVERR_BAD_INDEX);
+    return false;
 }
 __device__ __forceinline__ float2 qkv_pair(int slot, int H, int hd, int i, float a0, float a1, float inv,
                                            const float* __restrict__ qnorm, const float* __restrict__ knorm,
@@ -206,8 +226,7 @@ __device__ __forceinline__ float2 qkv_pair(int slot, int H, int hd, int i, float
 // (i, i + hd/2).
 __global__ void qkv_post_kernel(Planes y, int H, int hd, int has_kv,
                                 const float* __restrict__ qnorm, const float* __restrict__ knorm, float eps,
-                                int rope_angles, float rope_base, G4Rows R, uint16_t* __restrict__ q_out,
-                                uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache, int cache_cap) {
+                                int rope_angles, float rope_base, G4Rows R, uint16_t* __restrict__ q_out, KvSink kv) {
     pdl_trigger();
     pdl_wait();
     __shared__ float red[32];
@@ -219,9 +238,16 @@ __global__ void qkv_post_kernel(Planes y, int H, int hd, int has_kv,
     const float inv = rsqrtf(block_sum(a0 * a0 + a1 * a1, red) / (float)hd + eps);
     const int pos = row_position(R, r);
     const float2 o = qkv_pair(slot, H, hd, i, a0, a1, inv, qnorm, knorm, rope_angles, rope_base, pos);
-    uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kcache, vcache, cache_cap);
-    dst[i] = (uint16_t)f32_to_bf16_bits(o.x);
-    dst[i + half] = (uint16_t)f32_to_bf16_bits(o.y);
+    if (!kv_row_ok(slot, H, pos, kv)) return;
+    uint16_t* dst2;
+    uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kv, &dst2);
+    const uint16_t b0 = (uint16_t)f32_to_bf16_bits(o.x), b1 = (uint16_t)f32_to_bf16_bits(o.y);
+    dst[i] = b0;
+    dst[i + half] = b1;
+    if (dst2) {
+        dst2[i] = b0;
+        dst2[i + half] = b1;
+    }
 }
 
 // hd = 256 * NF: one warp per (row, head slot), 8 per CTA, so a decode batch is a few
@@ -234,8 +260,7 @@ template <int NF>
 __global__ void __launch_bounds__(kQkvWarps * 32)
 qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restrict__ qnorm,
                      const float* __restrict__ knorm, float eps, int rope_angles, float rope_base, G4Rows R,
-                     uint16_t* __restrict__ q_out, uint16_t* __restrict__ kcache, uint16_t* __restrict__ vcache,
-                     int cache_cap) {
+                     uint16_t* __restrict__ q_out, KvSink kv) {
     constexpr int hd = 256 * NF, half = hd / 2, G = 2 * NF;  // float4 groups per lane
     constexpr int PB = NF <= 2 ? 4 : 2;                        // slices per load batch
     pdl_trigger();
@@ -279,7 +304,9 @@ qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restr
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     const float inv = rsqrtf(ss / (float)hd + eps);
     const int pos = row_position(R, r);
-    uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kcache, vcache, cache_cap);
+    if (!kv_row_ok(slot, H, pos, kv)) return;
+    uint16_t* dst2;
+    uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kv, &dst2);
 #pragma unroll
     for (int f = 0; f < NF; ++f) {
         const int i0 = 4 * (lane + 32 * f);
@@ -291,9 +318,14 @@ qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restr
             o0[c] = o.x;
             o1[c] = o.y;
         }
-        *reinterpret_cast<uint2*>(dst + i0) = make_uint2(pack_bf16x2_bits(o0[0], o0[1]), pack_bf16x2_bits(o0[2], o0[3]));
-        *reinterpret_cast<uint2*>(dst + i0 + half) =
-            make_uint2(pack_bf16x2_bits(o1[0], o1[1]), pack_bf16x2_bits(o1[2], o1[3]));
+        const uint2 lo2 = make_uint2(pack_bf16x2_bits(o0[0], o0[1]), pack_bf16x2_bits(o0[2], o0[3]));
+        const uint2 hi2 = make_uint2(pack_bf16x2_bits(o1[0], o1[1]), pack_bf16x2_bits(o1[2], o1[3]));
+        *reinterpret_cast<uint2*>(dst + i0) = lo2;
+        *reinterpret_cast<uint2*>(dst + i0 + half) = hi2;
+        if (dst2) {
+            *reinterpret_cast<uint2*>(dst2 + i0) = lo2;
+            *reinterpret_cast<uint2*>(dst2 + i0 + half) = hi2;
+        }
     }
 }
 
@@ -535,9 +567,14 @@ g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, co
                       static_cast<uint16_t*>(x_out_bf16), ctx->d_err);
 }
 
-g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd, int has_kv, const float* qnorm,
-                             const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
-                             int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap) {
+}  // extern "C"
+
+namespace {
+
+g4_status qkv_post_impl(g4_ctx* ctx, const g4_planes* y, int heads, int hd, int has_kv, const float* qnorm,
+                        const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
+                        int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap, int ring,
+                        int mirror, int pos_limit) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;
     if (rows < 0 || !planes_ok(y) || !qnorm || !rows_map || !q_out_bf16 ||
@@ -553,17 +590,44 @@ g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd,
     const long long units = (long long)rows * (heads + (has_kv ? 2 : 0));
     const dim3 wgrid((unsigned)((units + kQkvWarps - 1) / kQkvWarps)), wblock(kQkvWarps * 32);
     uint16_t* qo = static_cast<uint16_t*>(q_out_bf16);
-    uint16_t* kc = static_cast<uint16_t*>(kcache_bf16);
-    uint16_t* vc = static_cast<uint16_t*>(vcache_bf16);
+    const KvSink kv{static_cast<uint16_t*>(kcache_bf16), static_cast<uint16_t*>(vcache_bf16), cache_cap, ring, mirror,
+                    pos_limit, ctx->d_err};
     if (f4 && hd == 256)
         return g4::launch(ctx, "qkv_post_warp_kernel", qkv_post_warp_kernel<1>, wgrid, wblock, 0, 1, P, heads, has_kv,
-                          rows, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kc, vc, cache_cap);
+                          rows, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kv);
     if (f4 && hd == 512)
         return g4::launch(ctx, "qkv_post_warp_kernel", qkv_post_warp_kernel<2>, wgrid, wblock, 0, 1, P, heads, has_kv,
-                          rows, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kc, vc, cache_cap);
+                          rows, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kv);
     return g4::launch(ctx, "qkv_post_kernel", qkv_post_kernel, dim3(heads + (has_kv ? 2 : 0), rows), dim3(hd / 2), 0,
-                      1, P, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kc, vc,
-                      cache_cap);
+                      1, P, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, *rows_map, qo, kv);
+}
+
+}  // namespace
+
+extern "C" {
+
+g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd, int has_kv, const float* qnorm,
+                             const float* knorm, float eps, int rope_angles, float rope_base, const G4Rows* rows_map,
+                             int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap) {
+    if (has_kv && cache_cap < 1) return g4::set_error(G4_ERR_INVALID, "g4_qkv_post: cache_cap %d", cache_cap);
+    return qkv_post_impl(ctx, y, heads, hd, has_kv, qnorm, knorm, eps, rope_angles, rope_base, rows_map, rows,
+                         q_out_bf16, kcache_bf16, vcache_bf16, cache_cap, 0, 0, cache_cap);
+}
+
+g4_status g4_qkv_post_kv(g4_ctx* ctx, const g4_planes* y, int heads, int hd, const float* qnorm, const float* knorm,
+                         float eps, int rope_angles, float rope_base, const G4Rows* rows_map, int rows,
+                         void* q_out_bf16, const g4_kv* kv) {
+    if (!kv)
+        return qkv_post_impl(ctx, y, heads, hd, 0, qnorm, knorm, eps, rope_angles, rope_base, rows_map, rows,
+                             q_out_bf16, nullptr, nullptr, 1, 0, 0, 1);
+    if (hd != kv->hd) return g4::set_error(G4_ERR_INVALID, "g4_qkv_post_kv: hd %d != cache hd %d", hd, kv->hd);
+    if (!rows_map || rows_map->rows_per_seq < 1) return g4::set_error(G4_ERR_INVALID, "g4_qkv_post_kv: bad row map");
+    const int seq_rows = kv->ring ? kv->seq_rows : kv->rows_total;
+    if (rows > 0 && (long long)(rows_map->seq_base + (rows - 1) / rows_map->rows_per_seq + 1) * seq_rows >
+                        kv->rows_total)
+        return g4::set_error(G4_ERR_RANGE, "g4_qkv_post_kv: sequences beyond the cache (%d rows)", kv->rows_total);
+    return qkv_post_impl(ctx, y, heads, hd, 1, qnorm, knorm, eps, rope_angles, rope_base, rows_map, rows, q_out_bf16,
+                         kv->k, kv->v, seq_rows, kv->ring, kv->mirror, kv->ring ? kv->capacity : seq_rows);
 }
 
 g4_status g4_qkv_post(g4_ctx* ctx, const float* y, int ldy, int heads, int hd, int has_kv, const float* qnorm,

@@ -284,10 +284,15 @@ class Gemma4Model:
     persistent g4_decoder launch instead of the ~430 operator launches of the op path
     (prefill and batched decode always use the operators).  Off by default: on B200 the
     operator chain with programmatic dependent launch measures faster (1.6 vs 3.0 ms per
-    token at config 4), the persistent step paying ~10 us per grid-barrier phase."""
+    token at config 4), the persistent step paying ~10 us per grid-barrier phase.
+
+    ring_kv: the caches of sliding-window layers keep each sequence's last window +
+    max_rows - 1 positions (g4_kv_create_ring; the Node reference trims its sliding caches
+    to the window, node-reference/src/attention.js:299-305) whenever that is smaller than
+    max_seq; global layers keep every position."""
 
     def __init__(self, ctx: Context, cfg: ModelConfig, w: dict, max_batch: int = 1, max_seq: int = 512,
-                 max_rows: int | None = None, pdl: bool = True, persistent: bool = False):
+                 max_rows: int | None = None, pdl: bool = True, persistent: bool = False, ring_kv: bool = True):
         self.ctx, self.cfg = ctx, cfg
         self.persistent = persistent and max_batch == 1
         self._dec = None
@@ -309,11 +314,13 @@ class Gemma4Model:
                                name=f"layers.{i}.gu")
             for n in ("n_in", "n_pa", "n_pf", "n_pff", "n_pple", "qn", "kn"):
                 L[n] = _dev_f32(lw[n], dev)
-            L["kv"] = None if s["shared"] else KVCache(ctx, s["hd"], max_batch * max_seq)
+            L["kv"] = None if s["shared"] else self._cache(s, ring_kv)
             self.layers.append(L)
         for L in self.layers:
             if L["spec"]["shared"]:
-                L["kv"] = self.layers[L["spec"]["kv_src"]]["kv"]
+                src = self.layers[L["spec"]["kv_src"]]
+                assert src["spec"]["full"] == L["spec"]["full"], "a KV-shared layer reads a cache of its own kind"
+                L["kv"] = src["kv"]
         self.top = W4Linear(ctx, w["top"][0], w["top"][1], name="per_layer_model_projection")
         self.ple_norm = _dev_f32(w["ple_norm"], dev)
         self.final_norm = _dev_f32(w["final_norm"], dev)
@@ -323,6 +330,20 @@ class Gemma4Model:
         self._alloc(self.max_rows)
         self.graph = None
         self._capturing = False
+
+    def _cache(self, spec: dict, ring_kv: bool) -> KVCache:
+        """A layer's cache: a ring of window + max_rows - 1 slots per sequence for a sliding
+        layer when that saves memory (a prefill of up to max_rows tokens then still finds
+        every key its rows' windows need), else max_seq rows per sequence."""
+        hd = spec["hd"]
+        ring = max(self.cfg.window + self.max_rows - 1, 16384 // hd)
+        if ring_kv and not spec["full"] and ring + 16384 // hd < self.max_seq:
+            return KVCache(self.ctx, hd, self.max_seq, ring=ring, nseq=self.max_batch)
+        return KVCache(self.ctx, hd, self.max_batch * self.max_seq)
+
+    def kv_stride(self, kv: KVCache) -> int:
+        """Rows per sequence of a layer cache (g4_attention_rows seq_stride)."""
+        return kv.seq_rows if kv.ring else self.max_seq
 
     # ------------------------------------------------------------ buffers ---
     def _alloc(self, R):
@@ -387,10 +408,15 @@ class Gemma4Model:
             kp, vp = C.c_void_p(), C.c_void_p()
             call("g4_kv_buffers", kv.handle, C.byref(kp), C.byref(vp))
             qkv = self._w4p(Ly["qkv"], b["x"], rows)
-            call("g4_qkv_post_planes", h, C.byref(qkv), cfg.heads, hd, 0 if s["shared"] else 1,
-                 _ptr(Ly["qn"]), _ptr(Ly["kn"]), C.c_float(cfg.eps), s["rope_angles"], C.c_float(s["rope_base"]),
-                 C.byref(rmap), rows, _ptr(b["q"]), kp, vp, self.max_seq)
-            call("g4_attention_rows", h, _ptr(b["q"]), kv.handle, rows, cfg.heads, hd, C.byref(rmap), self.max_seq,
+            if kv.ring and not s["shared"]:
+                call("g4_qkv_post_kv", h, C.byref(qkv), cfg.heads, hd, _ptr(Ly["qn"]), _ptr(Ly["kn"]),
+                     C.c_float(cfg.eps), s["rope_angles"], C.c_float(s["rope_base"]), C.byref(rmap), rows,
+                     _ptr(b["q"]), kv.handle)
+            else:
+                call("g4_qkv_post_planes", h, C.byref(qkv), cfg.heads, hd, 0 if s["shared"] else 1,
+                     _ptr(Ly["qn"]), _ptr(Ly["kn"]), C.c_float(cfg.eps), s["rope_angles"], C.c_float(s["rope_base"]),
+                     C.byref(rmap), rows, _ptr(b["q"]), kp, vp, self.max_seq)
+            call("g4_attention_rows", h, _ptr(b["q"]), kv.handle, rows, cfg.heads, hd, C.byref(rmap), self.kv_stride(kv),
                  0 if s["full"] else 1, cfg.window, _ptr(b["attn"]))
             y = self._w4p(Ly["o"], b["attn"], rows)
             call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pa"]), C.c_float(1.0),
@@ -512,14 +538,34 @@ class Gemma4Model:
             if Ly["spec"]["shared"]:
                 continue
             hd = Ly["spec"]["hd"]
+            kv = Ly["kv"]
             kp, vp = C.c_void_p(), C.c_void_p()
-            call("g4_kv_buffers", Ly["kv"].handle, C.byref(kp), C.byref(vp))
+            call("g4_kv_buffers", kv.handle, C.byref(kp), C.byref(vp))
+            pitch = self.kv_stride(kv) * hd * 2
+            # (first storage row, first source row, rows) of each copy; a ring cache keeps
+            # the last `ring` positions at slot p % ring, then repeats slots 0.. after the ring
+            n = min(length, kv.ring) if kv.ring else length
+            if kv.ring:
+                s0 = (length - n) % kv.ring
+                first = min(n, kv.ring - s0)
+                parts = [(s0, 0, first), (0, first, n - first)]
+            else:
+                parts = [(0, 0, n)]
             for dst, sd in ((kp, 0.3), (vp, 1.0)):
-                src = (torch.randn((nseq, length, hd), device=self.dev, generator=g) * sd).to(torch.bfloat16)
-                rc = cudart.cudaMemcpy2DAsync(dst, self.max_seq * hd * 2, C.c_void_p(src.data_ptr()), length * hd * 2,
-                                              length * hd * 2, nseq, 3, stream)
-                if rc != 0:
-                    raise G4Error(-3, f"cudaMemcpy2DAsync failed ({rc})")
+                src = (torch.randn((nseq, n, hd), device=self.dev, generator=g) * sd).to(torch.bfloat16)
+                for row, srow, cnt in parts:
+                    if cnt <= 0:
+                        continue
+                    rc = cudart.cudaMemcpy2DAsync(dst.value + row * hd * 2, pitch, src.data_ptr() + srow * hd * 2,
+                                                  n * hd * 2, cnt * hd * 2, nseq, 3, stream)
+                    if rc != 0:
+                        raise G4Error(-3, f"cudaMemcpy2DAsync failed ({rc})")
+                if kv.ring:
+                    mirror = kv.seq_rows - kv.ring
+                    rc = cudart.cudaMemcpy2DAsync(dst.value + kv.ring * hd * 2, pitch, dst.value, pitch,
+                                                  mirror * hd * 2, nseq, 3, stream)
+                    if rc != 0:
+                        raise G4Error(-3, f"cudaMemcpy2DAsync failed ({rc})")
                 torch.cuda.current_stream(self.dev).synchronize()
         self.seq_pos[:nseq] = length
 

@@ -179,14 +179,29 @@ class PleW4Table:
 
 
 class KVCache:
-    """KVCache (gemma4-webgpu.js:122-137) with bf16 storage."""
+    """KVCache (gemma4-webgpu.js:122-137) with bf16 storage.
 
-    def __init__(self, ctx: Context, head_dim: int, max_seq: int):
+    ring > 0: a sliding-window cache of `nseq` sequences that keeps each sequence's last
+    `ring` positions (g4_kv_create_ring); max_seq stays the position limit.  `rows` is the
+    storage height and `seq_rows` the row stride per sequence."""
+
+    def __init__(self, ctx: Context, head_dim: int, max_seq: int, ring: int = 0, nseq: int = 1):
         self.ctx = ctx
         h = C.c_void_p()
-        call("g4_kv_create", ctx.handle, head_dim, max_seq, C.byref(h))
+        if ring:
+            call("g4_kv_create_ring", ctx.handle, head_dim, max_seq, ring, nseq, C.byref(h))
+        else:
+            call("g4_kv_create", ctx.handle, head_dim, max_seq, C.byref(h))
         self.handle = h
         self.head_dim, self.max_seq = head_dim, max_seq
+        r, sr, n = C.c_int(0), C.c_int(0), C.c_int(0)
+        call("g4_kv_layout", h, C.byref(r), C.byref(sr), C.byref(n))
+        self.ring, self.seq_rows, self.nseq = r.value, sr.value, n.value
+        self.rows = self.seq_rows * self.nseq if self.ring else max_seq
+
+    def slot(self, pos: int) -> int:
+        """Storage row of position pos (of sequence 0)."""
+        return pos % self.ring if self.ring else pos
 
     @property
     def length(self) -> int:
@@ -205,12 +220,12 @@ class KVCache:
         call("g4_kv_reset", self.handle)
 
     def tensors(self) -> tuple[torch.Tensor, torch.Tensor]:
-        """Copies of the bf16 K and V storage [max_seq, head_dim] (for tests)."""
+        """Copies of the bf16 K and V storage [rows, head_dim] (for tests)."""
         kp, vp = C.c_void_p(), C.c_void_p()
         call("g4_kv_buffers", self.handle, C.byref(kp), C.byref(vp))
-        n = self.max_seq * self.head_dim
-        return _wrap_device(kp.value, n, self.ctx).view(self.max_seq, self.head_dim), \
-            _wrap_device(vp.value, n, self.ctx).view(self.max_seq, self.head_dim)
+        n = self.rows * self.head_dim
+        return _wrap_device(kp.value, n, self.ctx).view(self.rows, self.head_dim), \
+            _wrap_device(vp.value, n, self.ctx).view(self.rows, self.head_dim)
 
     def close(self):
         if getattr(self, "handle", None):

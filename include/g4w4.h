@@ -188,6 +188,20 @@ g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids
  * Replaces KVCache (custom-webgpu/gemma4-webgpu.js:122-137): per-layer K and V
  * [capacity, hd], here in bf16.  Positions are absolute: slot = position. */
 g4_status g4_kv_create(g4_ctx* ctx, int hd, int capacity, g4_kv** out);
+/* A sliding-window cache that keeps only the last `ring` positions of each of `nseq`
+ * sequences, as the Node reference trims its sliding-layer caches to the window
+ * (node-reference/src/attention.js:299-305), instead of [capacity] rows per sequence.
+ * Position p sits in slot p % ring; the cache holds nseq * (ring + 16384/hd) rows (the
+ * first 16384/hd slots are repeated after the ring so that a key tile never wraps).
+ * Positions still run to `capacity` (g4_kv_append's limit).  Attention on it must be
+ * sliding with span + window - 1 <= ring, span = keylen - first query position (the
+ * rows per sequence for g4_attention_rows, whose seq_stride must be ring + 16384/hd);
+ * anything else is G4_ERR_INVALID / G4_ERR_RANGE.  ring >= 16384/hd.  g4_kv_append
+ * works on single-sequence ring caches; batched ones are filled by g4_qkv_post_kv. */
+g4_status g4_kv_create_ring(g4_ctx* ctx, int hd, int capacity, int ring, int nseq, g4_kv** out);
+/* ring = 0 for a linear cache; seq_rows = rows per sequence of a ring cache (ring + 16384/hd),
+ * or all rows of a linear one; nseq = sequences of a ring cache (1 for a linear one). */
+g4_status g4_kv_layout(const g4_kv* kv, int* ring, int* seq_rows, int* nseq);
 g4_status g4_kv_destroy(g4_kv* kv);
 /* Appends rows of K (post k-norm + RoPE) and V (post RMS) at start_pos, which must
  * equal the cache length (gemma4-webgpu.js:128-135, same errors).  src_dtype is
@@ -308,6 +322,14 @@ g4_status g4_post_norm_add_planes(g4_ctx* ctx, float* h, const g4_planes* y, con
 g4_status g4_qkv_post_planes(g4_ctx* ctx, const g4_planes* y, int heads, int hd, int has_kv, const float* qnorm,
                              const float* knorm, float eps, int rope_angles, float rope_base, const g4_rows* map,
                              int rows, void* q_out_bf16, void* kcache_bf16, void* vcache_bf16, int cache_cap);
+/* g4_qkv_post_planes writing K and V into a cache object (linear or ring): row r's K/V go to
+ * sequence seq(r)'s rows (seq * seq_rows, g4_kv_layout) at slot position (linear) or
+ * position % ring (ring, with the mirrored copy).  kv = NULL processes q only (KV-shared
+ * layers).  A position at or past the cache capacity raises G4_DEVERR_BAD_INDEX on the
+ * device and writes no K/V. */
+g4_status g4_qkv_post_kv(g4_ctx* ctx, const g4_planes* y, int heads, int hd, const float* qnorm, const float* knorm,
+                         float eps, int rope_angles, float rope_base, const g4_rows* map, int rows, void* q_out_bf16,
+                         const g4_kv* kv);
 g4_status g4_gelu_mul_planes(g4_ctx* ctx, const g4_planes* gate_up, int rows, int inter, void* out_bf16);
 g4_status g4_gelu_ple_planes(g4_ctx* ctx, const g4_planes* gate, const float* per_layer, int layer, int layers,
                              int dim, int rows, void* out_bf16);

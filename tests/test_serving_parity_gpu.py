@@ -131,6 +131,7 @@ def test_config5_full_size_sampled_sequences(rt, ctx, full_weights):
     B, ctx_len, steps = 256, 4096, 8
     max_seq = ctx_len + steps + 8
     gpu = model.Gemma4Model(ctx, cfg, w, max_batch=B, max_seq=max_seq, max_rows=B)
+    assert sum(1 for L in gpu.layers if L["kv"].ring) == 28  # every sliding layer keeps a ring
     gpu.fill_kv_random(ctx_len, seed=3)
     gpu.buf["next"][:B] = 0
     gpu.capture_decode(batch=B)
@@ -140,11 +141,16 @@ def test_config5_full_size_sampled_sequences(rt, ctx, full_weights):
     for i, L in enumerate(gpu.layers):
         if L["spec"]["shared"]:
             continue
-        kt, vt = L["kv"].tensors()
+        kv = L["kv"]
+        kt, vt = kv.tensors()
         for s in sampled:
-            rows = slice(s * max_seq, s * max_seq + ctx_len)
-            states[s]["k"][i][:ctx_len] = kt[rows].float().cpu().numpy()
-            states[s]["v"][i][:ctx_len] = vt[rows].float().cpu().numpy()
+            if kv.ring:  # a sliding layer's ring: its slots hold the positions its windows still reach
+                lo = max(0, ctx_len - cfg.window)
+                rows = torch.from_numpy(s * kv.seq_rows + np.arange(lo, ctx_len) % kv.ring).to(kt.device)
+            else:
+                lo, rows = 0, slice(s * max_seq, s * max_seq + ctx_len)
+            states[s]["k"][i][lo:ctx_len] = kt[rows].float().cpu().numpy()
+            states[s]["v"][i][lo:ctx_len] = vt[rows].float().cpu().numpy()
         del kt, vt
         torch.cuda.empty_cache()
     for s in sampled:
@@ -197,3 +203,32 @@ def test_config4_prompt_2048_through_tcgen05(rt, ctx, full_weights):
     print(f"config 4: prefill 2048 + {steps} steps, near ties {tally.ties}, worst value error {tally.worst_val:.2e}, "
           f"min margin {tally.min_margin:.4f}")
     assert len(tally.ties) <= 1
+
+
+@pytest.mark.parametrize("B", [1, 40])
+def test_ring_kv_model_equals_linear_kv(rt, ctx, B):
+    """The sliding layers' ring caches (window 16 + 8 prefill rows - 1 -> a 64-slot ring,
+    wrapped twice by 150 greedy steps) give the picks and capped logits of linear caches bit
+    for bit: the attention reads the same key tiles in the same order."""
+    cfg = small_cfg()
+    w = model.random_weights(cfg, seed=7 + B, **FULL_KW)
+    rng = np.random.default_rng(B + 70)
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab, int(n))] for n in rng.integers(1, 9, B)]
+    steps, max_seq = 150, 200
+    res = []
+    for ring in (True, False):
+        m = model.Gemma4Model(ctx, cfg, w, max_batch=B, max_seq=max_seq, max_rows=8, ring_kv=ring)
+        rings = [L["kv"].ring for L in m.layers if not L["spec"]["shared"]]
+        assert (sum(1 for r in rings if r) == sum(1 for L in m.layers if not L["spec"]["full"])) == ring
+        first = [m.prefill(s, p) for s, p in enumerate(prompts)]
+        m.buf["next"][:B] = torch.tensor(first, dtype=torch.int32, device="cuda")
+        m.capture_decode(batch=B)
+        ids, vals = [first], []
+        for _ in range(steps):
+            ids.append(m.replay_decode().cpu().numpy().copy())
+            vals.append(m.buf["val"][:B].cpu().numpy().copy())
+        ctx.check_device()
+        m.close()
+        res.append((np.array(ids), np.array(vals)))
+    assert np.array_equal(res[0][0], res[1][0])
+    assert np.array_equal(res[0][1], res[1][1])
