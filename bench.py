@@ -51,7 +51,7 @@ PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 # dram__bytes_read.sum + dram__bytes_write.sum per launch from the committed ncu captures
 # (profiles/).  Writes that are still in L2 when a kernel ends are not counted by ncu.
 TRAFFIC = {
-    "ple_gather_kernel": 20_571_136 + 19_982_080,  # T = 4096 (profiles/ple_gather_kernel__config2_*)
+    "ple_gather_kernel": 20_566_272 + 15_701_760,  # T = 4096 (profiles/ple_gather_kernel__config2_*)
     "gemv_w4a16_kernel": 5_336_576,                # config 1 (profiles/gemv_w4a16_kernel__config1_*)
     "attn_decode_kernel": 4_221_696,               # one sequence at keylen 4096 (profiles/attn_decode_kernel__dram_bytes_*)
 }

@@ -14,83 +14,122 @@ namespace {
 using namespace g4dev;
 
 // One CTA per token, one thread per packed 32-bit word (8 columns) at a time.  Consecutive
-// threads own consecutive words, so a warp loads 128 contiguous bytes of nibbles (plus the
-// 16 contiguous bytes of their 8 scales) and stores 512 contiguous bytes of bf16 output in
-// one instruction each.  Each thread first issues the loads of all kPleWords of its words,
-// then decodes and stores them (8960 columns = 1120 words = 160 threads x 7).
+// threads own consecutive words, so a warp loads 128 contiguous bytes of nibbles and stores
+// 512 contiguous bytes of bf16 output in one instruction each.  The row's scales (560 bytes)
+// go to shared memory first, one 16-byte load per 8 groups, issued together with the word
+// loads: half the load instructions of a per-word scale load.  Each thread issues the loads
+// of all its words, then decodes and stores them (8960 columns = 1120 words = 160 threads
+// x 7).  The table's own width is compiled in (kWPR = 1120): without the per-word bounds
+// checks and runtime strides the kernel measured 16.8 instead of 17.6 us per 4096 tokens;
+// other widths take the generic instance (kWPR = 0).
 //
 // Decode (ple-w4-shard-reader.js:89-95): column c is nibble (c & 1) of byte c >> 1,
 // i.e. bits 4c..4c+3 of the little-endian 32-bit word c >> 3; value = two's
 // complement nibble * f32(scale), exact in f32.
 constexpr int kPleThreads = 160;
 constexpr int kPleWords = 7;
+constexpr int kPleWidthWords = 1120;  // 8960 columns
 
+// Word j of an output row: 8 columns from packed word w with the bf16 scale bits sb.
 template <bool kF32Out>
+__device__ __forceinline__ void ple_store_word(uint32_t w, uint32_t sb, void* __restrict__ out, size_t j) {
+    if constexpr (!kF32Out) {
+        // bf16 out = RNE(q * s).  q * s is exact in f32, so rounding it once to bf16
+        // equals one correctly rounded bf16 multiply of the exact operands q and s.
+        const uint32_t s2 = sb | (sb << 16);
+        uint32_t r[4];
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+            // nibbles pp and pp+4 of the word -> bf16x2 (128 + (n ^ 8)) -> minus 136 = signed q
+            uint32_t v;
+            asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(v) : "r"(w >> (4 * pp)), "r"(0x000F000Fu), "r"(0x43084308u));
+            uint32_t q;
+            asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(0x43084308u));
+            asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[pp]) : "r"(q), "r"(s2));
+        }
+        // r[pp] holds columns (pp, pp+4) of this word; emit (0,1) (2,3) (4,5) (6,7)
+        uint4 ov;
+        ov.x = __byte_perm(r[0], r[1], 0x5410);
+        ov.y = __byte_perm(r[2], r[3], 0x5410);
+        ov.z = __byte_perm(r[0], r[1], 0x7632);
+        ov.w = __byte_perm(r[2], r[3], 0x7632);
+        reinterpret_cast<uint4*>(out)[j] = ov;
+    } else {
+        const float s = bf16_bits_to_f32(sb);
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            // ((n ^ 8) | 0x4B000000) as f32 = 2^23 + q + 8
+            const uint32_t m = ((w >> (4 * e)) & 0xFu) ^ 0x4B000008u;
+            v[e] = (__uint_as_float(m) - 8388616.0f) * s;
+        }
+        float4* o = reinterpret_cast<float4*>(out) + j * 2;
+        o[0] = make_float4(v[0], v[1], v[2], v[3]);
+        o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+}
+
+// kWPR > 0: rows of exactly kWPR words (a multiple of kPleThreads; words_per_row and
+// groups_per_row are then ignored).  An out-of-range id gives a zero row and raises the
+// device error word.
+template <bool kF32Out, int kWPR>
 __global__ void __launch_bounds__(kPleThreads) ple_gather_kernel(const uint32_t* __restrict__ packed,
                                                                  const uint16_t* __restrict__ scales,
                                                                  const int32_t* __restrict__ ids, int vocab,
                                                                  int words_per_row, int groups_per_row,
                                                                  void* __restrict__ out, uint32_t* err) {
+    extern __shared__ __align__(16) uint16_t s_scales[];  // [groups_per_row]
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.x;
     const int id = __ldg(ids + t);
     const bool ok = (unsigned)id < (unsigned)vocab;
     if (!ok && threadIdx.x == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
-    const uint32_t* prow = packed + (size_t)(ok ? id : 0) * words_per_row;
-    const uint16_t* srow = scales + (size_t)(ok ? id : 0) * groups_per_row;
-    const size_t orow = (size_t)t * words_per_row;
-    for (int base = 0; base < words_per_row; base += kPleThreads * kPleWords) {
-        uint32_t w[kPleWords], sb[kPleWords];
+    const int rid = ok ? id : 0;
+    if constexpr (kWPR > 0) {
+        static_assert(kWPR % kPleThreads == 0 && kWPR % 32 == 0, "whole words per thread, whole 16-byte scale loads");
+        constexpr int kW = kWPR / kPleThreads;
+        const uint32_t* prow = packed + (size_t)rid * kWPR;
+        if (threadIdx.x < kWPR / 32)
+            reinterpret_cast<uint4*>(s_scales)[threadIdx.x] =
+                __ldg(reinterpret_cast<const uint4*>(scales + (size_t)rid * (kWPR / 4)) + threadIdx.x);
+        uint32_t w[kW];
 #pragma unroll
-        for (int k = 0; k < kPleWords; ++k) {
-            const int j = base + k * kPleThreads + threadIdx.x;
-            w[k] = 0;
-            sb[k] = 0;
-            if (ok && j < words_per_row) {
-                w[k] = __ldg(prow + j);
-                sb[k] = __ldg(srow + (j >> 2));  // 4 words = one group of 32 columns
-            }
+        for (int k = 0; k < kW; ++k) w[k] = __ldg(prow + k * kPleThreads + threadIdx.x);
+        __syncthreads();
+        const size_t orow = (size_t)t * kWPR;
+#pragma unroll
+        for (int k = 0; k < kW; ++k) {
+            const int j = k * kPleThreads + threadIdx.x;
+            ple_store_word<kF32Out>(ok ? w[k] : 0u, ok ? (uint32_t)s_scales[j >> 2] : 0u, out, orow + j);
         }
+    } else {
+        const uint32_t* prow = packed + (size_t)rid * words_per_row;
+        const uint16_t* srow = scales + (size_t)rid * groups_per_row;
+        const size_t orow = (size_t)t * words_per_row;
+        if (groups_per_row % 8 == 0) {  // the row's scales start on a 16-byte boundary
+            for (int i = threadIdx.x; i < groups_per_row / 8; i += kPleThreads)
+                reinterpret_cast<uint4*>(s_scales)[i] =
+                    ok ? __ldg(reinterpret_cast<const uint4*>(srow) + i) : make_uint4(0u, 0u, 0u, 0u);
+        } else {
+            for (int i = threadIdx.x; i < groups_per_row; i += kPleThreads) s_scales[i] = ok ? __ldg(srow + i) : 0;
+        }
+        bool staged = false;
+        for (int base = 0; base < words_per_row; base += kPleThreads * kPleWords) {
+            uint32_t w[kPleWords];
 #pragma unroll
-        for (int k = 0; k < kPleWords; ++k) {
-            const int j = base + k * kPleThreads + threadIdx.x;
-            if (j >= words_per_row) continue;
-            if constexpr (!kF32Out) {
-                // bf16 out = RNE(q * s).  q * s is exact in f32, so rounding it once to bf16
-                // equals one correctly rounded bf16 multiply of the exact operands q and s.
-                const uint32_t s2 = sb[k] | (sb[k] << 16);
-                uint32_t r[4];
+            for (int k = 0; k < kPleWords; ++k) {
+                const int j = base + k * kPleThreads + threadIdx.x;
+                w[k] = (ok && j < words_per_row) ? __ldg(prow + j) : 0u;
+            }
+            if (!staged) {  // the scales are in shared memory (uniform branch: the loop is the CTA's)
+                __syncthreads();
+                staged = true;
+            }
 #pragma unroll
-                for (int pp = 0; pp < 4; ++pp) {
-                    // nibbles pp and pp+4 of the word -> bf16x2 (128 + (n ^ 8)) -> minus 136 = signed q
-                    uint32_t v;
-                    asm("lop3.b32 %0, %1, %2, %3, 0x6A;"
-                        : "=r"(v)
-                        : "r"(w[k] >> (4 * pp)), "r"(0x000F000Fu), "r"(0x43084308u));
-                    uint32_t q;
-                    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(v), "r"(0x43084308u));
-                    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r[pp]) : "r"(q), "r"(s2));
-                }
-                // r[pp] holds columns (pp, pp+4) of this word; emit (0,1) (2,3) (4,5) (6,7)
-                uint4 ov;
-                ov.x = __byte_perm(r[0], r[1], 0x5410);
-                ov.y = __byte_perm(r[2], r[3], 0x5410);
-                ov.z = __byte_perm(r[0], r[1], 0x7632);
-                ov.w = __byte_perm(r[2], r[3], 0x7632);
-                reinterpret_cast<uint4*>(out)[orow + j] = ov;
-            } else {
-                const float s = bf16_bits_to_f32(sb[k]);
-                float v[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    // ((n ^ 8) | 0x4B000000) as f32 = 2^23 + q + 8
-                    const uint32_t m = ((w[k] >> (4 * e)) & 0xFu) ^ 0x4B000008u;
-                    v[e] = (__uint_as_float(m) - 8388616.0f) * s;
-                }
-                float4* o = reinterpret_cast<float4*>(out) + (orow + j) * 2;
-                o[0] = make_float4(v[0], v[1], v[2], v[3]);
-                o[1] = make_float4(v[4], v[5], v[6], v[7]);
+            for (int k = 0; k < kPleWords; ++k) {
+                const int j = base + k * kPleThreads + threadIdx.x;
+                if (j < words_per_row) ple_store_word<kF32Out>(w[k], s_scales[j >> 2], out, orow + j);  // 4 words = one group
             }
         }
     }
@@ -215,11 +254,19 @@ g4_status g4_ple_gather(g4_ctx* ctx, const g4_ple_table* tab, const int32_t* ids
     const int gpr = tab->width / 32, wpr = tab->width / 8;
     const uint32_t* p = reinterpret_cast<const uint32_t*>(tab->packed);
     const dim3 grid((unsigned)T), block(kPleThreads);
-    if (out_dtype == G4_BF16)
-        return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false>, grid, block, 0, 1, p,
-                          static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
-    return g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true>, grid, block, 0, 1, p,
-                      static_cast<const uint16_t*>(tab->scales), d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
+    const size_t smem = ((size_t)gpr * 2 + 15) & ~size_t(15);
+    if (smem > 48 * 1024) return g4::set_error(G4_ERR_UNSUPPORTED, "g4_ple_gather: width %d", tab->width);
+    const uint16_t* sc = static_cast<const uint16_t*>(tab->scales);
+    const bool bf = out_dtype == G4_BF16;
+    if (wpr == kPleWidthWords)
+        return bf ? g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false, kPleWidthWords>, grid, block, smem, 1,
+                               p, sc, d_ids, tab->vocab, wpr, gpr, out, ctx->d_err)
+                  : g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true, kPleWidthWords>, grid, block, smem, 1,
+                               p, sc, d_ids, tab->vocab, wpr, gpr, out, ctx->d_err);
+    return bf ? g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<false, 0>, grid, block, smem, 1, p, sc, d_ids,
+                           tab->vocab, wpr, gpr, out, ctx->d_err)
+              : g4::launch(ctx, "ple_gather_kernel", ple_gather_kernel<true, 0>, grid, block, smem, 1, p, sc, d_ids,
+                           tab->vocab, wpr, gpr, out, ctx->d_err);
 }
 
 }  // extern "C"

@@ -117,3 +117,23 @@ def test_full_size_config2_properties(rt, ctx, oracle):
     assert torch.equal(out, again)
     del tab, packed, sc
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("width", [256, 512, 9216])
+def test_other_widths_bit_exact(rt, ctx, oracle, width):
+    """Widths other than the table's 8960 columns take the generic kernel instance: 16-byte
+    scale loads when the groups fill whole vectors (512, 9216), scalar ones otherwise (256),
+    and more words per row than one pass of the CTA (9216); f32 and bf16 bit-exact."""
+    rng = np.random.default_rng(width)
+    vocab = 50
+    q = rng.integers(-7, 8, size=(vocab, width), dtype=np.int8)
+    nib = (q.astype(np.int16) & 0xF).astype(np.uint8)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+    scales = oracle.f32_to_bf16_bits(np.abs(rng.normal(0, 0.05, (vocab, width // 32))).astype(np.float32))
+    tab = rt.PleW4Table(ctx, packed, scales, width=width)
+    ids = rng.integers(0, vocab, 77).astype(np.int32)
+    for dt, bf in ((torch.float32, False), (torch.bfloat16, True)):
+        out = tab.rows_to_gpu(ids, dt)
+        ref = oracle.ple_read_rows(packed, scales, ids, bf16=bf)
+        assert np.array_equal(_bits(out), ref.view(np.int32 if not bf else np.int16))
+    ctx.check_device()
