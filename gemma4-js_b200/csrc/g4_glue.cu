@@ -88,6 +88,32 @@ __device__ __forceinline__ float4 ld4_planes(const Planes& P, size_t off) {
     return a;
 }
 
+// ld4_planes at two offsets, every load of both issued before the first add (a warp issues
+// in order, so an add that waits on a load holds back the loads behind it).
+__device__ __forceinline__ void ld4_planes2(const Planes& P, size_t off_a, size_t off_b, float4& a, float4& b) {
+    const float* pa = P.base + off_a;
+    const float* pb = P.base + off_b;
+    a = __ldg(reinterpret_cast<const float4*>(pa));
+    b = __ldg(reinterpret_cast<const float4*>(pb));
+    for (int s0 = 1; s0 < P.count; s0 += kPlaneBatch / 2) {
+        float4 ba[kPlaneBatch / 2], bb[kPlaneBatch / 2];
+#pragma unroll
+        for (int j = 0; j < kPlaneBatch / 2; ++j) {
+            const bool in = s0 + j < P.count;
+            const size_t o = (size_t)(s0 + j) * P.stride;
+            ba[j] = in ? __ldg(reinterpret_cast<const float4*>(pa + o)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            bb[j] = in ? __ldg(reinterpret_cast<const float4*>(pb + o)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < kPlaneBatch / 2; ++j) {
+            if (s0 + j < P.count) {
+                a.x += ba[j].x; a.y += ba[j].y; a.z += ba[j].z; a.w += ba[j].w;
+                b.x += bb[j].x; b.y += bb[j].y; b.z += bb[j].z; b.w += bb[j].w;
+            }
+        }
+    }
+}
+
 // RMS_SHADER: y = x * rsqrt(mean(x^2) + eps) * scale (scale optional).
 __global__ void __launch_bounds__(kRowThreads) rms_kernel(const float* __restrict__ x, const float* __restrict__ scale,
                                                           int width, float eps, void* __restrict__ out, int out_bf16) {
@@ -108,6 +134,28 @@ __global__ void __launch_bounds__(kRowThreads) rms_kernel(const float* __restric
     }
 }
 
+// RMS_SHADER for width % 4 == 0, width <= 4096: one float4 of the row per thread, loaded
+// once (the scale, immutable, before the PDL wait), one reduction.
+__global__ void __launch_bounds__(1024) rms4_kernel(const float* __restrict__ x, const float* __restrict__ scale,
+                                                    int width, float eps, void* __restrict__ out, int out_bf16) {
+    pdl_trigger();
+    __shared__ float red[32];
+    const int r = blockIdx.x, i = threadIdx.x * 4;
+    const bool on = i < width;
+    float4 sc = make_float4(1.f, 1.f, 1.f, 1.f), v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (on && scale) sc = __ldg(reinterpret_cast<const float4*>(scale + i));
+    pdl_wait();
+    if (on) v = *reinterpret_cast<const float4*>(x + (size_t)r * width + i);
+    const float inv = rsqrtf(block_sum(v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w, red) / (float)width + eps);
+    if (!on) return;
+    const float4 o = make_float4(v.x * inv * sc.x, v.y * inv * sc.y, v.z * inv * sc.z, v.w * inv * sc.w);
+    if (out_bf16)
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(out) + (size_t)r * width + i) =
+            make_uint2(pack_bf16x2_bits(o.x, o.y), pack_bf16x2_bits(o.z, o.w));
+    else
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)r * width + i) = o;
+}
+
 // ADD_SCALE: y = (a + b) * s.
 __global__ void add_scale_kernel(const float* __restrict__ a, const float* __restrict__ b, long long n, float s,
                                  float* __restrict__ y) {
@@ -126,15 +174,18 @@ __global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__
                                                              const float* __restrict__ w_next, int width, float eps,
                                                              uint16_t* __restrict__ x_out) {
     pdl_trigger();
-    pdl_wait();
     __shared__ float red[32];
     const int r = blockIdx.x, i = threadIdx.x * 4;
     const bool on = i < width;
-    float4 yv = make_float4(0.f, 0.f, 0.f, 0.f), hv = yv, wp = yv;
-    if (on) {
-        yv = ld4_planes(y, (size_t)r * y.ld + i);
+    float4 yv = make_float4(0.f, 0.f, 0.f, 0.f), hv = yv, wp = yv, wn = yv;
+    if (on) {  // the norm weights are immutable: fetched while the predecessor drains
+        wp = __ldg(reinterpret_cast<const float4*>(w_post + i));
+        if (w_next) wn = __ldg(reinterpret_cast<const float4*>(w_next + i));
+    }
+    pdl_wait();
+    if (on) {  // h first: its load is in flight with the planes' (one L2 round trip in all)
         hv = *reinterpret_cast<const float4*>(h + (size_t)r * width + i);
-        wp = *reinterpret_cast<const float4*>(w_post + i);
+        yv = ld4_planes(y, (size_t)r * y.ld + i);
     }
     const float inv = rsqrtf(block_sum(yv.x * yv.x + yv.y * yv.y + yv.z * yv.z + yv.w * yv.w, red) / (float)width + eps);
     hv.x = (hv.x + yv.x * inv * wp.x) * skip;
@@ -147,10 +198,7 @@ __global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__
     if (w_next) {
         const float inv2 =
             rsqrtf(block_sum(hv.x * hv.x + hv.y * hv.y + hv.z * hv.z + hv.w * hv.w, red) / (float)width + eps);
-        if (on) {
-            const float4 wn = *reinterpret_cast<const float4*>(w_next + i);
-            o = make_float4(hv.x * inv2 * wn.x, hv.y * inv2 * wn.y, hv.z * inv2 * wn.z, hv.w * inv2 * wn.w);
-        }
+        if (on) o = make_float4(hv.x * inv2 * wn.x, hv.y * inv2 * wn.y, hv.z * inv2 * wn.z, hv.w * inv2 * wn.w);
     }
     if (on)
         *reinterpret_cast<uint2*>(x_out + (size_t)r * width + i) = make_uint2(pack_bf16x2_bits(o.x, o.y), pack_bf16x2_bits(o.z, o.w));
@@ -161,7 +209,7 @@ __global__ void __launch_bounds__(1024) post_norm_add_kernel(float* __restrict__
 __global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __restrict__ table, int vocab, int width,
                                                             const int32_t* __restrict__ ids, float scale,
                                                             float* __restrict__ h, uint16_t* __restrict__ x,
-                                                            uint32_t* err) {
+                                                            uint32_t* err, int vec) {
     pdl_trigger();
     pdl_wait();
     const int r = blockIdx.x;
@@ -169,6 +217,26 @@ __global__ void __launch_bounds__(kRowThreads) embed_kernel(const uint16_t* __re
     const bool ok = (unsigned)id < (unsigned)vocab;
     if (!ok && threadIdx.x == 0) raise_error(err, G4_DEVERR_BAD_INDEX);
     const uint16_t* er = table + (size_t)(ok ? id : 0) * width;
+    if (vec) {  // width % 8 == 0, 16-byte aligned rows: every load of the row in flight at once
+        for (int i0 = threadIdx.x * 8; i0 < width; i0 += blockDim.x * 8) {
+            const uint4 e = ok ? __ldg(reinterpret_cast<const uint4*>(er + i0)) : make_uint4(0u, 0u, 0u, 0u);
+            const uint32_t w[4] = {e.x, e.y, e.z, e.w};
+            float v[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                v[2 * k] = bf16_bits_to_f32(w[k] & 0xFFFFu) * scale;
+                v[2 * k + 1] = bf16_bits_to_f32(w[k] >> 16) * scale;
+            }
+            float4* hr = reinterpret_cast<float4*>(h + (size_t)r * width + i0);
+            hr[0] = make_float4(v[0], v[1], v[2], v[3]);
+            hr[1] = make_float4(v[4], v[5], v[6], v[7]);
+            if (x)
+                *reinterpret_cast<uint4*>(x + (size_t)r * width + i0) =
+                    make_uint4(pack_bf16x2_bits(v[0], v[1]), pack_bf16x2_bits(v[2], v[3]), pack_bf16x2_bits(v[4], v[5]),
+                               pack_bf16x2_bits(v[6], v[7]));
+        }
+        return;
+    }
     for (int i = threadIdx.x; i < width; i += blockDim.x) {
         const float v = ok ? bf16_bits_to_f32(er[i]) * scale : 0.f;
         h[(size_t)r * width + i] = v;
@@ -207,12 +275,10 @@ __device__ __forceinline__ bool kv_row_ok(int slot, int H, int pos, const KvSink
     if (kv.err) atomicOr(kv.err, G4_DEVERR_BAD_INDEX);
     return false;
 }
-__device__ __forceinline__ float2 qkv_pair(int slot, int H, int hd, int i, float a0, float a1, float inv,
-                                           const float* __restrict__ qnorm, const float* __restrict__ knorm,
-                                           int rope_angles, float rope_base, int pos) {
+__device__ __forceinline__ float2 qkv_pair_s(int slot, int H, int hd, int i, float a0, float a1, float inv,
+                                             float s0, float s1, int rope_angles, float rope_base, int pos) {
     if (slot == H + 1) return make_float2(a0 * inv, a1 * inv);  // v: RMS without scale (official-w4a16-layer0.js:176-182)
-    const float* sc = slot < H ? qnorm : knorm;
-    const float x0 = a0 * inv * sc[i], x1 = a1 * inv * sc[i + (hd >> 1)];
+    const float x0 = a0 * inv * s0, x1 = a1 * inv * s1;
     float sn = 0.f, cs = 1.f;
     if (i < rope_angles) {
         const float theta = (float)pos / powf(rope_base, 2.f * (float)i / (float)hd);
@@ -220,6 +286,14 @@ __device__ __forceinline__ float2 qkv_pair(int slot, int H, int hd, int i, float
         cs = cosf(theta);
     }
     return make_float2(x0 * cs - x1 * sn, x1 * cs + x0 * sn);
+}
+__device__ __forceinline__ float2 qkv_pair(int slot, int H, int hd, int i, float a0, float a1, float inv,
+                                           const float* __restrict__ qnorm, const float* __restrict__ knorm,
+                                           int rope_angles, float rope_base, int pos) {
+    const float* sc = slot < H ? qnorm : knorm;
+    const bool scaled = slot <= H;
+    return qkv_pair_s(slot, H, hd, i, a0, a1, inv, scaled ? sc[i] : 1.f, scaled ? sc[i + (hd >> 1)] : 1.f,
+                      rope_angles, rope_base, pos);
 }
 
 // Any hd % 64 == 0: one CTA per (row, head slot), thread i owns the rotation pair
@@ -264,14 +338,28 @@ qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restr
     constexpr int hd = 256 * NF, half = hd / 2, G = 2 * NF;  // float4 groups per lane
     constexpr int PB = NF <= 2 ? 4 : 2;                        // slices per load batch
     pdl_trigger();
-    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int slots = H + (has_kv ? 2 : 0);
     const int unit = blockIdx.x * kQkvWarps + (threadIdx.x >> 5);
-    if (unit >= rows * slots) return;
-    const int r = unit / slots, slot = unit - r * slots;
-    const float* src = y.base + (size_t)r * y.ld + (size_t)slot * hd;
+    const bool valid = unit < rows * slots;
+    const int r = valid ? unit / slots : 0, slot = valid ? unit - r * slots : 0;
     auto goff = [&](int g) { return (g < NF ? 0 : half) + 4 * (lane + 32 * (g % NF)); };
+    // The lane's norm scales (immutable) are fetched while the predecessor drains; the
+    // row's position with the planes.  A warp issues in order: nothing below consumes a
+    // load before every load of the row has been issued.
+    float4 sc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) sc[g] = make_float4(1.f, 1.f, 1.f, 1.f);
+    if (valid && slot <= H) {
+        const float* nrm = slot < H ? qnorm : knorm;
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] = __ldg(reinterpret_cast<const float4*>(nrm + goff(g)));
+    }
+    pdl_wait();
+    if (!valid) return;
+    const int seq = row_seq(R, r);
+    const int seq_pos = R.seq_pos ? R.seq_pos[seq] : 0;
+    const float* src = y.base + (size_t)r * y.ld + (size_t)slot * hd;
     float4 a[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) a[g] = __ldg(reinterpret_cast<const float4*>(src + goff(g)));
@@ -303,7 +391,7 @@ qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restr
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
     const float inv = rsqrtf(ss / (float)hd + eps);
-    const int pos = row_position(R, r);
+    const int pos = seq_pos + R.pos0 + r % R.rows_per_seq;
     if (!kv_row_ok(slot, H, pos, kv)) return;
     uint16_t* dst2;
     uint16_t* dst = qkv_dst(slot, H, hd, r, R, pos, q_out, kv, &dst2);
@@ -311,10 +399,13 @@ qkv_post_warp_kernel(Planes y, int H, int has_kv, int rows, const float* __restr
     for (int f = 0; f < NF; ++f) {
         const int i0 = 4 * (lane + 32 * f);
         const float lo[4] = {a[f].x, a[f].y, a[f].z, a[f].w}, hi[4] = {a[NF + f].x, a[NF + f].y, a[NF + f].z, a[NF + f].w};
+        const float slo[4] = {sc[f].x, sc[f].y, sc[f].z, sc[f].w};
+        const float shi[4] = {sc[NF + f].x, sc[NF + f].y, sc[NF + f].z, sc[NF + f].w};
         float o0[4], o1[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const float2 o = qkv_pair(slot, H, hd, i0 + c, lo[c], hi[c], inv, qnorm, knorm, rope_angles, rope_base, pos);
+            const float2 o = qkv_pair_s(slot, H, hd, i0 + c, lo[c], hi[c], inv, slo[c], shi[c], rope_angles, rope_base,
+                                        pos);
             o0[c] = o.x;
             o1[c] = o.y;
         }
@@ -339,8 +430,8 @@ __global__ void gelu_mul_kernel(Planes gu, int inter, long long n4, uint16_t* __
     const int q = inter >> 2;
     const long long r = i / q, c = (i - r * q) * 4;
     const size_t row = (size_t)r * gu.ld;
-    const float4 g = ld4_planes(gu, row + c);
-    const float4 u = ld4_planes(gu, row + inter + c);
+    float4 g, u;
+    ld4_planes2(gu, row + c, row + inter + c, g, u);
     *reinterpret_cast<uint2*>(out + r * inter + c) =
         make_uint2(pack_bf16x2_bits(gelu_ref(g.x) * u.x, gelu_ref(g.y) * u.y),
                    pack_bf16x2_bits(gelu_ref(g.z) * u.z, gelu_ref(g.w) * u.w));
@@ -354,8 +445,8 @@ __global__ void gelu_ple_kernel(Planes gate, const float* __restrict__ per_layer
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const long long r = i / dim, d = i - r * dim;
-    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(ld_planes(gate, (size_t)r * gate.ld + d)) *
-                                        per_layer[(r * layers + layer) * dim + d]);
+    const float pl = per_layer[(r * layers + layer) * dim + d];  // in flight with the planes' loads
+    out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(ld_planes(gate, (size_t)r * gate.ld + d)) * pl);
 }
 
 // SCALE + PLE_MIX: p = proj * proj_scale; y = (rms(p) * norm + tok_ple * sqrt(dim)) / sqrt(2)
@@ -363,13 +454,15 @@ __global__ void gelu_ple_kernel(Planes gate, const float* __restrict__ per_layer
 __global__ void ple_mix_kernel(const float* __restrict__ proj, float proj_scale, const float* __restrict__ norm,
                                const float* __restrict__ tok_ple, int dim, float eps, float* __restrict__ out) {
     pdl_trigger();
-    pdl_wait();
     __shared__ float red[32];
     const size_t base = (size_t)blockIdx.x * dim;
     const int d = threadIdx.x;
+    const float nd = __ldg(norm + d);  // immutable: fetched while the predecessor drains
+    pdl_wait();
+    const float tp = tok_ple[base + d];
     const float p = proj[base + d] * proj_scale;
     const float inv = rsqrtf(block_sum(p * p, red) / (float)dim + eps);
-    out[base + d] = (p * inv * norm[d] + tok_ple[base + d] * sqrtf((float)dim)) * 0.7071067811865476f;
+    out[base + d] = (p * inv * nd + tp * sqrtf((float)dim)) * 0.7071067811865476f;
 }
 
 // softcap + argmax, pass 1: per (row, chunk) the largest tanh(v / cap) * cap and its
@@ -520,6 +613,11 @@ g4_status g4_rms(g4_ctx* ctx, const float* x, const float* scale, int rows, int 
     if (st) return st;
     if (rows < 0 || width <= 0 || !x || !out) return g4::set_error(G4_ERR_INVALID, "g4_rms: bad arguments");
     if (rows == 0) return G4_OK;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(scale) |
+                         reinterpret_cast<uintptr_t>(out);
+    if (width % 4 == 0 && width <= 4096 && al % 16 == 0)
+        return g4::launch(ctx, "rms4_kernel", rms4_kernel, dim3(rows), dim3(((width / 4 + 31) / 32) * 32), 0, 1, x,
+                          scale, width, eps, out, (int)(out_dtype == G4_BF16));
     return g4::launch(ctx, "rms_kernel", rms_kernel, dim3(rows), dim3(kRowThreads), 0, 1, x, scale, width, eps, out,
                       (int)(out_dtype == G4_BF16));
 }
@@ -562,9 +660,11 @@ g4_status g4_embed(g4_ctx* ctx, const void* table_bf16, int vocab, int width, co
     if (st) return st;
     if (rows < 0 || !table_bf16 || !ids_dev || !h_out) return g4::set_error(G4_ERR_INVALID, "g4_embed: bad arguments");
     if (rows == 0) return G4_OK;
+    const int vec = width % 8 == 0 && ((reinterpret_cast<uintptr_t>(table_bf16) | reinterpret_cast<uintptr_t>(h_out) |
+                                         reinterpret_cast<uintptr_t>(x_out_bf16)) % 16 == 0);
     return g4::launch(ctx, "embed_kernel", embed_kernel, dim3(rows), dim3(kRowThreads), 0, 1,
                       static_cast<const uint16_t*>(table_bf16), vocab, width, ids_dev, scale, h_out,
-                      static_cast<uint16_t*>(x_out_bf16), ctx->d_err);
+                      static_cast<uint16_t*>(x_out_bf16), ctx->d_err, vec);
 }
 
 }  // extern "C"
