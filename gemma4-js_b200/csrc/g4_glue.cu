@@ -282,8 +282,7 @@ __device__ __forceinline__ float2 qkv_pair_s(int slot, int H, int hd, int i, flo
     float sn = 0.f, cs = 1.f;
     if (i < rope_angles) {
         const float theta = (float)pos / powf(rope_base, 2.f * (float)i / (float)hd);
-        sn = sinf(theta);
-        cs = cosf(theta);
+        sincosf(theta, &sn, &cs);  // one argument reduction for both
     }
     return make_float2(x0 * cs - x1 * sn, x1 * cs + x0 * sn);
 }
@@ -447,6 +446,22 @@ __global__ void gelu_ple_kernel(Planes gate, const float* __restrict__ per_layer
     const long long r = i / dim, d = i - r * dim;
     const float pl = per_layer[(r * layers + layer) * dim + d];  // in flight with the planes' loads
     out[i] = (uint16_t)f32_to_bf16_bits(gelu_ref(ld_planes(gate, (size_t)r * gate.ld + d)) * pl);
+}
+
+// GELU_PLE with four columns per thread (dim % 4 == 0, 16-byte aligned planes and per_layer).
+__global__ void gelu_ple4_kernel(Planes gate, const float* __restrict__ per_layer, int layer, int layers, int dim,
+                                 long long n4, uint16_t* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n4) return;
+    const int q = dim >> 2;
+    const long long r = i / q, c = (i - r * q) * 4;
+    const float4 pl = *reinterpret_cast<const float4*>(per_layer + (r * layers + layer) * dim + c);  // with the planes
+    const float4 g = ld4_planes(gate, (size_t)r * gate.ld + c);
+    *reinterpret_cast<uint2*>(out + r * dim + c) =
+        make_uint2(pack_bf16x2_bits(gelu_ref(g.x) * pl.x, gelu_ref(g.y) * pl.y),
+                   pack_bf16x2_bits(gelu_ref(g.z) * pl.z, gelu_ref(g.w) * pl.w));
 }
 
 // SCALE + PLE_MIX: p = proj * proj_scale; y = (rms(p) * norm + tok_ple * sqrt(dim)) / sqrt(2)
@@ -764,6 +779,12 @@ g4_status g4_gelu_ple_planes(g4_ctx* ctx, const g4_planes* gate, const float* pe
         return g4::set_error(G4_ERR_INVALID, "g4_gelu_ple: bad arguments");
     const long long n = (long long)rows * dim;
     if (n == 0) return G4_OK;
+    const bool f4 = dim % 4 == 0 && gate->ld % 4 == 0 && (gate->count == 1 || gate->stride % 4 == 0) &&
+                    ((reinterpret_cast<uintptr_t>(gate->base) | reinterpret_cast<uintptr_t>(per_layer)) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(out_bf16) & 7) == 0;
+    if (f4)
+        return g4::launch(ctx, "gelu_ple4_kernel", gelu_ple4_kernel, dim3(blocks_for(n / 4, 128)), dim3(128), 0, 1,
+                          planes_of(gate), per_layer, layer, layers, dim, n / 4, static_cast<uint16_t*>(out_bf16));
     return g4::launch(ctx, "gelu_ple_kernel", gelu_ple_kernel, dim3(blocks_for(n, 256)), dim3(256), 0, 1,
                       planes_of(gate), per_layer, layer, layers, dim, n, static_cast<uint16_t*>(out_bf16));
 }
