@@ -18,6 +18,7 @@
 // weights and activations, so every lane loads its operand with one 16-byte load and
 // activations with two 16-byte loads.  The same blocks feed the tcgen05 GEMM producer.
 #include <cooperative_groups.h>
+#include <algorithm>
 #include <stdio.h>
 
 #include "g4_common.cuh"
@@ -151,22 +152,28 @@ __host__ __device__ constexpr int gemv_smem_bytes(int P, int M) {
 // are summed across warps in shared memory and across the S CTAs of the cluster
 // through distributed shared memory: no global scratch, no atomics.
 // kNB = number of 8-row activation tiles (1: M <= 8, 2: M <= 16).
-template <int kNB>
+// kGeglu (one K slice, one pass): a gate/up linear whose 128-row slabs are 64 gate rows then
+// the 64 matching up rows; CTA y computes gate tile 8 (y / 4) + y % 4 and its up tile 4 tiles
+// later from one staging of both, and writes bf16(gelu(gate) * up) (GELU_MUL) to y [M, N/2]:
+// the GeGLU of the gate/up linear without an f32 round trip and a second launch.
+template <int kNB, bool kGeglu>
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ldx,
                   void* __restrict__ y, int ldy, int y_f32, int chunks_per_split, uint32_t* err) {
+    constexpr int kT = kGeglu ? 2 : 1;  // weight tiles per CTA
     extern __shared__ __align__(128) uint8_t sm[];
     const int P = min(chunks_per_split, kGemvPass);
     const int xstride = gemv_xstride(P);
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm);
-    uint8_t* wsm = sm + 128;
-    uint8_t* ssm = wsm + P * 512;
-    uint8_t* xsm = ssm + P * 64;
-    float* red = reinterpret_cast<float*>(wsm);  // [warps][kNB*4][32], after the last pass
+    uint8_t* wsm = sm + 128;               // [kT][P * 512]
+    uint8_t* ssm = wsm + kT * P * 512;     // [kT][P * 64]
+    uint8_t* xsm = ssm + kT * P * 64;
+    float* red = reinterpret_cast<float*>(wsm);  // [warps][kT][kNB*4][32], after the last pass
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int split = blockIdx.x, nt = blockIdx.y;
+    const int split = blockIdx.x;
+    const int nt = kGeglu ? (int)(blockIdx.y >> 2) * 8 + (int)(blockIdx.y & 3) : (int)blockIdx.y;
     const int c_begin = split * chunks_per_split;
     const int c_end = min(L.Kc, c_begin + chunks_per_split);
 
@@ -185,9 +192,11 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         pdl_trigger();
     }
 
-    float acc[kNB][4];
+    float acc[kT][kNB][4];
 #pragma unroll
-    for (int j = 0; j < kNB; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int tt = 0; tt < kT; ++tt)
+#pragma unroll
+        for (int j = 0; j < kNB; ++j) acc[tt][j][0] = acc[tt][j][1] = acc[tt][j][2] = acc[tt][j][3] = 0.f;
 
     bool ok = true;
     uint32_t phase = 0;
@@ -196,11 +205,14 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         const int k0 = p0 * 64;
         const int klen = min(L.K, (p0 + nch) * 64) - k0;  // valid activation columns
         if (threadIdx.x == 0) {
-            const uint32_t bytes = nch * 512 + nch * 64 + M * klen * 2;
+            const uint32_t bytes = kT * (nch * 512 + nch * 64) + M * klen * 2;
             mbar_arrive_expect_tx(bar, bytes);
-            const size_t blk = (size_t)nt * L.Kc + p0;
-            bulk_load(wsm, L.wfrag + blk * 32, nch * 512, bar);
-            bulk_load(ssm, L.sfrag + blk * 8, nch * 64, bar);
+#pragma unroll
+            for (int tt = 0; tt < kT; ++tt) {  // kGeglu: the up tile sits 4 tiles after the gate tile
+                const size_t blk = (size_t)(nt + 4 * tt) * L.Kc + p0;
+                bulk_load(wsm + tt * P * 512, L.wfrag + blk * 32, nch * 512, bar);
+                bulk_load(ssm + tt * P * 64, L.sfrag + blk * 8, nch * 64, bar);
+            }
             if (p0 == c_begin) {  // weights are immutable; activations come from the predecessor
                 pdl_wait();
                 pdl_trigger();
@@ -215,9 +227,11 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         ok = mbar_wait(bar, phase, err);
         __syncthreads();
         if (ok) {
-            for (int c = warp; c < nch; c += kGemvWarps) {
-                const uint4 wv = *reinterpret_cast<const uint4*>(wsm + c * 512 + lane * 16);
-                const uint2 sv = *reinterpret_cast<const uint2*>(ssm + c * 64 + g * 8);
+            for (int c = warp; c < nch; c += kGemvWarps)
+#pragma unroll
+            for (int tt = 0; tt < kT; ++tt) {
+                const uint4 wv = *reinterpret_cast<const uint4*>(wsm + tt * P * 512 + c * 512 + lane * 16);
+                const uint2 sv = *reinterpret_cast<const uint2*>(ssm + tt * P * 64 + c * 64 + g * 8);
                 const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
                 for (int G = 0; G < 2; ++G) {
@@ -240,10 +254,10 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
                         const float z[4] = {0.f, 0.f, 0.f, 0.f};
                         mma_bf16_16816(d, a0, b0, z);
                         mma_bf16_16816(d, a1, b1, d);
-                        acc[j][0] = fmaf(s_lo, d[0], acc[j][0]);
-                        acc[j][1] = fmaf(s_lo, d[1], acc[j][1]);
-                        acc[j][2] = fmaf(s_hi, d[2], acc[j][2]);
-                        acc[j][3] = fmaf(s_hi, d[3], acc[j][3]);
+                        acc[tt][j][0] = fmaf(s_lo, d[0], acc[tt][j][0]);
+                        acc[tt][j][1] = fmaf(s_lo, d[1], acc[tt][j][1]);
+                        acc[tt][j][2] = fmaf(s_hi, d[2], acc[tt][j][2]);
+                        acc[tt][j][3] = fmaf(s_hi, d[3], acc[tt][j][3]);
                     }
                 }
             }
@@ -257,18 +271,36 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
 
     // ---- reduce the warps of the CTA ----
 #pragma unroll
-    for (int j = 0; j < kNB; ++j)
+    for (int tt = 0; tt < kT; ++tt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) red[(warp * kNB * 4 + j * 4 + e) * 32 + lane] = acc[j][e];
+        for (int j = 0; j < kNB; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) red[((warp * kT + tt) * kNB * 4 + j * 4 + e) * 32 + lane] = acc[tt][j][e];
     __syncthreads();
     if (warp == 0) {
 #pragma unroll
-        for (int q = 0; q < kNB * 4; ++q) {
+        for (int q = 0; q < kT * kNB * 4; ++q) {
             float s = red[q * 32 + lane];
 #pragma unroll
-            for (int w2 = 1; w2 < kGemvWarps; ++w2) s += red[(w2 * kNB * 4 + q) * 32 + lane];
+            for (int w2 = 1; w2 < kGemvWarps; ++w2) s += red[(w2 * kT * kNB * 4 + q) * 32 + lane];
             red[q * 32 + lane] = s;
         }
+    }
+    if constexpr (kGeglu) {  // one K slice: the CTA holds whole sums
+        if (warp != 0) return;
+#pragma unroll
+        for (int j = 0; j < kNB; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int f = (int)(blockIdx.y >> 2) * 64 + (int)(blockIdx.y & 3) * 16 + g + ((e & 2) ? 8 : 0);
+                const int b = j * 8 + 2 * t + (e & 1);
+                if (b < M && f < L.N / 2) {
+                    const float gate = red[(j * 4 + e) * 32 + lane], up = red[(kNB * 4 + j * 4 + e) * 32 + lane];
+                    reinterpret_cast<uint16_t*>(y)[(size_t)b * ldy + f] = (uint16_t)f32_to_bf16_bits(gelu_ref(gate) * up);
+                }
+            }
+        }
+        return;
     }
     // ---- reduce the S CTAs of the cluster through distributed shared memory ----
     const int S = gridDim.x;
@@ -313,9 +345,9 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
     const g4_linear_dev& L = lin->dev;
     static std::atomic<uint64_t> attr_set{0};
     if (!(attr_set.load() & (1ull << ctx->device))) {
-        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            gemv_smem_bytes(kGemvPass, 8)));
-        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            gemv_smem_bytes(kGemvPass, 16)));
         attr_set.fetch_or(1ull << ctx->device);
     }
@@ -334,13 +366,39 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
         void* ys = y_f32 ? (void*)(reinterpret_cast<float*>(y) + (size_t)m0 * L.N)
                          : (void*)(reinterpret_cast<uint16_t*>(y) + (size_t)m0 * L.N);
         // the split-K cluster runs along x: grid (S, NT), CTA (split, tile)
-        g4_status st = mm <= 8 ? launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<1>, dim3(S, L.NT), dim3(kGemvWarps * 32),
+        g4_status st = mm <= 8 ? launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<1, false>, dim3(S, L.NT), dim3(kGemvWarps * 32),
                                         smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err)
-                               : launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<2>, dim3(S, L.NT), dim3(kGemvWarps * 32),
+                               : launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<2, false>, dim3(S, L.NT), dim3(kGemvWarps * 32),
                                         smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
         if (st) return st;
     }
     return G4_OK;
+}
+
+// GeGLU of a gate/up linear (rows in 64-row gate/up slabs) for M <= 16, when one CTA's K
+// range is the whole row (one slice, one pass): gemv_w4a16_kernel<kNB, true>.  Returns
+// G4_ERR_UNSUPPORTED (nothing launched) otherwise; the caller then takes the planes path.
+g4_status launch_gemv_geglu(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, uint16_t* out) {
+    const g4_linear_dev& L = lin->dev;
+    if (L.N % 128 != 0 || L.Kc > kGemvPass || M > 16) return G4_ERR_UNSUPPORTED;
+    // the split rule of launch_gemv: a GeGLU CTA needs the whole K, so only where it keeps one slice
+    if (L.NT < 2 * ctx->num_sms && (L.Kc + 1) / 2 >= 24) return G4_ERR_UNSUPPORTED;
+    static std::atomic<uint64_t> attr_set{0};
+    const int P = L.Kc;
+    const size_t need1 = 128 + 2 * (size_t)P * 576 + 8 * gemv_xstride(P), need2 = 128 + 2 * (size_t)P * 576 + 16 * gemv_xstride(P);
+    const size_t red1 = 128 + (size_t)kGemvWarps * 2 * 4 * 32 * 4, red2 = 128 + (size_t)kGemvWarps * 2 * 8 * 32 * 4;
+    if (!(attr_set.load() & (1ull << ctx->device))) {
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)std::max<size_t>(128 + 2 * (size_t)kGemvPass * 576 + 8 * gemv_xstride(kGemvPass), red1)));
+        G4_CHECK_CUDA(cudaFuncSetAttribute(gemv_w4a16_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)std::max<size_t>(128 + 2 * (size_t)kGemvPass * 576 + 16 * gemv_xstride(kGemvPass), red2)));
+        attr_set.fetch_or(1ull << ctx->device);
+    }
+    const dim3 grid(1, (unsigned)(L.NT / 2));
+    return M <= 8 ? launch(ctx, "gemv_w4a16_kernel<geglu>", gemv_w4a16_kernel<1, true>, grid, dim3(kGemvWarps * 32),
+                           std::max(need1, red1), 1, L, x, M, L.K, out, L.N / 2, 0, L.Kc, ctx->d_err)
+                  : launch(ctx, "gemv_w4a16_kernel<geglu>", gemv_w4a16_kernel<2, true>, grid, dim3(kGemvWarps * 32),
+                           std::max(need2, red2), 1, L, x, M, L.K, out, L.N / 2, 0, L.Kc, ctx->d_err);
 }
 
 }  // namespace g4
@@ -482,6 +540,10 @@ g4_status g4_linear_w4a16_geglu(g4_ctx* ctx, const g4_linear* lin, const void* x
     const uint16_t* x = static_cast<const uint16_t*>(x_bf16);
     uint16_t* out = static_cast<uint16_t*>(out_bf16);
     if (M > 16 && g4::gemm_supported(lin, M)) return g4::launch_gemm_geglu(ctx, lin, x, M, out);
+    if (M <= 16) {
+        st = g4::launch_gemv_geglu(ctx, lin, x, M, out);
+        if (st != G4_ERR_UNSUPPORTED) return st;
+    }
     g4_planes pl;
     st = g4_linear_w4a16_planes(ctx, lin, x_bf16, M, &pl);
     if (st) return st;

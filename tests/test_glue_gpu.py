@@ -261,11 +261,14 @@ def test_dense_argmax_fused_matches_two_pass(rt, ctx, M, cap):
         assert torch.allclose(vals2, best, atol=1e-3)
 
 
-@pytest.mark.parametrize("M,K,inter", [(256, 1536, 6144), (40, 512, 1024), (3, 512, 1024), (300, 256, 512)])
+@pytest.mark.parametrize("M,K,inter", [(256, 1536, 6144), (40, 512, 1024), (3, 512, 1024), (300, 256, 512),
+                                      (1, 1536, 6144), (16, 1536, 6144), (8, 2048, 1024), (5, 256, 512),
+                                      (2, 4096, 1024)])
 def test_geglu_fused_linear_matches_linear_then_gelu_mul(rt, ctx, M, K, inter):
     """g4_linear_w4a16_geglu on the interleaved rows gives the same bits as the linear on
     [gate; up] (f32) followed by g4_gelu_mul: fused epilogue (unsplit tiles), planes +
-    GeGLU pass (split K), GEMV below 17 rows."""
+    GeGLU pass (split K), and below 17 rows the GEMV computing each gate tile with its up
+    tile in one CTA (K up to 2048; K = 4096 takes the GEMV + GeGLU pass)."""
     model = importlib.import_module("gemma4-js_b200.model")
     gen = g(M + K + inter)
     N = 2 * inter
