@@ -118,6 +118,7 @@ SIGNATURES = {
     "g4_gelu_ple": (_S, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "g4_linear_w4a16_planes": (_S, [_P, _P, _P, _I, _P]),
     "g4_linear_w4a16_geglu": (_S, [_P, _P, _P, _I, _P]),
+    "g4_linear_w4a16_gelu_ple": (_S, [_P, _P, _P, _I, _P, _I, _I, _P]),
     "g4_dense_argmax": (_S, [_P, _P, _P, _I, _F, _P, _P]),
     "g4_post_norm_add_planes": (_S, [_P, _P, _P, _P, _F, _P, _I, _I, _F, _P]),
     "g4_qkv_post_planes": (_S, [_P, _P, _I, _I, _I, _P, _P, _F, _I, _F, _P, _I, _P, _P, _P, _I]),

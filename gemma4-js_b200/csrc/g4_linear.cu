@@ -159,7 +159,8 @@ __host__ __device__ constexpr int gemv_smem_bytes(int P, int M) {
 template <int kNB, bool kGeglu>
 __global__ void __launch_bounds__(kGemvWarps * 32)
 gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ldx,
-                  void* __restrict__ y, int ldy, int y_f32, int chunks_per_split, uint32_t* err) {
+                  void* __restrict__ y, int ldy, int y_f32, int chunks_per_split, const float* __restrict__ ple,
+                  int ple_ld, uint32_t* err) {
     constexpr int kT = kGeglu ? 2 : 1;  // weight tiles per CTA
     extern __shared__ __align__(128) uint8_t sm[];
     const int P = min(chunks_per_split, kGemvPass);
@@ -268,6 +269,19 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
         pdl_wait();
         pdl_trigger();
     }
+    // ple != null: GELU_PLE epilogue, y bf16 = gelu(v) * ple[b * ple_ld + row]; the factors are
+    // loaded here, in flight during the reductions (every thread has passed its PDL wait).
+    float pf[kNB][4];
+    if (!kGeglu && ple && warp == 0 && split == 0) {
+#pragma unroll
+        for (int j = 0; j < kNB; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int row = nt * 16 + g + ((e & 2) ? 8 : 0);
+                const int b = j * 8 + 2 * t + (e & 1);
+                pf[j][e] = (row < L.N && b < M) ? ple[(size_t)b * ple_ld + row] : 0.f;
+            }
+    }
 
     // ---- reduce the warps of the CTA ----
 #pragma unroll
@@ -327,7 +341,10 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
             const int b = j * 8 + 2 * t + (e & 1);
             if (row < L.N && b < M) {
                 const float v = red[(j * 4 + e) * 32 + lane];
-                if (y_f32)
+                if (ple)
+                    reinterpret_cast<uint16_t*>(y)[(size_t)b * ldy + row] =
+                        (uint16_t)f32_to_bf16_bits(gelu_ref(v) * pf[j][e]);
+                else if (y_f32)
                     reinterpret_cast<float*>(y)[(size_t)b * ldy + row] = v;
                 else
                     reinterpret_cast<uint16_t*>(y)[(size_t)b * ldy + row] = (uint16_t)f32_to_bf16_bits(v);
@@ -341,7 +358,7 @@ gemv_w4a16_kernel(g4_linear_dev L, const uint16_t* __restrict__ x, int M, int ld
 namespace g4 {
 
 g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y,
-                      int y_f32) {
+                      int y_f32, const float* ple, int ple_ld) {
     const g4_linear_dev& L = lin->dev;
     static std::atomic<uint64_t> attr_set{0};
     if (!(attr_set.load() & (1ull << ctx->device))) {
@@ -365,11 +382,12 @@ g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int 
         const uint16_t* xs = x + (size_t)m0 * L.K;
         void* ys = y_f32 ? (void*)(reinterpret_cast<float*>(y) + (size_t)m0 * L.N)
                          : (void*)(reinterpret_cast<uint16_t*>(y) + (size_t)m0 * L.N);
+        const float* ples = ple ? ple + (size_t)m0 * ple_ld : nullptr;
         // the split-K cluster runs along x: grid (S, NT), CTA (split, tile)
         g4_status st = mm <= 8 ? launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<1, false>, dim3(S, L.NT), dim3(kGemvWarps * 32),
-                                        smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err)
+                                        smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ples, ple_ld, ctx->d_err)
                                : launch(ctx, "gemv_w4a16_kernel", gemv_w4a16_kernel<2, false>, dim3(S, L.NT), dim3(kGemvWarps * 32),
-                                        smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ctx->d_err);
+                                        smem, S, L, xs, mm, L.K, ys, L.N, y_f32, cps, ples, ple_ld, ctx->d_err);
         if (st) return st;
     }
     return G4_OK;
@@ -396,9 +414,9 @@ g4_status launch_gemv_geglu(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x
     }
     const dim3 grid(1, (unsigned)(L.NT / 2));
     return M <= 8 ? launch(ctx, "gemv_w4a16_kernel<geglu>", gemv_w4a16_kernel<1, true>, grid, dim3(kGemvWarps * 32),
-                           std::max(need1, red1), 1, L, x, M, L.K, out, L.N / 2, 0, L.Kc, ctx->d_err)
+                           std::max(need1, red1), 1, L, x, M, L.K, out, L.N / 2, 0, L.Kc, nullptr, 0, ctx->d_err)
                   : launch(ctx, "gemv_w4a16_kernel<geglu>", gemv_w4a16_kernel<2, true>, grid, dim3(kGemvWarps * 32),
-                           std::max(need2, red2), 1, L, x, M, L.K, out, L.N / 2, 0, L.Kc, ctx->d_err);
+                           std::max(need2, red2), 1, L, x, M, L.K, out, L.N / 2, 0, L.Kc, nullptr, 0, ctx->d_err);
 }
 
 }  // namespace g4
@@ -518,7 +536,7 @@ g4_status g4_linear_w4a16_impl(g4_ctx* ctx, const g4_linear* lin, const void* x_
     const int y_f32 = y_dtype == G4_F32;
     if (impl == 0) impl = (M <= 16) ? 1 : 2;
     if (impl == 2 && !g4::gemm_supported(lin, M)) impl = 1;
-    if (impl == 1) return g4::launch_gemv(ctx, lin, static_cast<const uint16_t*>(x_bf16), M, y, y_f32);
+    if (impl == 1) return g4::launch_gemv(ctx, lin, static_cast<const uint16_t*>(x_bf16), M, y, y_f32, nullptr, 0);
     if (impl == 2) return g4::launch_gemm(ctx, lin, static_cast<const uint16_t*>(x_bf16), M, y, y_f32);
     return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_impl: impl %d", impl);
 }
@@ -550,6 +568,25 @@ g4_status g4_linear_w4a16_geglu(g4_ctx* ctx, const g4_linear* lin, const void* x
     return g4::launch_geglu_planes(ctx, pl, M, lin->dev.N, out);
 }
 
+g4_status g4_linear_w4a16_gelu_ple(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
+                                   const float* per_layer, int layer, int layers, void* out_bf16) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    if (!lin || !x_bf16 || !per_layer || !out_bf16 || M < 0 || layer < 0 || layer >= layers)
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_gelu_ple: bad arguments");
+    if (M == 0) return G4_OK;
+    if (reinterpret_cast<uintptr_t>(x_bf16) % 16 != 0)
+        return g4::set_error(G4_ERR_INVALID, "g4_linear_w4a16_gelu_ple: x must be 16-byte aligned");
+    const int N = lin->dev.N;
+    if (M <= 16 || !g4::gemm_supported(lin, M))  // GELU_PLE in the GEMV's epilogue
+        return g4::launch_gemv(ctx, lin, static_cast<const uint16_t*>(x_bf16), M, out_bf16, 0,
+                               per_layer + (size_t)layer * N, layers * N);
+    g4_planes pl;
+    st = g4_linear_w4a16_planes(ctx, lin, x_bf16, M, &pl);
+    if (st) return st;
+    return g4_gelu_ple_planes(ctx, &pl, per_layer, layer, layers, N, M, out_bf16);
+}
+
 g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, g4_planes* out) {
     g4_status st = g4::use_device(ctx);
     if (st) return st;
@@ -562,7 +599,7 @@ g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* 
     st = g4::ensure_workspace(ctx, (size_t)M * lin->dev.N * 4);
     if (st) return st;
     *out = g4_planes{static_cast<const float*>(ctx->ws), 1, 0, lin->dev.N};
-    return g4::launch_gemv(ctx, lin, x, M, ctx->ws, 1);
+    return g4::launch_gemv(ctx, lin, x, M, ctx->ws, 1, nullptr, 0);
 }
 
 }  // extern "C"

@@ -23,7 +23,8 @@ struct g4_linear {
 
 namespace g4 {
 constexpr int kTblkBytes = 2 * 128 * 16 + 2 * 128 * 2;  // 4608
-g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32);
+g4_status launch_gemv(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32,
+                      const float* ple = nullptr, int ple_ld = 0);
 // tcgen05 W4A16 GEMM, weights dequantised into tensor memory (g4_gemm_w4.cu)
 bool gemm_supported(const g4_linear* lin, int M);
 g4_status launch_gemm(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x, int M, void* y, int y_f32);

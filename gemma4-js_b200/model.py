@@ -425,8 +425,9 @@ class Gemma4Model:
             y = self._w4p(Ly["down"], b["act"], rows)
             call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pff"]), C.c_float(1.0), None,
                  rows, H, C.c_float(cfg.eps), _ptr(b["x"]))
-            pg = self._w4p(Ly["pg"], b["x"], rows)
-            call("g4_gelu_ple_planes", h, C.byref(pg), _ptr(b["per_layer"]), i, L, P, rows, _ptr(b["pa"]))
+            # PLE gate + GELU x per-layer input (gemma4-webgpu.js:299-300); one launch up to 16 rows
+            call("g4_linear_w4a16_gelu_ple", h, Ly["pg"].handle, _ptr(b["x"]), rows, _ptr(b["per_layer"]), i, L,
+                 _ptr(b["pa"]))
             y = self._w4p(Ly["pp"], b["pa"], rows)
             w_next = self.layers[i + 1]["n_in"] if i + 1 < L else self.final_norm  # :404 final rms fused here
             call("g4_post_norm_add_planes", h, _ptr(b["h"]), C.byref(y), _ptr(Ly["n_pple"]), C.c_float(Ly["skip"]),

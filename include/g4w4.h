@@ -148,6 +148,12 @@ g4_status g4_linear_w4a16_planes(g4_ctx* ctx, const g4_linear* lin, const void* 
  * 128 = 64 gate rows then the 64 matching up rows (N % 128 == 0).  Same bits as
  * g4_linear_w4a16 (G4_F32) + g4_gelu_mul on the un-interleaved rows. */
 g4_status g4_linear_w4a16_geglu(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M, void* out_bf16);
+/* GPUOps.w4 followed by GPUOps.geluPle (GELU_PLE, custom-webgpu/gpu-runtime.js:1159-1173) for the
+ * per-layer-input gate: out bf16 [M, N] = bf16(gelu(x . W^T) * per_layer[row, layer, :]),
+ * per_layer f32 [M, layers, N].  Up to 16 rows the product goes straight from the GEMV's
+ * epilogue (one launch); above, the tcgen05 GEMM's planes and g4_gelu_ple_planes (the same bits). */
+g4_status g4_linear_w4a16_gelu_ple(g4_ctx* ctx, const g4_linear* lin, const void* x_bf16, int M,
+                                   const float* per_layer, int layer, int layers, void* out_bf16);
 
 /* Dequantises rows [row_start, row_start+row_count) of the weight into out
  * [row_count, K]: f32 = (nibble-8) * f32(scale) exactly as dequantizeOfficialW4A16Rows

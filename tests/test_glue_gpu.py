@@ -329,3 +329,25 @@ def test_fused_head_pick_matches_oracle_softcap_and_tie_rule(rt, ctx, oracle):
     assert ids.cpu().tolist() == expect
     ref_vals = np.array([np.tanh(E[expect[m], m] / np.float32(30.0)) * np.float32(30.0) for m in range(M)], np.float32)
     assert np.allclose(vals.cpu().numpy(), ref_vals, rtol=2e-6, atol=0)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 1536, 256), (5, 1536, 256), (16, 512, 256), (40, 1536, 256), (3, 4096, 512)])
+def test_linear_gelu_ple_matches_planes_then_gelu_ple(rt, ctx, M, K, N):
+    """g4_linear_w4a16_gelu_ple (GELU_PLE in the GEMV epilogue up to 16 rows, planes + the
+    GELU_PLE pass above) gives the bits of g4_linear_w4a16_planes + g4_gelu_ple_planes."""
+    gen = g(M + K + N)
+    layers, layer = 35, 7
+    packed = torch.randint(-2**31, 2**31 - 1, (N, K // 8), device="cuda", dtype=torch.int32, generator=gen)
+    sc = torch.randn((N, K // 32), device="cuda", generator=gen).abs_().mul_(0.02).to(torch.bfloat16)
+    lin = rt.W4Linear(ctx, packed, sc)
+    x = torch.randn((M, K), device="cuda", generator=gen).to(torch.bfloat16)
+    per_layer = torch.randn((M, layers * N), device="cuda", generator=gen)
+    pl = L.G4Planes()
+    L.call("g4_linear_w4a16_planes", ctx.handle, lin.handle, P(x), M, C.byref(pl))
+    a1 = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+    L.call("g4_gelu_ple_planes", ctx.handle, C.byref(pl), P(per_layer), layer, layers, N, M, P(a1))
+    a2 = torch.empty_like(a1)
+    L.call("g4_linear_w4a16_gelu_ple", ctx.handle, lin.handle, P(x), M, P(per_layer), layer, layers, P(a2))
+    ctx.check_device()
+    assert torch.equal(a1, a2)
+    assert float(a2.float().abs().sum()) > 0
