@@ -81,6 +81,7 @@ struct W4Params {
     // geglu: the weight rows of every 128-row slab are 64 gate rows then the 64 matching up
     // rows; y is bf16 [M, N/2] = gelu(gate) * up (GELU_MUL), computed from the staged tile.
     int geglu;
+    int wsplit;  // weight blocks and X on separate stage barriers (see the kernel)
     uint32_t* err;
 };
 
@@ -117,7 +118,14 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     uint64_t* a_empty = a_full + kAStages;
     uint64_t* acc_full = a_empty + kAStages;
     uint64_t* acc_empty = acc_full + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 1);
+    // p.wsplit (a grid of at most one tile per CTA, a decode-size linear): the weight blocks
+    // of a stage complete on w_full and its X boxes on load_full, so the dequantisers, which
+    // need only the blocks (requested before the PDL wait), start while X (the predecessor's
+    // output) is still on its way.  Otherwise both arrive on load_full (the persistent
+    // prefill GEMM measured 1-2 % faster that way).
+    uint64_t* w_full = acc_empty + 1;
+    uint64_t* wb = p.wsplit ? w_full : load_full;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(w_full + kStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = p.ksplit;
@@ -143,6 +151,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&load_full[s], 1);
+            mbar_init(&w_full[s], 1);
             mbar_init(&load_empty[s], 1 + kDq);  // the MMA (X read) and every dequant warp (blocks read)
         }
         for (int s = 0; s < kAStages; ++s) {
@@ -171,10 +180,10 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             for (int t = tile0; t < ntiles && pre < kStages; t += tstep)
                 for (int j = 0; j < NST && pre < kStages; ++j, ++pre) {
                     const int ws = t / p.MT, nsub = min(kSub, KT - j * kSub);
-                    mbar_arrive_expect_tx(&load_full[pre], (uint32_t)nsub * (xsub + kBlkBytes));
+                    mbar_arrive_expect_tx(&wb[pre], (uint32_t)nsub * (kBlkBytes + (p.wsplit ? 0 : xsub)));
                     bulk_load(smem + Smem::kOffBlk + pre * kSub * kBlkBytes,
                               p.tblk + ((size_t)ws * p.Kc + k0 + j * kSub) * kBlkBytes, nsub * kBlkBytes,
-                              &load_full[pre]);
+                              &wb[pre]);
                 }
             pdl_wait();
             bool ok = true;
@@ -188,11 +197,12 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
                             ok = false;
                             break;
                         }
-                        mbar_arrive_expect_tx(&load_full[s], (uint32_t)nsub * (xsub + kBlkBytes));
+                        mbar_arrive_expect_tx(&wb[s], (uint32_t)nsub * (kBlkBytes + (p.wsplit ? 0 : xsub)));
                         bulk_load(smem + Smem::kOffBlk + s * kSub * kBlkBytes,
                                   p.tblk + ((size_t)ws * p.Kc + k0 + j * kSub) * kBlkBytes, nsub * kBlkBytes,
-                                  &load_full[s]);
+                                  &wb[s]);
                     }
+                    if (p.wsplit) mbar_arrive_expect_tx(&load_full[s], (uint32_t)nsub * xsub);
                     for (int u = 0; u < nsub; ++u)
                         tma_load_2d(smem + Smem::kOffX + s * kXBytes + u * kXSub, &xmap, &load_full[s],
                                     (k0 + j * kSub + u) * TK, ms * p.TT);
@@ -201,6 +211,10 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             // Drain: our copies must land before the CTA can exit.
             for (int j = g > kStages ? g - kStages : 0; j < g; ++j)
                 mbar_wait(&load_full[j % kStages], (j / kStages) & 1, p.err, 0x102);
+            const int gw = g > pre ? g : pre;  // weight blocks requested, prefetched ones included
+            if (p.wsplit)
+                for (int j = gw > kStages ? gw - kStages : 0; j < gw; ++j)
+                    mbar_wait(&w_full[j % kStages], (j / kStages) & 1, p.err, 0x10a);
         }
         __syncwarp();
     } else if (warp == 1) {
@@ -247,7 +261,7 @@ gemm_w4_tmem_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_const
             for (int j = 0; j < NST; ++j, ++g) {
                 const int s = g % kStages, sa = g % kAStages;
                 const bool live = h < min(kSub, KT - j * kSub);
-                ok = mbar_wait_warp(&load_full[s], (g / kStages) & 1, p.err, 0x106);
+                ok = mbar_wait_warp(&wb[s], (g / kStages) & 1, p.err, 0x106);
                 if (ok && g >= kAStages) ok = mbar_wait_warp(&a_empty[sa], ((g / kAStages) - 1) & 1, p.err, 0x107);
                 if (!ok) break;
                 if (live) {
@@ -544,6 +558,7 @@ static g4_status gemm_core(g4_ctx* ctx, const g4_linear* lin, const uint16_t* x,
     }
     if (st) return st;
     const unsigned grid = S > 1 ? (unsigned)(ntiles * S) : (unsigned)std::min<long long>(ntiles, ctx->num_sms);
+    p.wsplit = (S > 1 || ntiles <= ctx->num_sms) ? 1 : 0;  // every CTA one tile (or one K slice of one)
     st = p.geglu ? launch(ctx, "gemm_w4_tmem_kernel<geglu>", gemm_w4_tmem_kernel<true>, dim3(grid), dim3(kThreads),
                           Smem::kBytes, 1, xmap, ymap, p)
                  : launch(ctx, "gemm_w4_tmem_kernel", gemm_w4_tmem_kernel<false>, dim3(grid), dim3(kThreads),
