@@ -75,6 +75,7 @@ SIGNATURES = {
     "g4_ctx_destroy": (_S, [_P]),
     "g4_ctx_set_stream": (_S, [_P, _P]),
     "g4_ctx_set_pdl": (_S, [_P, _I]),
+    "g4_selftest_wait_timeout": (_S, [_P, C.c_uint32]),
     "g4_stream_sync": (_S, [_P]),
     "g4_ctx_check_device": (_S, [_P, C.POINTER(C.c_uint32)]),
     "g4_last_error_string": (C.c_char_p, []),

@@ -181,6 +181,31 @@ g4_status g4_ctx_check_device(g4_ctx* ctx, uint32_t* flags) {
     return G4_OK;
 }
 
+}  // extern "C"
+
+namespace {
+// One thread waits on an mbarrier that nothing arrives on, through the bounded wait every
+// kernel of the library uses (mbar_wait): it gives up after kWaitLimitNs, raises
+// G4_DEVERR_TIMEOUT with `site` and returns.
+__global__ void wait_timeout_selftest_kernel(uint32_t* err, uint32_t site) {
+    using namespace g4dev;
+    __shared__ __align__(8) uint64_t bar;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0, err, site);
+}
+}  // namespace
+
+extern "C" {
+
+g4_status g4_selftest_wait_timeout(g4_ctx* ctx, uint32_t site) {
+    g4_status st = g4::use_device(ctx);
+    if (st) return st;
+    wait_timeout_selftest_kernel<<<1, 1, 0, ctx->stream>>>(ctx->d_err, site);
+    G4_CHECK_CUDA(cudaGetLastError());
+    return G4_OK;
+}
+
 const char* g4_last_error_string(void) { return t_last_error.c_str(); }
 
 const char* g4_version(void) { return "g4w4 0.1 sm_100a"; }

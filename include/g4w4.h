@@ -88,6 +88,12 @@ g4_status g4_stream_sync(g4_ctx* ctx);
  * *flags receives the raw bit set (0 = clean); the status is G4_ERR_TIMEOUT or
  * G4_ERR_DEVICE when a bit was set. */
 g4_status g4_ctx_check_device(g4_ctx* ctx, uint32_t* flags);
+/* Exercises the timeout path of the device-side bounded waits (no reference counterpart):
+ * one thread waits on an mbarrier that nothing completes, through the same bounded wait
+ * every kernel here uses; after about 2 s it raises G4_DEVERR_TIMEOUT with `site` and
+ * returns, so g4_ctx_check_device reports G4_ERR_TIMEOUT naming the site, and the context
+ * stays usable.  Nothing faults or hangs. */
+g4_status g4_selftest_wait_timeout(g4_ctx* ctx, uint32_t site);
 /* Message of the last failing call on this host thread ("" if none). */
 const char* g4_last_error_string(void);
 /* Library version string. */
